@@ -1,0 +1,413 @@
+"""Benchmark of the quantized matmul path on B200.
+
+Workload (one "step"): quantization::matmul of fp32 activations x [8192 x 8192]
+~N(0,1) with INT8 per-column weights W [K=8192 x N=65536] (~N(0,0.02) before
+quantization), i.e. the prefill INT8 GEMM M=8192 K=8192 N=65536.  The step is
+the full path: per-row activation quantizer + tcgen05 GEMM with the fused
+fp32 rescale epilogue.  On N GPUs the weight is column-sharded (N/p columns
+per GPU, no data exchange inside the step) and each GPU then all-gathers the
+output shards over NCCL so every GPU holds the full [M, N] result.
+
+Metric: int8 TOPS (2*M*N*K ops / step time).  x is 256 MiB, W 512 MiB and y
+2 GiB, all larger than the 126 MB L2, so no L2 flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+``--impl reference`` times the ZYRON reference's own CPU implementation
+(oracle/_ref/libzyron_ref.so, compiled from the reference's sources; falls
+back to the C restatement in oracle/ when that library is absent) on a
+bounded row sample of the same workload, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M_ROWS, K_DIM, N_COLS = 8192, 8192, 65536
+WORKLOAD = "prefill_int8_gemm_M8192_K8192_N65536"
+METRIC = "int8 qmatmul throughput (quantization::matmul, prefill INT8 GEMM)"
+UNIT = "TOPS"
+# The reference parallelises over rows only (one std::thread per row chunk),
+# so a bounded CPU sample is one row per host thread: every thread busy, one
+# row (K x N = 537 M scalar MACs) each, about 2 s per step.
+
+
+def ops(m, n, k):
+    return 2.0 * m * n * k
+
+
+# --------------------------------------------------------------------------
+# clocks sampled during the timed region (NVML reads only)
+# --------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index):
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # NVML unavailable: no clock record
+            self.nv = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(0.01)
+
+    def __enter__(self):
+        if self.nv is not None:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.nv is not None:
+            self.t.join()
+
+    def summary(self):
+        return {
+            "sm_mhz": statistics.median(self.samples) if self.samples else None,
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(self.reasons),
+            "samples": len(self.samples),
+        }
+
+
+# --------------------------------------------------------------------------
+# reference CPU timing (oracle/_ref or the oracle port) -- checker side only
+# --------------------------------------------------------------------------
+def synthetic_zyq_bytes(K, N, seed):
+    """A .zyq record with random INT8 codes / scales of the workload's shape.
+    The reference matmul's cost does not depend on the values."""
+    from oracle import oracle as O
+
+    rng = np.random.default_rng(seed)
+    payload = rng.integers(-127, 128, size=K * N, dtype=np.int8).view(np.uint8)
+    scales = (np.abs(rng.standard_normal(N)) * 0.02 * 4.0 / 127.0 + 1e-6).astype(np.float32)
+    return O.zyq_bytes(1, K, N, scales, payload)
+
+
+def reference_cpu_timer(zyq: bytes, x_rows: np.ndarray):
+    """Returns (time_one_call, threads, kind) for quantization::matmul of
+    x_rows against the .zyq weight, on the host cores."""
+    from oracle import oracle as O
+
+    if O.ref_available():
+        R = O.RefMatrix.load_bytes(zyq)
+        threads = O.ref_set_threads(os.cpu_count() or 1)
+
+        def call():
+            t0 = time.perf_counter()
+            R.matmul(x_rows)
+            return time.perf_counter() - t0
+
+        return call, threads, "reference", R
+    # oracle port (single thread)
+    K = int(np.frombuffer(zyq[12:20], dtype="<u8")[0])
+    N = int(np.frombuffer(zyq[20:28], dtype="<u8")[0])
+    scales = np.frombuffer(zyq[36:36 + 4 * N], dtype=np.float32)
+    payload = np.frombuffer(zyq[36 + 4 * N + 8:], dtype=np.uint8)
+
+    def call():
+        t0 = time.perf_counter()
+        O.matmul(x_rows, 1, payload, scales, N)
+        return time.perf_counter() - t0
+
+    return call, 1, "port", None
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    K, N = K_DIM, N_COLS
+    zyq = synthetic_zyq_bytes(K, N, seed=1)
+    x = np.random.default_rng(0).standard_normal((64, K)).astype(np.float32)
+    from oracle import oracle as O
+
+    threads = O.ref_set_threads(os.cpu_count() or 1) if O.ref_available() else 1
+    rows = max(1, min(64, threads))
+    call, threads, kind, _keep = reference_cpu_timer(zyq, x[:rows])
+    for _ in range(args.warmup):
+        call()
+    times = [call() for _ in range(args.steps)]
+    t = sum(times) / len(times)
+    value = ops(rows, N, K) / t / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "M": M_ROWS, "K": K, "N": N, "weight": "int8 per-column",
+                   "sample_rows_per_step": rows},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": f"{rows} of {M_ROWS} rows x K={K} x N={N} per step, "
+                                   f"ZYRON quantization::matmul on {threads} host threads "
+                                   f"(os.cpu_count()={os.cpu_count()})"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------
+# our arm
+# --------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import zyron_b200 as zb
+    from zyron_b200 import _lib
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    L = _lib.lib()
+    stream = torch.cuda.current_stream(dev)
+    sp = C.c_void_p(stream.cuda_stream)
+
+    M, K, N = args.shape
+    assert N % world == 0
+    n_loc = N // world
+    c0 = rank * n_loc
+
+    # Inputs, generated on the device (seeded): x is the same on every rank,
+    # each rank quantizes its own column shard of W on the device.
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    x = torch.randn((M, K), generator=g, device=dev, dtype=torch.float32)
+    g.manual_seed(1000 + rank)
+    w_f32 = torch.randn((K, n_loc), generator=g, device=dev, dtype=torch.float32).mul_(0.02)
+    W = zb.quantize(w_f32, zb.Type.Int8)
+    del w_f32
+    torch.cuda.empty_cache()
+    y = torch.empty((M, n_loc), dtype=torch.float32, device=dev)
+    y_full = torch.empty((world, M, n_loc), dtype=torch.float32, device=dev) if world > 1 else None
+    ws_bytes = L.zq_matmul_workspace_bytes(W.handle, M)
+    ws = torch.empty(ws_bytes + 256, dtype=torch.uint8, device=dev)
+    ws_ptr = (ws.data_ptr() + 255) & ~255
+
+    def step():
+        _lib.check(L.zq_matmul(W.handle, C.c_void_p(x.data_ptr()), M, None, C.c_void_p(y.data_ptr()),
+                               C.c_void_p(ws_ptr), ws_bytes, sp))
+        if world > 1:
+            dist.all_gather_into_tensor(y_full, y)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+
+    sampler = ClockSampler(local_rank)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with sampler:
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+
+    # GEMM kernel alone (activation codes precomputed), same stream: the
+    # dominant kernel's average launch duration for the roofline.
+    Kp = L.zq_weight_padded_k(W.handle)
+    codes = torch.empty((M, Kp), dtype=torch.int8, device=dev)
+    rs = torch.empty((M,), dtype=torch.float32, device=dev)
+    _lib.check(L.zq_quantize_rows(C.c_void_p(x.data_ptr()), M, K, C.c_void_p(codes.data_ptr()), Kp,
+                                  C.c_void_p(rs.data_ptr()), sp))
+
+    def gemm_only():
+        _lib.check(L.zq_matmul_codes(W.handle, C.c_void_p(codes.data_ptr()), C.c_void_p(rs.data_ptr()), M, None,
+                                     C.c_void_p(y.data_ptr()), C.c_void_p(ws_ptr), ws_bytes, sp))
+
+    def quant_only():
+        _lib.check(L.zq_quantize_rows(C.c_void_p(x.data_ptr()), M, K, C.c_void_p(codes.data_ptr()), Kp,
+                                      C.c_void_p(rs.data_ptr()), sp))
+
+    def time_loop(fn, n):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(n):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        return a.elapsed_time(b) / n
+
+    reps = max(args.steps, 10)
+    gemm_ms = time_loop(gemm_only, reps)
+    quant_ms = time_loop(quant_only, reps)
+    code = zb.device_error(stream)
+
+    # End to end through the public host entry point (zq_matmul_host):
+    # pinned host x in, host y out, H2D + compute + D2H inside every step.
+    x_h = torch.empty((M, K), dtype=torch.float32, pin_memory=True)
+    x_h.copy_(x.cpu())
+    y_h = torch.empty((M, n_loc), dtype=torch.float32, pin_memory=True)
+
+    def e2e_step():
+        _lib.check(L.zq_matmul_host(W.handle, C.c_void_p(x_h.data_ptr()), M, None, C.c_void_p(y_h.data_ptr()), sp))
+
+    e2e_ms = float("nan")
+    if not args.no_e2e:
+        e2e_steps = max(3, min(args.steps, 10))
+        for _ in range(max(1, min(args.warmup, 3))):
+            e2e_step()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        b.record(stream)
+        barrier()
+        e2e_ms = a.elapsed_time(b) / e2e_steps
+
+    # max over ranks
+    if world > 1:
+        t = torch.tensor([ms, gemm_ms, quant_ms, e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, gemm_ms, quant_ms, e2e_ms = t.tolist()
+
+    if rank != 0:
+        return
+
+    total_ops = ops(M, N, K)
+    value = total_ops / (ms * 1e-3) / 1e12
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    if "bf16_tflops" in peaks:
+        int8_peak = 2.0 * float(peaks["bf16_tflops"])
+        peak_src = "measured: 2 x MEASURED_PEAKS bf16_tflops (burst); int8 dense MMA rate is twice bf16 on sm_100"
+    else:
+        int8_peak = 2.0 * 1590.0
+        peak_src = "fallback: 2 x 1590 TFLOP/s bf16 (earlier pool measurement)"
+    gemm_tops = ops(M, n_loc, K) / (gemm_ms * 1e-3) / 1e12
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "gemm_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch_full_workload")
+
+    cpu = None
+    if world == 1 and not args.skip_cpu_baseline:
+        try:
+            zyq = W.save_bytes()
+            from oracle import oracle as O
+
+            rows = max(1, min(64, O.ref_set_threads(os.cpu_count() or 1) if O.ref_available() else 1))
+            xs = x[:rows].cpu().numpy()
+            call, threads, kind, _keep = reference_cpu_timer(zyq, xs)
+            call()  # warm
+            tc = min(call() for _ in range(2))
+            cpu = {"value": ops(rows, N, K) / tc / 1e12, "unit": UNIT, "cores": threads,
+                   "kind": kind,
+                   "sample": f"{rows} of {M} rows x K={K} x N={N} (same weights), best of 2, "
+                             f"ZYRON quantization::matmul on {threads} threads (os.cpu_count()={os.cpu_count()})"}
+        except Exception as exc:  # report, never fail the bench on the baseline leg
+            cpu = {"value": None, "unit": UNIT, "cores": None, "kind": None, "sample": f"failed: {exc}"}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": WORKLOAD if (M, K, N) == (M_ROWS, K_DIM, N_COLS) else f"prefill_int8_gemm_M{M}_K{K}_N{N}",
+                   "M": M, "K": K, "N": N, "weight": "int8 per-column (device quantize)",
+                   "x": "N(0,1) fp32", "w": "N(0,0.02) fp32 before quantization",
+                   "parallelism": f"column-sharded x{world}" + (" + NCCL all-gather of outputs" if world > 1 else ""),
+                   "l2": "inputs larger than L2 (x 256 MiB, W 512 MiB, y 2 GiB); no flush"},
+        "gpu_launches": (2 * args.steps),
+        "clocks": sampler.summary(),
+        "roofline": {"bound": "tensor", "kernel": "gemm_i8_kernel (tcgen05.mma kind::i8)",
+                     "achieved": gemm_tops, "peak": int8_peak, "unit": UNIT, "frac": gemm_tops / int8_peak,
+                     "peak_source": peak_src, "traffic": traffic,
+                     "ms_per_launch": gemm_ms, "ops_per_launch": ops(M, n_loc, K)},
+        "kernels_ms": {"quantize_rows": quant_ms, "gemm_i8": gemm_ms},
+        "e2e": {"value": total_ops / (e2e_ms * 1e-3) / 1e12 / (1 if world == 1 else 1), "unit": UNIT,
+                "ms_per_step": e2e_ms, "h2d_bytes_per_step": M * K * 4, "d2h_bytes_per_step": M * n_loc * 4,
+                "api": "zq_matmul_host (pinned host x -> host y), per rank on its column shard"},
+        "cpu_baseline": cpu,
+        "device_error": code,
+    }
+    if world > 1:
+        line["e2e"]["value"] = ops(M, N, K) / (e2e_ms * 1e-3) / 1e12
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--skip-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling runs)")
+    ap.add_argument("--shape", type=lambda v: tuple(int(t) for t in v.split(",")),
+                    default=(M_ROWS, K_DIM, N_COLS), help="M,K,N override for small profiling cases")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and world == 1 and args.gpus > 1:
+        raise SystemExit("--gpus > 1 must be launched with torch.distributed.run (one process per GPU)")
+
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,157 @@
+/*
+ * zq.h -- C ABI of the B200 quantized matmul library (libzyron_b200.so).
+ *
+ * This is the boundary under ZYRON's `zyron::quantization` API.  The C++20
+ * drop-in (zyron_b200/cpp: QuantizedMatrix, quantize, matmul, QuantizedLinear)
+ * and the Python bindings (zyron_b200/_lib.py) both call only these entry
+ * points.  Plain pointers and sizes; no C++ or torch types.
+ *
+ * Conventions
+ *   - Weights are the reference's logical [rows = K][cols = N] matrix.
+ *     Host payloads use the reference storage: column-major (element (r, c)
+ *     at linear index c*K + r), INT4 two codes per byte with the low nibble
+ *     holding the even linear index (reference: src/quantization/
+ *     quantization.cpp:52-67, 155).
+ *   - Activations x are fp32 row-major [m][K], outputs y fp32 row-major
+ *     [m][N].  Pointers named *_dev / x / y / out are device pointers on the
+ *     weight's device; *_host pointers are host memory (pinned or pageable).
+ *   - `stream` is a cudaStream_t; NULL selects the calling thread's
+ *     per-thread default stream.  Compute calls are asynchronous on it unless
+ *     stated otherwise.
+ *   - Every call validates its arguments on the host before any launch and
+ *     returns a zq_status.  zq_last_error() gives the calling thread's last
+ *     message; messages of errors the reference also raises are identical to
+ *     the reference's (e.g. "ZYRON quantization: weights are empty").
+ *   - There is no CPU fallback: without a usable sm_100 device every compute
+ *     call fails with ZQ_ERR_CUDA.
+ */
+#ifndef ZQ_H
+#define ZQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum zq_status {
+    ZQ_OK = 0,
+    ZQ_ERR_INVALID_ARGUMENT = 1, /* reference: std::invalid_argument */
+    ZQ_ERR_OUT_OF_RANGE = 2,     /* reference: std::out_of_range */
+    ZQ_ERR_OVERFLOW = 3,         /* reference: std::overflow_error */
+    ZQ_ERR_RUNTIME = 4,          /* reference: std::runtime_error (format, I/O) */
+    ZQ_ERR_CUDA = 5,             /* a CUDA runtime call failed */
+    ZQ_ERR_DEVICE_TIMEOUT = 6    /* a bounded device-side wait gave up */
+} zq_status;
+
+/* zyron::quantization::Type values (include/zyron/quantization/quantization.hpp:13-16). */
+#define ZQ_TYPE_INT8 1
+#define ZQ_TYPE_INT4 2
+
+/* A quantized weight resident in device memory (replaces the storage of
+ * zyron::quantization::QuantizedMatrix, quantization.hpp:18-52). */
+typedef struct zq_weight zq_weight;
+
+/* Last error message of the calling thread ("" if none). */
+const char* zq_last_error(void);
+
+/* ABI version of this header (bumped on incompatible changes). */
+int zq_abi_version(void);
+#define ZQ_ABI_VERSION 1
+
+/* ---- weights ------------------------------------------------------------ */
+
+/* Upload a quantized matrix given in the reference's host storage: `scales`
+ * has `cols` floats, `payload` has rows*cols bytes (INT8) or
+ * ceil(rows*cols/2) bytes (INT4).  The device copy is made on the current
+ * device.  Replaces the storage fill of quantize() / QuantizedMatrix::load
+ * (quantization.cpp:121-162, 269-311) with a device upload. */
+zq_status zq_weight_create(int type, size_t rows, size_t cols, const float* scales_host,
+                           const void* payload_host, size_t payload_bytes, void* stream,
+                           zq_weight** out);
+
+/* quantize() on the device: w_dev is fp32 row-major [rows][cols] on the
+ * current device.  Bit-identical to the reference's quantize()
+ * (quantization.cpp:121-162). */
+zq_status zq_weight_quantize(const float* w_dev, size_t rows, size_t cols, int type, void* stream,
+                             zq_weight** out);
+
+/* Parse one .zyq record from memory and upload it (QuantizedMatrix::load(istream),
+ * quantization.cpp:269-311: same checks, same order, same messages).  On
+ * success *consumed is the number of bytes of the record. */
+zq_status zq_weight_load_zyq(const void* bytes, size_t len, size_t* consumed, void* stream,
+                             zq_weight** out);
+
+/* Serialise to the .zyq format (QuantizedMatrix::save(ostream),
+ * quantization.cpp:247-261).  Call with buf == NULL to get the size in *len.
+ * Synchronous. */
+zq_status zq_weight_save_zyq(const zq_weight* w, void* buf, size_t cap, size_t* len, void* stream);
+
+/* Shape / type / payload size in the reference's storage / device ordinal. */
+zq_status zq_weight_info(const zq_weight* w, int* type, size_t* rows, size_t* cols,
+                         size_t* payload_bytes, int* device);
+
+/* Copy scales and the reference-layout payload back to the host.  Synchronous. */
+zq_status zq_weight_download(const zq_weight* w, float* scales_host, void* payload_host, void* stream);
+
+/* A new weight holding columns [col_begin, col_end) of `w` (device to device,
+ * current device).  Used for column-parallel sharding: a column's codes and
+ * scale are independent of every other column. */
+zq_status zq_weight_slice_cols(const zq_weight* w, size_t col_begin, size_t col_end, void* stream,
+                               zq_weight** out);
+
+zq_status zq_weight_destroy(zq_weight* w);
+
+/* ---- compute ------------------------------------------------------------ */
+
+/* Device scratch needed by zq_matmul for `m` activation rows. */
+size_t zq_matmul_workspace_bytes(const zq_weight* w, size_t m);
+
+/* The per-row dynamic activation quantizer on its own (quantization.cpp:
+ * 202-212): q is int8 [m][ldq] with ldq >= k (codes in [0, k), zeros in
+ * [k, ldq)), row_scale fp32 [m], all device. */
+zq_status zq_quantize_rows(const float* x, size_t m, size_t k, int8_t* q, size_t ldq, float* row_scale,
+                           void* stream);
+
+/* Row length of the activation codes zq_matmul_codes expects for `w`
+ * (rows rounded up to 16 codes for INT8, 32 for INT4). */
+size_t zq_weight_padded_k(const zq_weight* w);
+
+/* quantization::matmul (quantization.cpp:177-238) followed, when bias is not
+ * NULL, by QuantizedLinear::forward's bias add (quantized_linear.cpp:33-50).
+ * x [m][rows], bias [cols] or NULL, y [m][cols]; all device pointers.
+ * m <= 8 runs the HBM-bound GEMV, larger m the tcgen05 GEMM.  `workspace`
+ * must hold zq_matmul_workspace_bytes(w, m) bytes and must not be shared by
+ * calls that may overlap on the GPU.  Results are bit-identical to the
+ * reference. */
+zq_status zq_matmul(const zq_weight* w, const float* x, size_t m, const float* bias, float* y,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* zq_matmul with the activation quantizer already applied: q is int8
+ * [m][zq_weight_padded_k(w)] (as written by zq_quantize_rows with that ldq),
+ * row_scale fp32 [m].  Lets a producer kernel emit codes directly and lets
+ * the matmul kernel be timed on its own.  Same workspace rule as zq_matmul. */
+zq_status zq_matmul_codes(const zq_weight* w, const int8_t* q, const float* row_scale, size_t m,
+                          const float* bias, float* y, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The same computation from host buffers to host buffers: copies x (and
+ * bias) to the device, runs zq_matmul, copies y back and synchronises the
+ * stream.  Device buffers are cached per thread and grow as needed. */
+zq_status zq_matmul_host(const zq_weight* w, const float* x_host, size_t m, const float* bias_host,
+                         float* y_host, void* stream);
+
+/* QuantizedMatrix::dequantize() (quantization.cpp:164-175): out is fp32
+ * row-major [rows][cols] on the device. */
+zq_status zq_dequantize(const zq_weight* w, float* out, void* stream);
+
+/* Synchronise `stream`, then read and clear the current device's error word
+ * (0 = none; otherwise which bounded wait gave up).  Returns
+ * ZQ_ERR_DEVICE_TIMEOUT when the word was set. */
+zq_status zq_device_error(void* stream, uint32_t* code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ZQ_H */

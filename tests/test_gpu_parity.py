@@ -1,0 +1,177 @@
+"""GPU parity of the CUDA path against the oracle, through the C ABI.
+
+Integer work (activation codes, weight codes, payloads) and the fp32 outputs
+are compared BIT FOR BIT: the CUDA epilogue evaluates the reference's
+float(acc) * s_row * s_col (+ bias) with the same three roundings, so any
+difference is a bug.  The oracle (oracle/zq_oracle.c) is itself pinned to the
+reference by tests/test_oracle.py.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def bits(a):
+    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+
+
+def assert_bits_equal(got, want, what):
+    g, w = bits(got), bits(want)
+    if not np.array_equal(g, w):
+        bad = np.argwhere(g != w)
+        i = tuple(bad[0])
+        raise AssertionError(f"{what}: {len(bad)} mismatches, first at {i}: got {got[i]!r} want {want[i]!r}")
+
+
+def make(rng, M, K, N, edge=True):
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    w = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+    if edge:
+        if M > 1:
+            x[1] = 0.0
+        if M > 2:
+            x[2, 0] = np.nan
+        if M > 3:
+            x[3, K // 2] = np.inf
+        if N > 2:
+            w[:, 1] = 0.0
+    return x, w
+
+
+@pytest.fixture(scope="module")
+def zb(cuda):
+    import zyron_b200
+
+    return zyron_b200
+
+
+def test_golden_vectors_through_cuda(zb, golden):
+    import torch
+
+    for ci, (M, K, N) in enumerate(golden["shapes"]):
+        M, K, N = int(M), int(K), int(N)
+        x = torch.from_numpy(golden[f"c{ci}_x"]).cuda()
+        bias = torch.from_numpy(golden[f"c{ci}_bias"]).cuda()
+        for qt in (1, 2):
+            p = f"c{ci}_t{qt}"
+            W = zb.QuantizedMatrix.from_parts(qt, K, N, golden[p + "_scales"], golden[p + "_payload"])
+            assert_bits_equal(zb.matmul(x, W).cpu().numpy(), golden[p + "_y"], p + " matmul")
+            assert_bits_equal(zb.matmul(x, W, bias=bias).cpu().numpy(), golden[p + "_ylin"], p + " linear")
+            assert_bits_equal(W.dequantize().cpu().numpy(), golden[p + "_deq"], p + " dequantize")
+            assert W.save_bytes() == golden[p + "_zyq"].tobytes(), p + " save"
+            W2 = zb.QuantizedMatrix.load_bytes(golden[p + "_zyq"].tobytes())
+            assert np.array_equal(W2.payload(), golden[p + "_payload"])
+            # device quantize() == reference quantize()
+            Wq = zb.quantize(torch.from_numpy(golden[f"c{ci}_w"]).cuda(), zb.Type(qt))
+            assert np.array_equal(Wq.payload(), golden[p + "_payload"]), p + " device quantize payload"
+            assert_bits_equal(Wq.scales(), golden[p + "_scales"], p + " device quantize scales")
+    assert zb.device_error() == 0
+
+
+@pytest.mark.parametrize("M,K", [(1, 1), (3, 17), (8, 4096), (37, 1000), (300, 2048), (2, 3)])
+def test_quantize_rows_bit_exact(zb, M, K):
+    import torch
+
+    rng = np.random.default_rng(M * 7 + K)
+    x, _ = make(rng, M, K, 1)
+    if M > 4:
+        x[4] = np.float32(1e-45) * rng.integers(-3, 4, K)  # denormals
+    if M > 5 and K > 3:
+        x[5] = 0.5
+        x[5, 0] = 127.0
+        x[5, 1] = -2.5
+        x[5, 2] = 3.5
+    q, s = zb.quantize_rows(torch.from_numpy(x).cuda())
+    qo, so = O.quantize_rows(x)
+    assert np.array_equal(q.cpu().numpy(), qo)
+    assert_bits_equal(s.cpu().numpy(), so, "row scales")
+
+
+SHAPES = [
+    # decode GEMV sizes (M <= 8)
+    (1, 64, 7), (1, 4096, 1000), (2, 31, 33), (3, 129, 255), (5, 1000, 300), (8, 4096, 1100), (8, 33, 1),
+    # tcgen05 GEMM sizes: ragged M / N / K around the 128 x {64,128,256} tiles
+    (9, 64, 130), (64, 512, 512), (127, 256, 64), (128, 128, 256), (129, 384, 257), (200, 1000, 100),
+    (256, 2048, 520), (300, 17, 33), (513, 640, 1024), (1024, 256, 4096),
+]
+
+
+@pytest.mark.parametrize("qt", [1, 2])
+@pytest.mark.parametrize("M,K,N", SHAPES)
+def test_matmul_bit_exact(zb, qt, M, K, N):
+    import torch
+
+    rng = np.random.default_rng(M * 131 + K * 7 + N + qt)
+    x, w = make(rng, M, K, N)
+    b = rng.standard_normal(N).astype(np.float32)
+    pay, sc = O.quantize_weights(w, qt)
+    W = zb.QuantizedMatrix.from_parts(qt, K, N, sc, pay)
+    xd = torch.from_numpy(x).cuda()
+    y = zb.matmul(xd, W).cpu().numpy()
+    _, _, _, yo = O.matmul(x, qt, pay, sc, N)
+    assert_bits_equal(y, yo, f"matmul t{qt} {M}x{K}x{N}")
+    yb = zb.matmul(xd, W, bias=torch.from_numpy(b).cuda()).cpu().numpy()
+    _, _, _, ybo = O.matmul(x, qt, pay, sc, N, b)
+    assert_bits_equal(yb, ybo, f"linear t{qt} {M}x{K}x{N}")
+    assert zb.device_error() == 0
+
+
+@pytest.mark.parametrize("qt", [1, 2])
+def test_host_entry_point(zb, qt):
+    rng = np.random.default_rng(11 + qt)
+    for M, K, N in [(1, 300, 70), (40, 96, 130)]:
+        x, w = make(rng, M, K, N)
+        b = rng.standard_normal(N).astype(np.float32)
+        pay, sc = O.quantize_weights(w, qt)
+        W = zb.QuantizedMatrix.from_parts(qt, K, N, sc, pay)
+        assert_bits_equal(zb.matmul(x, W, bias=b), O.matmul(x, qt, pay, sc, N, b)[3], "host matmul")
+        # rank-3 input keeps its leading dims (quantization.cpp:192-196)
+        y3 = zb.matmul(x.reshape(1, M, K), W)
+        assert y3.shape == (1, M, N)
+
+
+def test_quantized_linear_mirror(zb):
+    """Mirror of the reference's test_quantized_linear (tests/test_phase5.cpp:129-155),
+    with the tolerance check replaced by bit-exact comparison to the oracle."""
+    import torch
+
+    rng = np.random.default_rng(31)
+    weight = rng.uniform(-0.5, 0.5, (16, 8)).astype(np.float32)
+    bias = rng.uniform(-0.2, 0.2, 8).astype(np.float32)
+    inp = rng.uniform(-1, 1, (4, 5, 16)).astype(np.float32)
+    for qt in (zb.Type.Int8, zb.Type.Int4):
+        lin = zb.QuantizedLinear(torch.from_numpy(weight).cuda(), bias, qt)
+        out = lin(torch.from_numpy(inp).cuda()).cpu().numpy()
+        assert out.shape == (4, 5, 8)
+        pay, sc = O.quantize_weights(weight, int(qt))
+        ref = O.matmul(inp.reshape(20, 16), int(qt), pay, sc, 8, bias)[3].reshape(4, 5, 8)
+        assert_bits_equal(out, ref, "QuantizedLinear")
+        fp = inp.reshape(20, 16) @ weight + bias
+        assert np.max(np.abs(fp.reshape(4, 5, 8) - out)) < (0.2 if qt == zb.Type.Int8 else 0.6)
+
+
+def test_slice_cols_and_odd_k_int4_roundtrip(zb):
+    import torch
+
+    rng = np.random.default_rng(5)
+    for qt, K, N in [(2, 33, 9), (2, 31, 70), (1, 7, 5)]:
+        _, w = make(rng, 2, K, N, edge=False)
+        pay, sc = O.quantize_weights(w, qt)
+        W = zb.QuantizedMatrix.from_parts(qt, K, N, sc, pay)
+        assert np.array_equal(W.payload(), pay)
+        for c in range(N):
+            for r in (0, K - 1):
+                assert W.value(c, r) == int(O.unpack_codes(qt, pay, K, N)[c, r])
+        S = W.slice_cols(2, N - 1)
+        codes = O.unpack_codes(qt, pay, K, N)[2:N - 1]
+        assert np.array_equal(O.unpack_codes(qt, S.payload(), K, N - 3), codes)
+        assert_bits_equal(S.scales(), sc[2:N - 1], "slice scales")
+        x = rng.standard_normal((3, K)).astype(np.float32)
+        full = zb.matmul(torch.from_numpy(x).cuda(), W).cpu().numpy()
+        part = zb.matmul(torch.from_numpy(x).cuda(), S).cpu().numpy()
+        assert_bits_equal(part, full[:, 2:N - 1], "column shard")

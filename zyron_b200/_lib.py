@@ -1,0 +1,133 @@
+"""ctypes binding of the C ABI in include/zq.h (libzyron_b200.so).
+
+The library is built in-tree (``python -m zyron_b200.build``).  There is no
+fallback: if the shared library is missing, :func:`lib` raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libzyron_b200.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "zq.h")
+
+ZQ_OK = 0
+ZQ_ERR_INVALID_ARGUMENT = 1
+ZQ_ERR_OUT_OF_RANGE = 2
+ZQ_ERR_OVERFLOW = 3
+ZQ_ERR_RUNTIME = 4
+ZQ_ERR_CUDA = 5
+ZQ_ERR_DEVICE_TIMEOUT = 6
+
+
+class ZQError(Exception):
+    """Base class; ``status`` is the zq_status code."""
+
+    status = -1
+
+
+class ZQInvalidArgument(ZQError, ValueError):
+    """std::invalid_argument in the reference."""
+
+    status = ZQ_ERR_INVALID_ARGUMENT
+
+
+class ZQOutOfRange(ZQError, IndexError):
+    """std::out_of_range in the reference."""
+
+    status = ZQ_ERR_OUT_OF_RANGE
+
+
+class ZQOverflow(ZQError, OverflowError):
+    """std::overflow_error in the reference."""
+
+    status = ZQ_ERR_OVERFLOW
+
+
+class ZQRuntimeError(ZQError, RuntimeError):
+    """std::runtime_error in the reference (format / I/O)."""
+
+    status = ZQ_ERR_RUNTIME
+
+
+class ZQCudaError(ZQError, RuntimeError):
+    status = ZQ_ERR_CUDA
+
+
+class ZQDeviceTimeout(ZQError, RuntimeError):
+    status = ZQ_ERR_DEVICE_TIMEOUT
+
+
+_ERRORS = {
+    ZQ_ERR_INVALID_ARGUMENT: ZQInvalidArgument,
+    ZQ_ERR_OUT_OF_RANGE: ZQOutOfRange,
+    ZQ_ERR_OVERFLOW: ZQOverflow,
+    ZQ_ERR_RUNTIME: ZQRuntimeError,
+    ZQ_ERR_CUDA: ZQCudaError,
+    ZQ_ERR_DEVICE_TIMEOUT: ZQDeviceTimeout,
+}
+
+_lib = None
+_lock = threading.Lock()
+
+vp = C.c_void_p
+sz = C.c_size_t
+st = C.c_int
+
+# name -> (restype, argtypes); must match include/zq.h
+SIGNATURES = {
+    "zq_last_error": (C.c_char_p, []),
+    "zq_abi_version": (C.c_int, []),
+    "zq_weight_create": (st, [C.c_int, sz, sz, vp, vp, sz, vp, C.POINTER(vp)]),
+    "zq_weight_quantize": (st, [vp, sz, sz, C.c_int, vp, C.POINTER(vp)]),
+    "zq_weight_load_zyq": (st, [vp, sz, C.POINTER(sz), vp, C.POINTER(vp)]),
+    "zq_weight_save_zyq": (st, [vp, vp, sz, C.POINTER(sz), vp]),
+    "zq_weight_info": (st, [vp, C.POINTER(C.c_int), C.POINTER(sz), C.POINTER(sz), C.POINTER(sz),
+                            C.POINTER(C.c_int)]),
+    "zq_weight_download": (st, [vp, vp, vp, vp]),
+    "zq_weight_slice_cols": (st, [vp, sz, sz, vp, C.POINTER(vp)]),
+    "zq_weight_destroy": (st, [vp]),
+    "zq_matmul_workspace_bytes": (sz, [vp, sz]),
+    "zq_quantize_rows": (st, [vp, sz, sz, vp, sz, vp, vp]),
+    "zq_weight_padded_k": (sz, [vp]),
+    "zq_matmul_codes": (st, [vp, vp, vp, sz, vp, vp, vp, sz, vp]),
+    "zq_matmul": (st, [vp, vp, sz, vp, vp, vp, sz, vp]),
+    "zq_matmul_host": (st, [vp, vp, sz, vp, vp, vp]),
+    "zq_dequantize": (st, [vp, vp, vp]),
+    "zq_device_error": (st, [vp, C.POINTER(C.c_uint32)]),
+}
+
+
+def header_symbols():
+    """Entry points declared in include/zq.h."""
+    with open(HEADER) as f:
+        text = f.read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(zq_[a-z0-9_]+)\s*\(", text)))
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise ImportError(
+                        f"zyron_b200 native library not built: {LIB_PATH} is missing "
+                        "(run `python -m zyron_b200.build`)")
+                L = C.CDLL(LIB_PATH)
+                for name, (res, args) in SIGNATURES.items():
+                    fn = getattr(L, name)
+                    fn.restype = res
+                    fn.argtypes = args
+                _lib = L
+    return _lib
+
+
+def check(status):
+    if status != ZQ_OK:
+        msg = lib().zq_last_error().decode(errors="replace")
+        raise _ERRORS.get(status, ZQError)(msg)

@@ -1,0 +1,618 @@
+// zq_api.cu -- the C ABI (include/zq.h) over the B200 kernels.
+//
+// Host-side responsibilities: argument validation with the reference's
+// messages, device weight objects in the panel layout, .zyq parsing /
+// writing, tensor-map creation for the tcgen05 GEMM, kernel dispatch and the
+// device error word.  No entry point falls back to the CPU.
+#include "zq.h"
+#include "zq_common.cuh"
+#include "zq_kernels.h"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <limits>
+#include <mutex>
+#include <string>
+#include <vector>
+
+// Error word written by bounded device waits (see mbar_wait_bounded).  One
+// per device; the host reads and clears it in zq_device_error().
+__device__ uint32_t g_zq_device_error = 0;
+
+struct zq_weight {
+    int type = 0;
+    size_t K = 0, N = 0;
+    int Kp = 0;
+    int device = 0;
+    uint8_t* panel = nullptr;  // [N][Kp] int8 or [N][Kp/2] packed int4
+    float* scales = nullptr;   // [N]
+    size_t panel_bytes = 0;
+    // Tensor maps over the INT8 panel, one per GEMM tile width (64/128/256).
+    std::mutex mu;
+    CUtensorMap tmap_b[3];
+    bool tmap_ready[3] = {false, false, false};
+};
+
+namespace {
+
+constexpr uint32_t kZyqMagic = 0x315A5951u;  // "QYZ1" (quantization.cpp:20)
+constexpr uint32_t kZyqVersion = 1;          // quantization.cpp:21
+
+thread_local std::string t_last_error;
+
+zq_status fail(zq_status s, const std::string& msg) {
+    t_last_error = msg;
+    return s;
+}
+
+zq_status cuda_fail(cudaError_t e, const char* what) {
+    std::string m = "zyron_b200: CUDA error in ";
+    m += what;
+    m += ": ";
+    m += cudaGetErrorName(e);
+    m += " (";
+    m += cudaGetErrorString(e);
+    m += ")";
+    return fail(ZQ_ERR_CUDA, m);
+}
+
+#define ZQ_CUDA(call)                                         \
+    do {                                                      \
+        cudaError_t _e = (call);                              \
+        if (_e != cudaSuccess) return cuda_fail(_e, #call);   \
+    } while (0)
+
+cudaStream_t as_stream(void* s) { return s ? static_cast<cudaStream_t>(s) : cudaStreamPerThread; }
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+bool mul_overflows(size_t a, size_t b) { return a != 0 && b > std::numeric_limits<size_t>::max() / a; }
+
+size_t ref_payload_bytes(int type, size_t K, size_t N) {
+    const size_t e = K * N;
+    return type == ZQ_TYPE_INT8 ? e : (e + 1) / 2;
+}
+
+size_t col_bytes(const zq_weight* w) { return w->type == ZQ_TYPE_INT8 ? (size_t)w->Kp : (size_t)w->Kp / 2; }
+
+// ---- driver entry point for tensor-map encoding (no libcuda link) ---------
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+zq_status get_encoder() {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    if (!g_encode) return fail(ZQ_ERR_CUDA, "zyron_b200: cuTensorMapEncodeTiled is unavailable");
+    return ZQ_OK;
+}
+
+// 2D K-major int8 map: rows x Kp bytes, box 128 bytes x box_rows, 128 B swizzle.
+zq_status encode_kmajor(CUtensorMap* map, const void* base, size_t rows, int Kp, int box_rows) {
+    zq_status s = get_encoder();
+    if (s != ZQ_OK) return s;
+    cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)Kp};
+    cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1u, 1u};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        char buf[160];
+        std::snprintf(buf, sizeof buf, "zyron_b200: cuTensorMapEncodeTiled failed (%d) rows=%zu Kp=%d box=%d",
+                      (int)r, rows, Kp, box_rows);
+        return fail(ZQ_ERR_CUDA, buf);
+    }
+    return ZQ_OK;
+}
+
+// ---- device error word ----------------------------------------------------
+std::mutex g_err_mu;
+uint32_t* g_err_ptr[64] = {nullptr};
+
+zq_status device_error_ptr(uint32_t** out) {
+    int dev = 0;
+    ZQ_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(ZQ_ERR_CUDA, "zyron_b200: device ordinal out of range");
+    std::lock_guard<std::mutex> lk(g_err_mu);
+    if (!g_err_ptr[dev]) {
+        void* p = nullptr;
+        ZQ_CUDA(cudaGetSymbolAddress(&p, g_zq_device_error));
+        g_err_ptr[dev] = static_cast<uint32_t*>(p);
+    }
+    *out = g_err_ptr[dev];
+    return ZQ_OK;
+}
+
+zq_status check_dims(size_t rows, size_t cols) {
+    if (rows == 0 || cols == 0) return fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON quantization: weights are empty");
+    if (mul_overflows(rows, cols)) return fail(ZQ_ERR_OVERFLOW, "ZYRON quantization: matrix size overflow");
+    if (rows > (size_t)std::numeric_limits<int>::max() - 64 || cols > (size_t)std::numeric_limits<int>::max())
+        return fail(ZQ_ERR_OVERFLOW, "zyron_b200: matrix dimension exceeds 2^31-1");
+    return ZQ_OK;
+}
+
+zq_status new_weight(int type, size_t K, size_t N, zq_weight** out) {
+    auto* w = new (std::nothrow) zq_weight;
+    if (!w) return fail(ZQ_ERR_RUNTIME, "zyron_b200: out of host memory");
+    w->type = type;
+    w->K = K;
+    w->N = N;
+    w->Kp = zq::padded_k(type, (int)K);
+    cudaGetDevice(&w->device);
+    w->panel_bytes = N * col_bytes(w);
+    cudaError_t e = cudaMalloc(&w->panel, w->panel_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&w->scales, N * sizeof(float));
+    if (e != cudaSuccess) {
+        cudaFree(w->panel);
+        cudaFree(w->scales);
+        delete w;
+        return cuda_fail(e, "cudaMalloc(weight)");
+    }
+    *out = w;
+    return ZQ_OK;
+}
+
+// Upload reference-layout payload into an allocated panel.
+zq_status upload_payload(zq_weight* w, const void* payload, cudaStream_t st) {
+    const size_t K = w->K, N = w->N;
+    ZQ_CUDA(cudaMemsetAsync(w->panel, 0, w->panel_bytes, st));
+    if (w->type == ZQ_TYPE_INT8) {
+        ZQ_CUDA(cudaMemcpy2DAsync(w->panel, (size_t)w->Kp, payload, K, K, N, cudaMemcpyHostToDevice, st));
+    } else if (K % 2 == 0) {
+        ZQ_CUDA(cudaMemcpy2DAsync(w->panel, (size_t)w->Kp / 2, payload, K / 2, K / 2, N, cudaMemcpyHostToDevice,
+                                  st));
+    } else {
+        const size_t bytes = ref_payload_bytes(w->type, K, N);
+        uint8_t* tmp = nullptr;
+        ZQ_CUDA(cudaMalloc(&tmp, bytes));
+        cudaError_t e = cudaMemcpyAsync(tmp, payload, bytes, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = zq::launch_repack_int4(tmp, (int)K, (int)N, w->Kp, w->panel, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        cudaFree(tmp);
+        if (e != cudaSuccess) return cuda_fail(e, "int4 repack upload");
+    }
+    return ZQ_OK;
+}
+
+zq_status download_payload(const zq_weight* w, void* payload, cudaStream_t st) {
+    const size_t K = w->K, N = w->N;
+    if (w->type == ZQ_TYPE_INT8) {
+        ZQ_CUDA(cudaMemcpy2DAsync(payload, K, w->panel, (size_t)w->Kp, K, N, cudaMemcpyDeviceToHost, st));
+    } else if (K % 2 == 0) {
+        ZQ_CUDA(cudaMemcpy2DAsync(payload, K / 2, w->panel, (size_t)w->Kp / 2, K / 2, N, cudaMemcpyDeviceToHost,
+                                  st));
+    } else {
+        const size_t bytes = ref_payload_bytes(w->type, K, N);
+        uint8_t* tmp = nullptr;
+        ZQ_CUDA(cudaMalloc(&tmp, bytes));
+        cudaError_t e = zq::launch_unpack_panel_int4(w->panel, (int)K, (int)N, w->Kp, tmp, st);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(payload, tmp, bytes, cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        cudaFree(tmp);
+        if (e != cudaSuccess) return cuda_fail(e, "int4 download");
+        return ZQ_OK;
+    }
+    ZQ_CUDA(cudaStreamSynchronize(st));
+    return ZQ_OK;
+}
+
+int tile_index(int block_n) { return block_n == 256 ? 2 : (block_n == 128 ? 1 : 0); }
+
+// Per-thread device buffers of zq_matmul_host.
+struct HostStaging {
+    int device = -1;
+    void* x = nullptr;
+    size_t x_cap = 0;
+    void* y = nullptr;
+    size_t y_cap = 0;
+    void* b = nullptr;
+    size_t b_cap = 0;
+    void* ws = nullptr;
+    size_t ws_cap = 0;
+    ~HostStaging() {
+        cudaFree(x);
+        cudaFree(y);
+        cudaFree(b);
+        cudaFree(ws);
+    }
+};
+thread_local HostStaging t_staging;
+
+cudaError_t ensure(void*& p, size_t& cap, size_t need) {
+    if (cap >= need) return cudaSuccess;
+    cudaFree(p);
+    p = nullptr;
+    cap = 0;
+    cudaError_t e = cudaMalloc(&p, need);
+    if (e == cudaSuccess) cap = need;
+    return e;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* zq_last_error(void) { return t_last_error.c_str(); }
+
+int zq_abi_version(void) { return ZQ_ABI_VERSION; }
+
+zq_status zq_weight_create(int type, size_t rows, size_t cols, const float* scales_host, const void* payload_host,
+                           size_t payload_bytes, void* stream, zq_weight** out) {
+    if (!out) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null output handle");
+    *out = nullptr;
+    if (type != ZQ_TYPE_INT8 && type != ZQ_TYPE_INT4)
+        return fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON quantization: unsupported type");
+    zq_status s = check_dims(rows, cols);
+    if (s != ZQ_OK) return s;
+    if (!scales_host || !payload_host) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null scales or payload");
+    if (payload_bytes != ref_payload_bytes(type, rows, cols))
+        return fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON quantization: invalid payload size");
+    zq_weight* w = nullptr;
+    s = new_weight(type, rows, cols, &w);
+    if (s != ZQ_OK) return s;
+    cudaStream_t st = as_stream(stream);
+    s = upload_payload(w, payload_host, st);
+    if (s == ZQ_OK) {
+        cudaError_t e = cudaMemcpyAsync(w->scales, scales_host, cols * sizeof(float), cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) s = cuda_fail(e, "weight upload");
+    }
+    if (s != ZQ_OK) {
+        zq_weight_destroy(w);
+        return s;
+    }
+    *out = w;
+    return ZQ_OK;
+}
+
+zq_status zq_weight_quantize(const float* w_dev, size_t rows, size_t cols, int type, void* stream, zq_weight** out) {
+    if (!out) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null output handle");
+    *out = nullptr;
+    if (type != ZQ_TYPE_INT8 && type != ZQ_TYPE_INT4)
+        return fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON quantization: unsupported type");
+    zq_status s = check_dims(rows, cols);
+    if (s != ZQ_OK) return s;
+    if (!w_dev) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null weights");
+    zq_weight* w = nullptr;
+    s = new_weight(type, rows, cols, &w);
+    if (s != ZQ_OK) return s;
+    cudaStream_t st = as_stream(stream);
+    uint32_t* tmp = nullptr;
+    cudaError_t e = cudaMalloc(&tmp, cols * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemsetAsync(w->panel, 0, w->panel_bytes, st);
+    if (e == cudaSuccess)
+        e = zq::launch_quantize_weights(w_dev, (int)rows, (int)cols, w->Kp, type, tmp, w->scales, w->panel, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    cudaFree(tmp);
+    if (e != cudaSuccess) {
+        zq_weight_destroy(w);
+        return cuda_fail(e, "device quantize");
+    }
+    *out = w;
+    return ZQ_OK;
+}
+
+zq_status zq_weight_load_zyq(const void* bytes, size_t len, size_t* consumed, void* stream, zq_weight** out) {
+    if (!out) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null output handle");
+    *out = nullptr;
+    const uint8_t* p = static_cast<const uint8_t*>(bytes);
+    size_t off = 0;
+    auto read = [&](void* dst, size_t n) -> bool {
+        if (!p || len - off < n || off > len) return false;
+        std::memcpy(dst, p + off, n);
+        off += n;
+        return true;
+    };
+    const char* corrupted = "ZYRON quantization: corrupted file";
+    uint32_t magic = 0, version = 0, type = 0;
+    uint64_t rows = 0, cols = 0, scale_count = 0, payload = 0;
+    // quantization.cpp:270-272 (short-circuit: the version is read only when
+    // the magic matches)
+    if (!read(&magic, 4)) return fail(ZQ_ERR_RUNTIME, corrupted);
+    if (magic != kZyqMagic) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: unsupported format");
+    if (!read(&version, 4)) return fail(ZQ_ERR_RUNTIME, corrupted);
+    if (version != kZyqVersion) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: unsupported format");
+    // 275-279
+    if (!read(&type, 4)) return fail(ZQ_ERR_RUNTIME, corrupted);
+    if (type != ZQ_TYPE_INT8 && type != ZQ_TYPE_INT4) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: invalid type");
+    // 280-289
+    if (!read(&rows, 8) || !read(&cols, 8)) return fail(ZQ_ERR_RUNTIME, corrupted);
+    if (rows == 0 || cols == 0) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: invalid matrix dimensions");
+    if (mul_overflows((size_t)rows, (size_t)cols)) return fail(ZQ_ERR_OVERFLOW, "ZYRON quantization: matrix size overflow");
+    // 291-297
+    if (!read(&scale_count, 8)) return fail(ZQ_ERR_RUNTIME, corrupted);
+    if (scale_count != cols) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: invalid scale count");
+    if (mul_overflows((size_t)cols, sizeof(float)) || len - off < cols * sizeof(float))
+        return fail(ZQ_ERR_RUNTIME, corrupted);
+    std::vector<float> scales((size_t)cols);
+    read(scales.data(), cols * sizeof(float));
+    for (float s : scales)
+        if (!(s > 0.0f) || !std::isfinite(s)) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: invalid scale");
+    // 299-309
+    if (!read(&payload, 8)) return fail(ZQ_ERR_RUNTIME, corrupted);
+    const size_t expected = ref_payload_bytes((int)type, (size_t)rows, (size_t)cols);
+    if (payload != expected) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: invalid payload size");
+    if (len - off < expected) return fail(ZQ_ERR_RUNTIME, corrupted);
+    const void* pay = p + off;
+    off += expected;
+    zq_status s = zq_weight_create((int)type, (size_t)rows, (size_t)cols, scales.data(), pay, expected, stream, out);
+    if (s == ZQ_OK && consumed) *consumed = off;
+    return s;
+}
+
+zq_status zq_weight_info(const zq_weight* w, int* type, size_t* rows, size_t* cols, size_t* payload_bytes,
+                         int* device) {
+    if (!w) return fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON quantization: weights are empty");
+    if (type) *type = w->type;
+    if (rows) *rows = w->K;
+    if (cols) *cols = w->N;
+    if (payload_bytes) *payload_bytes = ref_payload_bytes(w->type, w->K, w->N);
+    if (device) *device = w->device;
+    return ZQ_OK;
+}
+
+zq_status zq_weight_download(const zq_weight* w, float* scales_host, void* payload_host, void* stream) {
+    if (!w) return fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON quantization: weights are empty");
+    cudaStream_t st = as_stream(stream);
+    if (scales_host) ZQ_CUDA(cudaMemcpyAsync(scales_host, w->scales, w->N * sizeof(float), cudaMemcpyDeviceToHost, st));
+    if (payload_host) {
+        zq_status s = download_payload(w, payload_host, st);
+        if (s != ZQ_OK) return s;
+    }
+    ZQ_CUDA(cudaStreamSynchronize(st));
+    return ZQ_OK;
+}
+
+zq_status zq_weight_save_zyq(const zq_weight* w, void* buf, size_t cap, size_t* len, void* stream) {
+    if (!w) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: cannot save empty matrix");
+    const size_t pay = ref_payload_bytes(w->type, w->K, w->N);
+    const size_t total = 4 * 3 + 8 * 3 + w->N * sizeof(float) + 8 + pay;
+    if (len) *len = total;
+    if (!buf) return ZQ_OK;
+    if (cap < total) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: buffer too small");
+    uint8_t* p = static_cast<uint8_t*>(buf);
+    const uint32_t h32[3] = {kZyqMagic, kZyqVersion, (uint32_t)w->type};
+    const uint64_t h64[3] = {(uint64_t)w->K, (uint64_t)w->N, (uint64_t)w->N};
+    std::memcpy(p, h32, 12);
+    std::memcpy(p + 12, h64, 24);
+    float* scales = reinterpret_cast<float*>(p + 36);
+    const uint64_t pay64 = pay;
+    uint8_t* pay_at = p + 36 + w->N * sizeof(float);
+    std::memcpy(pay_at, &pay64, 8);
+    // scales may be unaligned inside the caller's buffer: go through a copy
+    std::vector<float> sc(w->N);
+    zq_status s = zq_weight_download(w, sc.data(), pay_at + 8, stream);
+    if (s != ZQ_OK) return s;
+    std::memcpy(scales, sc.data(), w->N * sizeof(float));
+    return ZQ_OK;
+}
+
+zq_status zq_weight_slice_cols(const zq_weight* w, size_t col_begin, size_t col_end, void* stream, zq_weight** out) {
+    if (!out) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null output handle");
+    *out = nullptr;
+    if (!w) return fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON quantization: weights are empty");
+    if (col_begin >= col_end || col_end > w->N)
+        return fail(ZQ_ERR_OUT_OF_RANGE, "zyron_b200: column slice out of range");
+    zq_weight* r = nullptr;
+    zq_status s = new_weight(w->type, w->K, col_end - col_begin, &r);
+    if (s != ZQ_OK) return s;
+    cudaStream_t st = as_stream(stream);
+    const size_t cb = col_bytes(w);
+    cudaError_t e = cudaMemcpyAsync(r->panel, w->panel + col_begin * cb, r->panel_bytes, cudaMemcpyDefault, st);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(r->scales, w->scales + col_begin, r->N * sizeof(float), cudaMemcpyDefault, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+        zq_weight_destroy(r);
+        return cuda_fail(e, "column slice");
+    }
+    *out = r;
+    return ZQ_OK;
+}
+
+zq_status zq_weight_destroy(zq_weight* w) {
+    if (!w) return ZQ_OK;
+    int cur = 0;
+    cudaGetDevice(&cur);
+    if (cur != w->device) cudaSetDevice(w->device);
+    cudaFree(w->panel);
+    cudaFree(w->scales);
+    if (cur != w->device) cudaSetDevice(cur);
+    delete w;
+    return ZQ_OK;
+}
+
+size_t zq_matmul_workspace_bytes(const zq_weight* w, size_t m) {
+    if (!w || m == 0) return 0;
+    size_t b = align256(m * (size_t)w->Kp) + align256(m * sizeof(float));
+    if (w->type == ZQ_TYPE_INT4 && m > (size_t)zq::kGemvMaxRows) b += align256(w->N * (size_t)w->Kp);
+    return b;
+}
+
+zq_status zq_quantize_rows(const float* x, size_t m, size_t k, int8_t* q, size_t ldq, float* row_scale,
+                           void* stream) {
+    if (m == 0) return ZQ_OK;
+    if (k == 0) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: k must be > 0");
+    if (ldq < k) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: ldq must be >= k");
+    if (!x || !q || !row_scale) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null pointer");
+    if (m > (size_t)std::numeric_limits<int>::max() || ldq > (size_t)std::numeric_limits<int>::max() - 64)
+        return fail(ZQ_ERR_OVERFLOW, "zyron_b200: dimension exceeds 2^31-1");
+    ZQ_CUDA(zq::launch_quantize_rows(x, (int)m, (int)k, (int)ldq, q, row_scale, as_stream(stream)));
+    return ZQ_OK;
+}
+
+size_t zq_weight_padded_k(const zq_weight* w) { return w ? (size_t)w->Kp : 0; }
+
+}  // extern "C"
+
+namespace {
+
+zq_status validate_matmul(const zq_weight* w, size_t m, const void* in, const float* y, const void* workspace,
+                          size_t workspace_bytes) {
+    if (!in || !y) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null input or output");
+    if (m > (size_t)std::numeric_limits<int>::max())
+        return fail(ZQ_ERR_OVERFLOW, "zyron_b200: row count exceeds 2^31-1");
+    const size_t need = zq_matmul_workspace_bytes(w, m);
+    if (!workspace || workspace_bytes < need) {
+        char buf[128];
+        std::snprintf(buf, sizeof buf, "zyron_b200: workspace too small (%zu < %zu bytes)", workspace_bytes, need);
+        return fail(ZQ_ERR_INVALID_ARGUMENT, buf);
+    }
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+        return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: workspace must be 256-byte aligned");
+    int dev = 0;
+    ZQ_CUDA(cudaGetDevice(&dev));
+    if (dev != w->device) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: weight lives on another device");
+    return ZQ_OK;
+}
+
+// Dot + epilogue on activation codes q [m][Kp] (row stride Kp) and row
+// scales rs.  `scratch` is where INT4 weights are expanded for the GEMM.
+zq_status run_codes(const zq_weight* w, const int8_t* codes, const float* rs, size_t m, const float* bias, float* y,
+                    uint8_t* scratch, cudaStream_t st, bool pdl) {
+    uint32_t* err = nullptr;
+    zq_status s = device_error_ptr(&err);
+    if (s != ZQ_OK) return s;
+    const int M = (int)m, N = (int)w->N, Kp = w->Kp;
+    if (M <= zq::kGemvMaxRows && zq::gemv_smem_bytes(M, Kp) <= 200 * 1024) {
+        zq::GemvArgs a{w->type, w->panel, N, Kp, w->scales, codes, rs, bias, y, M};
+        ZQ_CUDA(zq::launch_gemv(a, st, pdl));
+        return ZQ_OK;
+    }
+    const int bn = zq::gemm_block_n(M, N);
+    CUtensorMap tmap_a;
+    s = encode_kmajor(&tmap_a, codes, m, Kp, 128);
+    if (s != ZQ_OK) return s;
+    const CUtensorMap* tmap_b = nullptr;
+    CUtensorMap tmap_b_local;
+    if (w->type == ZQ_TYPE_INT8) {
+        zq_weight* mw = const_cast<zq_weight*>(w);
+        std::lock_guard<std::mutex> lk(mw->mu);
+        const int ti = tile_index(bn);
+        if (!mw->tmap_ready[ti]) {
+            s = encode_kmajor(&mw->tmap_b[ti], w->panel, w->N, Kp, bn);
+            if (s != ZQ_OK) return s;
+            mw->tmap_ready[ti] = true;
+        }
+        tmap_b = &mw->tmap_b[ti];
+    } else {
+        int8_t* panel8 = reinterpret_cast<int8_t*>(scratch);
+        ZQ_CUDA(zq::launch_expand_int4(w->panel, N, Kp, panel8, st));
+        s = encode_kmajor(&tmap_b_local, panel8, w->N, Kp, bn);
+        if (s != ZQ_OK) return s;
+        tmap_b = &tmap_b_local;
+        pdl = true;  // the GEMM follows the expand kernel directly
+    }
+    zq::GemmArgs g{&tmap_a, tmap_b, M, N, Kp, bn, rs, w->scales, bias, y, err};
+    ZQ_CUDA(zq::launch_gemm(g, st, pdl));
+    return ZQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+zq_status zq_matmul(const zq_weight* w, const float* x, size_t m, const float* bias, float* y, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+    if (!w) return fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON quantization: weights are empty");
+    if (m == 0) return ZQ_OK;
+    zq_status s = validate_matmul(w, m, x, y, workspace, workspace_bytes);
+    if (s != ZQ_OK) return s;
+    cudaStream_t st = as_stream(stream);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    int8_t* codes = reinterpret_cast<int8_t*>(ws);
+    float* rs = reinterpret_cast<float*>(ws + align256(m * (size_t)w->Kp));
+    uint8_t* scratch = ws + align256(m * (size_t)w->Kp) + align256(m * sizeof(float));
+    ZQ_CUDA(zq::launch_quantize_rows(x, (int)m, (int)w->K, w->Kp, codes, rs, st));
+    return run_codes(w, codes, rs, m, bias, y, scratch, st, true);
+}
+
+zq_status zq_matmul_codes(const zq_weight* w, const int8_t* q, const float* row_scale, size_t m, const float* bias,
+                          float* y, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!w) return fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON quantization: weights are empty");
+    if (m == 0) return ZQ_OK;
+    if (!row_scale) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null row scales");
+    zq_status s = validate_matmul(w, m, q, y, workspace, workspace_bytes);
+    if (s != ZQ_OK) return s;
+    if ((reinterpret_cast<uintptr_t>(q) & 15u) != 0)
+        return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: codes must be 16-byte aligned");
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    uint8_t* scratch = ws + align256(m * (size_t)w->Kp) + align256(m * sizeof(float));
+    return run_codes(w, q, row_scale, m, bias, y, scratch, as_stream(stream), false);
+}
+
+zq_status zq_matmul_host(const zq_weight* w, const float* x_host, size_t m, const float* bias_host, float* y_host,
+                         void* stream) {
+    if (!w) return fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON quantization: weights are empty");
+    if (m == 0) return ZQ_OK;
+    if (!x_host || !y_host) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null input or output");
+    if (mul_overflows(m, w->K) || mul_overflows(m, w->N))
+        return fail(ZQ_ERR_OVERFLOW, "ZYRON quantization: matrix size overflow");
+    HostStaging& h = t_staging;
+    int dev = 0;
+    ZQ_CUDA(cudaGetDevice(&dev));
+    if (h.device != dev) {
+        h.~HostStaging();
+        new (&h) HostStaging();
+        h.device = dev;
+    }
+    cudaStream_t st = as_stream(stream);
+    const size_t xb = m * w->K * sizeof(float), yb = m * w->N * sizeof(float);
+    const size_t wsb = zq_matmul_workspace_bytes(w, m);
+    ZQ_CUDA(ensure(h.x, h.x_cap, xb));
+    ZQ_CUDA(ensure(h.y, h.y_cap, yb));
+    ZQ_CUDA(ensure(h.ws, h.ws_cap, wsb));
+    float* bdev = nullptr;
+    if (bias_host) {
+        ZQ_CUDA(ensure(h.b, h.b_cap, w->N * sizeof(float)));
+        bdev = static_cast<float*>(h.b);
+        ZQ_CUDA(cudaMemcpyAsync(bdev, bias_host, w->N * sizeof(float), cudaMemcpyHostToDevice, st));
+    }
+    ZQ_CUDA(cudaMemcpyAsync(h.x, x_host, xb, cudaMemcpyHostToDevice, st));
+    zq_status s = zq_matmul(w, static_cast<const float*>(h.x), m, bdev, static_cast<float*>(h.y), h.ws, h.ws_cap,
+                            stream);
+    if (s != ZQ_OK) return s;
+    ZQ_CUDA(cudaMemcpyAsync(y_host, h.y, yb, cudaMemcpyDeviceToHost, st));
+    uint32_t code = 0;
+    return zq_device_error(stream, &code);
+}
+
+zq_status zq_dequantize(const zq_weight* w, float* out, void* stream) {
+    if (!w) return fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON quantization: weights are empty");
+    if (!out) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null output");
+    ZQ_CUDA(zq::launch_dequantize(w->panel, w->type, (int)w->K, (int)w->N, w->Kp, w->scales, out, as_stream(stream)));
+    return ZQ_OK;
+}
+
+zq_status zq_device_error(void* stream, uint32_t* code) {
+    ZQ_CUDA(cudaStreamSynchronize(as_stream(stream)));
+    uint32_t* p = nullptr;
+    zq_status s = device_error_ptr(&p);
+    if (s != ZQ_OK) return s;
+    uint32_t v = 0;
+    ZQ_CUDA(cudaMemcpy(&v, p, sizeof v, cudaMemcpyDeviceToHost));
+    if (code) *code = v;
+    if (v != 0) {
+        const uint32_t zero = 0;
+        ZQ_CUDA(cudaMemcpy(p, &zero, sizeof zero, cudaMemcpyHostToDevice));
+        char buf[96];
+        std::snprintf(buf, sizeof buf, "zyron_b200: device wait timed out (code %u)", v);
+        return fail(ZQ_ERR_DEVICE_TIMEOUT, buf);
+    }
+    return ZQ_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,174 @@
+// zq_common.cuh -- shared device helpers for the B200 quantized matmul path.
+//
+// Exact-arithmetic rules (the reference computes on an x86-64 CPU in IEEE
+// fp32; see src/quantization/quantization.cpp:45-50, 202-212, 231-232):
+//   * divisions use __fdiv_rn (correctly rounded, no fast-math),
+//   * lround() is round-half-away-from-zero -> roundf(),
+//   * the epilogue float(acc) * s_row * s_col (+ bias) is three separately
+//     rounded operations -> __int2float_rn / __fmul_rn / __fadd_rn, never an
+//     FMA.
+// The library is compiled without --use_fast_math and with denormals kept.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace zq {
+
+// Weight types; numerically identical to zyron::quantization::Type
+// (include/zyron/quantization/quantization.hpp:13-16).
+enum : int { kInt8 = 1, kInt4 = 2 };
+
+// Device-side error codes written into the per-device error word when a
+// bounded wait gives up.  The host reads and clears it with
+// zq_device_error().
+enum : uint32_t {
+    kDevErrNone = 0,
+    kDevErrTimeoutProducer = 1,
+    kDevErrTimeoutMma = 2,
+    kDevErrTimeoutEpilogue = 3,
+    kDevErrTimeoutDrain = 4,
+};
+
+// ---------------------------------------------------------------------------
+// Exact scalar arithmetic shared by every kernel
+// ---------------------------------------------------------------------------
+
+// Row / column scale: absmax / limit when absmax > 0, else 1.0
+// (quantization.cpp:147-148, 209).
+__device__ __forceinline__ float zq_scale_from_absmax(float absmax, float limit) {
+    return absmax > 0.0f ? __fdiv_rn(absmax, limit) : 1.0f;
+}
+
+// quantize_value (quantization.cpp:45-50).  A NaN quotient follows the x86-64
+// lround() result (LONG_MIN), which the clamp maps to -limit.
+__device__ __forceinline__ int zq_quantize_value(float v, float scale, int limit) {
+    if (!(scale > 0.0f) || isinf(scale)) return 0;  // scale <= 0, NaN or inf
+    const float t = __fdiv_rn(v, scale);
+    if (isnan(t)) return -limit;
+    const float r = roundf(t);  // half away from zero, exact for |t| < 2^23
+    if (r >= (float)limit) return limit;
+    if (r <= (float)-limit) return -limit;
+    return (int)r;
+}
+
+// y = float(acc) * s_row * s_col, evaluated left to right (quantization.cpp:231-232).
+__device__ __forceinline__ float zq_epilogue(int32_t acc, float s_row, float s_col) {
+    return __fmul_rn(__fmul_rn(__int2float_rn(acc), s_row), s_col);
+}
+
+// + bias as the separate pass of QuantizedLinear::forward (quantized_linear.cpp:44-48).
+__device__ __forceinline__ float zq_epilogue_bias(int32_t acc, float s_row, float s_col, float b) {
+    return __fadd_rn(zq_epilogue(acc, s_row, s_col), b);
+}
+
+// Sign-extend the eight 4-bit codes of a 32-bit word into two words of four
+// int8 codes each: `even` holds the low nibbles (even linear index), `odd`
+// the high nibbles (quantization.cpp:52-57).
+__device__ __forceinline__ void zq_unpack_int4x8(uint32_t w, uint32_t& even, uint32_t& odd) {
+    const uint32_t lo = w & 0x0F0F0F0Fu;
+    const uint32_t hi = (w >> 4) & 0x0F0F0F0Fu;
+    // v | ((v & 8) * 0x1E) per byte sets the high nibble to 0xF for negatives.
+    even = lo | ((lo & 0x08080808u) * 0x1Eu);
+    odd = hi | ((hi & 0x08080808u) * 0x1Eu);
+}
+
+// ---------------------------------------------------------------------------
+// PTX wrappers (sm_100a)
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile(
+        "{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+            smem_u32(bar)),
+        "r"(bytes)
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: gives up after `limit_ns` of wall time on the GPU's global
+// timer, records `code` in *err and returns false.  No wait in this library
+// can spin forever.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t* err,
+                                                  uint32_t code, uint64_t limit_ns = 4000000000ull) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    uint32_t spins = 0;
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((++spins & 255u) == 0u) {
+            if (*(volatile uint32_t*)err != kDevErrNone) return false;  // someone else failed
+            if (global_timer_ns() - t0 > limit_ns) {
+                atomicCAS(err, kDevErrNone, code);
+                return false;
+            }
+        }
+    }
+}
+
+// TMA 2D tiled load into shared memory, completion on an mbarrier.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_t* bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
+// Programmatic dependent launch controls (no-ops when launched without the
+// attribute).
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait_primary() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// 128-bit streaming load that bypasses L1 allocation (weights are read once).
+__device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+}  // namespace zq

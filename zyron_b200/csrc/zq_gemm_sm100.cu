@@ -1,0 +1,354 @@
+// zq_gemm_sm100.cu -- prefill-sized quantized matmul on 5th-generation tensor
+// cores (tcgen05, sm_100a).
+//
+// Computes y[m][n] = float(acc) * s_row[m] * s_col[n] (+ bias[n]) with
+// acc[m][n] = sum_k q_a[m][k] * q_w[n][k] in exact int32, i.e. the dot and
+// epilogue of quantization::matmul (src/quantization/quantization.cpp:
+// 215-232) and QuantizedLinear's bias pass (quantized_linear.cpp:44-48).
+//
+// Both operands are K-major int8: the activation codes are row-major [M][Kp]
+// and the weight panel is column-major [N][Kp] (one contiguous K-run per
+// output column, exactly the reference's column-major storage).  So A and B
+// load with the same kind of 2D TMA box and feed tcgen05.mma.kind::i8 without
+// any transpose.
+//
+// Structure (one CTA per SM, persistent over 128 x BN output tiles):
+//   warp 0      TMA producer: A box 128x128 B and B box BNx128 B per k-block,
+//               128-byte swizzle, STAGES-deep ring of shared-memory buffers.
+//   warp 1      TMEM allocator + MMA issuer: one thread issues
+//               tcgen05.mma.cta_group::1.kind::i8 (M=128, N=BN, K=32) four
+//               times per k-block into an int32 TMEM accumulator and commits
+//               to the stage's "empty" barrier.
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, exact
+//               fp32 rescale (+ bias), 128-bit global stores.
+// Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap
+// the main loop of tile i+1.  Every mbarrier wait is bounded (see
+// mbar_wait_bounded): on timeout the kernel records an error code, drains its
+// own in-flight copies and MMAs, frees TMEM and returns.
+#include "zq_common.cuh"
+#include "zq_kernels.h"
+
+#include <cuda.h>
+
+namespace zq {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 128;  // bytes == int8 codes per k-block (one 128 B swizzle row)
+constexpr int kUmmaK = 32;
+constexpr int kThreads = 192;
+constexpr int kEpilogueThreads = 128;
+
+template <int BN, int STAGES>
+struct Smem {
+    static constexpr int kABytes = kBM * kBK;
+    static constexpr int kBBytes = BN * kBK;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kBarrierBytes = 8 * (2 * STAGES + 4 + 1) + 16;
+    static constexpr int kTotal = 1024 /*alignment slack*/ + STAGES * kStageBytes + kBarrierBytes;
+};
+
+__device__ __forceinline__ uint64_t make_sw128_desc(uint32_t saddr) {
+    // tcgen05 shared-memory matrix descriptor: K-major, 128-byte swizzle,
+    // 8-row core groups 1024 B apart (SBO), LBO unused for this layout.
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)(1u) << 16;            // LBO (ignored for swizzled K-major)
+    d |= (uint64_t)(1024u >> 4) << 32;    // SBO
+    d |= (uint64_t)1 << 46;               // descriptor version (sm_100)
+    d |= (uint64_t)2 << 61;               // SWIZZLE_128B
+    return d;
+}
+
+template <int BN>
+__host__ __device__ constexpr uint32_t make_idesc_i8() {
+    return (2u << 4)                 // D format: s32
+           | (1u << 7)               // A: signed 8-bit
+           | (1u << 10)              // B: signed 8-bit
+           | (0u << 15) | (0u << 16) // both K-major
+           | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void tmem_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+          "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+          "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+          "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                   int M, int N, int Kp, const float* __restrict__ row_scale,
+                   const float* __restrict__ col_scale, const float* __restrict__ bias,
+                   float* __restrict__ y, uint32_t* __restrict__ err) {
+    using S = Smem<BN, STAGES>;
+    constexpr uint32_t kTmemCols = 2 * BN;  // power of two >= 32 for BN in {64,128,256}
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* stage_base = smem;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStageBytes);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + STAGES;
+    uint64_t* tfull = bars + 2 * STAGES;
+    uint64_t* tempty = bars + 2 * STAGES + 2;
+    uint64_t* mma_done = bars + 2 * STAGES + 4;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int m_tiles = (M + kBM - 1) / kBM;
+    const int n_tiles = (N + BN - 1) / BN;
+    const int num_tiles = m_tiles * n_tiles;
+    const int k_blocks = (Kp + kBK - 1) / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], kEpilogueThreads);
+        }
+        mbar_init(mma_done, 1);
+        fence_mbar_init();
+        tma_prefetch_desc(&tmap_a);
+        tma_prefetch_desc(&tmap_b);
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tmem_fence_before();
+    __syncthreads();
+    tmem_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    // The activation codes and row scales come from the quantizer launched
+    // just before this grid (programmatic dependent launch).
+    pdl_wait_primary();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int issued[STAGES];
+            uint32_t last_phase[STAGES];
+#pragma unroll
+            for (int s = 0; s < STAGES; ++s) issued[s] = 0, last_phase[s] = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+                const int mt = t % m_tiles;
+                const int nt = t / m_tiles;
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, err, kDevErrTimeoutProducer)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* sa = stage_base + stage * S::kStageBytes;
+                    uint8_t* sb = sa + S::kABytes;
+                    mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
+                    tma_load_2d(sa, &tmap_a, &full[stage], kb * kBK, mt * kBM);
+                    tma_load_2d(sb, &tmap_b, &full[stage], kb * kBK, nt * BN);
+                    issued[stage] = 1;
+                    last_phase[stage] = phase;
+                    if (++stage == STAGES) stage = 0, phase ^= 1u;
+                }
+            }
+            // Drain: every copy this thread issued must land before the CTA
+            // can exit (on the normal path these waits return at once).
+            for (int s = 0; s < STAGES; ++s)
+                if (issued[s]) mbar_wait_bounded(&full[s], last_phase[s], err, kDevErrTimeoutDrain);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = make_idesc_i8<BN>();
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+                if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, err, kDevErrTimeoutMma)) break;
+                tmem_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    if (!mbar_wait_bounded(&full[stage], phase, err, kDevErrTimeoutMma)) {
+                        ok = false;
+                        break;
+                    }
+                    tmem_fence_after();
+                    const uint32_t sa = smem_u32(stage_base + stage * S::kStageBytes);
+                    const uint32_t sb = sa + S::kABytes;
+#pragma unroll
+                    for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+                        umma_i8(d, make_sw128_desc(sa + kk * kUmmaK), make_sw128_desc(sb + kk * kUmmaK), idesc,
+                                (kb > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    umma_commit(&empty[stage]);
+                    if (++stage == STAGES) stage = 0, phase ^= 1u;
+                }
+                if (!ok) break;
+                umma_commit(&tfull[acc]);
+                if (++acc == 2) acc = 0, acc_phase ^= 1u;
+            }
+            // All MMAs issued by this thread complete before TMEM is freed.
+            umma_commit(mma_done);
+            mbar_wait_bounded(mma_done, 0, err, kDevErrTimeoutDrain);
+        }
+    } else {
+        // Epilogue warps 2..5 own TMEM lane quarters (warp % 4) * 32.
+        const int quarter = warp & 3;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        const bool vec_ok = ((N & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15u) == 0);
+        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+            const int mt = t % m_tiles;
+            const int nt = t / m_tiles;
+            if (!mbar_wait_bounded(&tfull[acc], acc_phase, err, kDevErrTimeoutEpilogue)) break;
+            tmem_fence_after();
+            const int row = mt * kBM + quarter * 32 + lane;
+            const bool row_ok = row < M;
+            const float sr = row_ok ? __ldg(row_scale + row) : 0.0f;
+            float* yrow = y + (size_t)(row_ok ? row : 0) * N;
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(taddr + c * 32, r);
+                tmem_ld_wait();
+                const int n0 = nt * BN + c * 32;
+                if (!row_ok || n0 >= N) continue;
+                const float4* cs4 = reinterpret_cast<const float4*>(col_scale + n0);
+                if (vec_ok && n0 + 32 <= N) {
+                    const float4* b4 = bias ? reinterpret_cast<const float4*>(bias + n0) : nullptr;
+                    float4* dst = reinterpret_cast<float4*>(yrow + n0);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float4 s = __ldg(cs4 + j);
+                        float4 o;
+                        if (b4) {
+                            const float4 b = __ldg(b4 + j);
+                            o.x = zq_epilogue_bias((int32_t)r[4 * j + 0], sr, s.x, b.x);
+                            o.y = zq_epilogue_bias((int32_t)r[4 * j + 1], sr, s.y, b.y);
+                            o.z = zq_epilogue_bias((int32_t)r[4 * j + 2], sr, s.z, b.z);
+                            o.w = zq_epilogue_bias((int32_t)r[4 * j + 3], sr, s.w, b.w);
+                        } else {
+                            o.x = zq_epilogue((int32_t)r[4 * j + 0], sr, s.x);
+                            o.y = zq_epilogue((int32_t)r[4 * j + 1], sr, s.y);
+                            o.z = zq_epilogue((int32_t)r[4 * j + 2], sr, s.z);
+                            o.w = zq_epilogue((int32_t)r[4 * j + 3], sr, s.w);
+                        }
+                        dst[j] = o;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int n = n0 + j;
+                        if (n < N) {
+                            const float sc = __ldg(col_scale + n);
+                            yrow[n] = bias ? zq_epilogue_bias((int32_t)r[j], sr, sc, __ldg(bias + n))
+                                           : zq_epilogue((int32_t)r[j], sr, sc);
+                        }
+                    }
+                }
+            }
+            tmem_fence_before();
+            mbar_arrive(&tempty[acc]);
+            if (++acc == 2) acc = 0, acc_phase ^= 1u;
+        }
+    }
+
+    tmem_fence_before();
+    __syncthreads();
+    tmem_fence_after();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                     : "memory");
+    }
+}
+
+template <int BN, int STAGES>
+cudaError_t launch_gemm_t(const GemmArgs& a, cudaStream_t stream, bool pdl) {
+    using S = Smem<BN, STAGES>;
+    auto kern = gemm_i8_kernel<BN, STAGES>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
+    if (e != cudaSuccess) return e;
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int tiles = ((a.M + kBM - 1) / kBM) * ((a.N + BN - 1) / BN);
+    const int grid = tiles < sms ? tiles : sms;
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = S::kTotal;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, *a.tmap_a, *a.tmap_b, a.M, a.N, a.Kp, a.row_scale, a.col_scale, a.bias,
+                              a.y, a.err);
+}
+
+}  // namespace
+
+int gemm_block_n(int M, int N) {
+    // Wide tiles when there are enough of them to fill the GPU; narrower
+    // tiles spread small problems over more SMs.
+    const long tiles256 = (long)((M + kBM - 1) / kBM) * ((N + 255) / 256);
+    if (tiles256 >= 148) return 256;
+    const long tiles128 = (long)((M + kBM - 1) / kBM) * ((N + 127) / 128);
+    if (tiles128 >= 148) return 128;
+    return 64;
+}
+
+cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream, bool pdl) {
+    switch (a.block_n) {
+        case 256: return launch_gemm_t<256, 4>(a, stream, pdl);
+        case 128: return launch_gemm_t<128, 6>(a, stream, pdl);
+        case 64: return launch_gemm_t<64, 8>(a, stream, pdl);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace zq

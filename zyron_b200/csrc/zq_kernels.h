@@ -1,0 +1,60 @@
+// zq_kernels.h -- internal launcher interface between the C ABI (zq_api.cu)
+// and the kernels.  Not installed; the public interface is include/zq.h.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace zq {
+
+constexpr int kGemvMaxRows = 8;
+
+// Codes per column on the device, rounded up so every column starts on a
+// 16-byte boundary (INT8: 16 codes, INT4: 32 codes).
+inline int padded_k(int type, int K) { return type == 1 ? (K + 15) / 16 * 16 : (K + 31) / 32 * 32; }
+
+struct GemvArgs {
+    int type;
+    const uint8_t* panel;
+    int N;
+    int Kp;
+    const float* col_scale;
+    const int8_t* q;
+    const float* row_scale;
+    const float* bias;
+    float* y;
+    int M;
+};
+
+struct GemmArgs {
+    const CUtensorMap* tmap_a;
+    const CUtensorMap* tmap_b;
+    int M, N, Kp;
+    int block_n;
+    const float* row_scale;
+    const float* col_scale;
+    const float* bias;
+    float* y;
+    uint32_t* err;
+};
+
+cudaError_t launch_quantize_rows(const float* x, int M, int K, int Kp, int8_t* q, float* row_scale,
+                                 cudaStream_t stream);
+cudaError_t launch_repack_int4(const uint8_t* src, int K, int N, int Kp, uint8_t* dst, cudaStream_t stream);
+cudaError_t launch_unpack_panel_int4(const uint8_t* panel, int K, int N, int Kp, uint8_t* dst,
+                                     cudaStream_t stream);
+cudaError_t launch_quantize_weights(const float* w, int K, int N, int Kp, int type, uint32_t* absmax_tmp,
+                                    float* scales, uint8_t* panel, cudaStream_t stream);
+cudaError_t launch_dequantize(const uint8_t* panel, int type, int K, int N, int Kp, const float* scales,
+                              float* out, cudaStream_t stream);
+cudaError_t launch_expand_int4(const uint8_t* panel4, int N, int Kp, int8_t* panel8, cudaStream_t stream);
+
+size_t gemv_smem_bytes(int M, int Kp);
+cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl);
+
+int gemm_block_n(int M, int N);
+cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream, bool pdl);
+
+}  // namespace zq

@@ -1,0 +1,344 @@
+// zq_quant.cu -- activation quantizer, weight layout kernels and dequantize.
+//
+// Device weight layout ("panel" layout).  The reference stores a K x N weight
+// column-major, element (row k, col n) at linear index n*K + k, INT4 as two
+// codes per byte with the low nibble holding the even linear index
+// (src/quantization/quantization.cpp:52-67, 155).  On the device every column
+// starts on a 16-byte boundary and is zero-padded to Kp codes:
+//   INT8: codes[n * Kp + k]                       Kp = roundup(K, 16)
+//   INT4: byte[n * Kp/2 + k/2], low nibble = even k   Kp = roundup(K, 32)
+// Zero codes contribute nothing to an integer dot product, so padding never
+// changes a result; it gives every TMA tensor map 16-byte strides and every
+// GEMV lane aligned 128-bit loads.
+#include "zq_common.cuh"
+#include "zq_kernels.h"
+
+#include <cstdint>
+
+namespace zq {
+
+// ---------------------------------------------------------------------------
+// Per-row dynamic activation quantizer (quantization.cpp:202-212).
+// One warp per row: pass 1 reduces |x| with fmaxf (NaN skipped, like
+// std::max), pass 2 writes codes; the [K, Kp) tail is zero-filled.
+// ---------------------------------------------------------------------------
+template <bool kVec>
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restrict__ x, int M, int K,
+                                                            int Kp, int8_t* __restrict__ q,
+                                                            float* __restrict__ row_scale) {
+    pdl_launch_dependents();
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= M) return;
+    const float* xr = x + (size_t)warp * K;
+    int8_t* qr = q + (size_t)warp * Kp;
+
+    float m = 0.0f;
+    if (kVec) {
+        const float4* x4 = reinterpret_cast<const float4*>(xr);
+        for (int i = lane; i < (K >> 2); i += 32) {
+            const float4 v = __ldg(x4 + i);
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+    } else {
+        for (int i = lane; i < K; i += 32) m = fmaxf(m, fabsf(__ldg(xr + i)));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float s = zq_scale_from_absmax(m, 127.0f);
+    if (lane == 0) row_scale[warp] = s;
+
+    if (kVec) {
+        const float4* x4 = reinterpret_cast<const float4*>(xr);
+        uint32_t* q4 = reinterpret_cast<uint32_t*>(qr);
+        for (int i = lane; i < (K >> 2); i += 32) {
+            const float4 v = __ldg(x4 + i);
+            const uint32_t b0 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value(v.x, s, 127);
+            const uint32_t b1 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value(v.y, s, 127);
+            const uint32_t b2 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value(v.z, s, 127);
+            const uint32_t b3 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value(v.w, s, 127);
+            q4[i] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+        }
+        for (int i = (K >> 2) + lane; i < (Kp >> 2); i += 32) q4[i] = 0u;
+    } else {
+        for (int i = lane; i < K; i += 32) qr[i] = (int8_t)zq_quantize_value(__ldg(xr + i), s, 127);
+        for (int i = K + lane; i < Kp; i += 32) qr[i] = 0;
+    }
+}
+
+cudaError_t launch_quantize_rows(const float* x, int M, int K, int Kp, int8_t* q, float* row_scale,
+                                 cudaStream_t stream) {
+    if (M <= 0) return cudaSuccess;
+    const int rows_per_block = 8;
+    const dim3 grid((M + rows_per_block - 1) / rows_per_block);
+    const bool vec = (K % 4 == 0) && (Kp % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(q) & 3u) == 0);
+    if (vec)
+        quantize_rows_kernel<true><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale);
+    else
+        quantize_rows_kernel<false><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// INT4 repack: reference nibble stream (column c at nibble c*K) -> panel
+// layout.  Needed only when K is odd (columns straddle bytes); even K is a
+// pitched copy.  One thread per output byte.
+// ---------------------------------------------------------------------------
+__global__ void repack_int4_kernel(const uint8_t* __restrict__ src, int K, int N, int Kp,
+                                   uint8_t* __restrict__ dst) {
+    const int bytes_per_col = Kp >> 1;
+    const size_t total = (size_t)N * bytes_per_col;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const size_t c = i / bytes_per_col;
+        const int j = (int)(i - c * bytes_per_col);
+        uint32_t out = 0;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int k = 2 * j + h;
+            if (k < K) {
+                const size_t lin = c * (size_t)K + k;
+                const uint8_t b = src[lin >> 1];
+                const uint32_t nib = (lin & 1u) ? (b >> 4) : (b & 0x0Fu);
+                out |= nib << (4 * h);
+            }
+        }
+        dst[i] = (uint8_t)out;
+    }
+}
+
+cudaError_t launch_repack_int4(const uint8_t* src, int K, int N, int Kp, uint8_t* dst, cudaStream_t stream) {
+    const size_t total = (size_t)N * (Kp >> 1);
+    const int threads = 256;
+    const int blocks = (int)((total + threads - 1) / threads < 148 * 16 ? (total + threads - 1) / threads
+                                                                         : 148 * 16);
+    repack_int4_kernel<<<blocks, threads, 0, stream>>>(src, K, N, Kp, dst);
+    return cudaGetLastError();
+}
+
+// Panel layout -> reference payload (for save / download).  INT4 only needs
+// a kernel when K is odd; one thread per output byte of the reference stream.
+__global__ void unpack_panel_int4_kernel(const uint8_t* __restrict__ panel, int K, int N, int Kp,
+                                         uint8_t* __restrict__ dst) {
+    const size_t nibbles = (size_t)K * N;
+    const size_t total = (nibbles + 1) / 2;
+    const int bpc = Kp >> 1;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+         i += (size_t)gridDim.x * blockDim.x) {
+        uint32_t out = 0;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const size_t lin = 2 * i + h;
+            if (lin < nibbles) {
+                const size_t c = lin / K;
+                const int k = (int)(lin - c * K);
+                const uint8_t b = panel[c * bpc + (k >> 1)];
+                out |= (uint32_t)((k & 1) ? (b >> 4) : (b & 0x0Fu)) << (4 * h);
+            }
+        }
+        dst[i] = (uint8_t)out;
+    }
+}
+
+cudaError_t launch_unpack_panel_int4(const uint8_t* panel, int K, int N, int Kp, uint8_t* dst,
+                                     cudaStream_t stream) {
+    const size_t total = ((size_t)K * N + 1) / 2;
+    const int threads = 256;
+    const size_t want = (total + threads - 1) / threads;
+    const int blocks = (int)(want < 148 * 16 ? want : 148 * 16);
+    unpack_panel_int4_kernel<<<blocks > 0 ? blocks : 1, threads, 0, stream>>>(panel, K, N, Kp, dst);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Weight quantization on the device (quantize(): quantization.cpp:121-162).
+// w is fp32 row-major [K][N].
+//   pass 1: per-column absmax; threads own columns (coalesced along N), the
+//           grid's y dimension splits K and partial maxima meet in an
+//           atomicMax on the non-negative float bit pattern.
+//   pass 2: scale = absmax / limit, codes written transposed into the panel
+//           layout through a 32 x 32 shared-memory tile.
+// ---------------------------------------------------------------------------
+__global__ void column_absmax_kernel(const float* __restrict__ w, int K, int N, int rows_per_block,
+                                     uint32_t* __restrict__ absmax_bits) {
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= N) return;
+    const int k0 = blockIdx.y * rows_per_block;
+    const int k1 = min(K, k0 + rows_per_block);
+    float m = 0.0f;
+    for (int k = k0; k < k1; ++k) m = fmaxf(m, fabsf(__ldg(w + (size_t)k * N + n)));
+    atomicMax(absmax_bits + n, __float_as_uint(m));
+}
+
+__global__ void column_scale_kernel(const uint32_t* __restrict__ absmax_bits, int N, float limit,
+                                    float* __restrict__ scales) {
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n < N) scales[n] = zq_scale_from_absmax(__uint_as_float(absmax_bits[n]), limit);
+}
+
+template <int kType>
+__global__ void __launch_bounds__(256) quantize_panel_kernel(const float* __restrict__ w, int K, int N,
+                                                             int Kp, const float* __restrict__ scales,
+                                                             uint8_t* __restrict__ panel) {
+    // tile: 32 columns (n) x 64 rows (k); threads (32, 8)
+    __shared__ int8_t tile[32][64 + 4];
+    const int n0 = blockIdx.x * 32;
+    const int k0 = blockIdx.y * 64;
+    const int tx = threadIdx.x, ty = threadIdx.y;
+    const int limit = kType == kInt8 ? 127 : 7;
+    const int n = n0 + tx;
+    const float s = n < N ? scales[n] : 1.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int k = k0 + ty + 8 * j;
+        int8_t v = 0;
+        if (n < N && k < K) v = (int8_t)zq_quantize_value(__ldg(w + (size_t)k * N + n), s, limit);
+        tile[tx][ty + 8 * j] = v;
+    }
+    __syncthreads();
+    if (kType == kInt8) {
+        // each warp row writes 64 consecutive k codes of one column as 32 x 2 bytes
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int c = ty + 8 * j;
+            const int nn = n0 + c;
+            const int k = k0 + 2 * tx;
+            if (nn < N && k < Kp) {
+                const uint16_t pair = (uint16_t)(uint8_t)tile[c][2 * tx] |
+                                      ((uint16_t)(uint8_t)tile[c][2 * tx + 1] << 8);
+                *reinterpret_cast<uint16_t*>(panel + (size_t)nn * Kp + k) = pair;
+            }
+        }
+    } else {
+        const int bpc = Kp >> 1;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int c = ty + 8 * j;
+            const int nn = n0 + c;
+            const int k = k0 + 2 * tx;  // byte k/2 holds codes k (low) and k+1 (high)
+            if (nn < N && k < Kp) {
+                const uint8_t b = (uint8_t)(((uint8_t)tile[c][2 * tx] & 0x0Fu) |
+                                            (((uint8_t)tile[c][2 * tx + 1] & 0x0Fu) << 4));
+                panel[(size_t)nn * bpc + (k >> 1)] = b;
+            }
+        }
+    }
+}
+
+cudaError_t launch_quantize_weights(const float* w, int K, int N, int Kp, int type, uint32_t* absmax_tmp,
+                                    float* scales, uint8_t* panel, cudaStream_t stream) {
+    cudaError_t e = cudaMemsetAsync(absmax_tmp, 0, sizeof(uint32_t) * (size_t)N, stream);
+    if (e != cudaSuccess) return e;
+    const int rows_per_block = 256;
+    dim3 g1((N + 127) / 128, (K + rows_per_block - 1) / rows_per_block);
+    column_absmax_kernel<<<g1, 128, 0, stream>>>(w, K, N, rows_per_block, absmax_tmp);
+    column_scale_kernel<<<(N + 255) / 256, 256, 0, stream>>>(absmax_tmp, N, type == kInt8 ? 127.0f : 7.0f,
+                                                            scales);
+    dim3 g2((N + 31) / 32, (Kp + 63) / 64);
+    if (type == kInt8)
+        quantize_panel_kernel<kInt8><<<g2, dim3(32, 8), 0, stream>>>(w, K, N, Kp, scales, panel);
+    else
+        quantize_panel_kernel<kInt4><<<g2, dim3(32, 8), 0, stream>>>(w, K, N, Kp, scales, panel);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// dequantize() (quantization.cpp:164-175): out[k][n] = float(code(n,k)) * s_n,
+// fp32 row-major [K][N].  32 x 32 tile transpose; reads the panel along k,
+// writes out along n.
+// ---------------------------------------------------------------------------
+template <int kType>
+__global__ void __launch_bounds__(256) dequantize_kernel(const uint8_t* __restrict__ panel, int K, int N,
+                                                         int Kp, const float* __restrict__ scales,
+                                                         float* __restrict__ out) {
+    __shared__ int8_t tile[32][64 + 4];  // [n][k]
+    const int n0 = blockIdx.x * 32;
+    const int k0 = blockIdx.y * 64;
+    const int tx = threadIdx.x, ty = threadIdx.y;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int c = ty + 8 * j;
+        const int nn = n0 + c;
+        const int k = k0 + 2 * tx;
+        int8_t a = 0, b = 0;
+        if (nn < N && k < Kp) {
+            if (kType == kInt8) {
+                const uint16_t pair = *reinterpret_cast<const uint16_t*>(panel + (size_t)nn * Kp + k);
+                a = (int8_t)(pair & 0xFF);
+                b = (int8_t)(pair >> 8);
+            } else {
+                const uint8_t byte = panel[(size_t)nn * (Kp >> 1) + (k >> 1)];
+                const int lo = byte & 0x0F, hi = byte >> 4;
+                a = (int8_t)(lo < 8 ? lo : lo - 16);
+                b = (int8_t)(hi < 8 ? hi : hi - 16);
+            }
+        }
+        tile[c][2 * tx] = a;
+        tile[c][2 * tx + 1] = b;
+    }
+    __syncthreads();
+    const int n = n0 + tx;
+    if (n >= N) return;
+    const float s = scales[n];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int k = k0 + ty + 8 * j;
+        if (k < K) out[(size_t)k * N + n] = __fmul_rn((float)tile[tx][ty + 8 * j], s);
+    }
+}
+
+cudaError_t launch_dequantize(const uint8_t* panel, int type, int K, int N, int Kp, const float* scales,
+                              float* out, cudaStream_t stream) {
+    dim3 g((N + 31) / 32, (K + 63) / 64);
+    if (type == kInt8)
+        dequantize_kernel<kInt8><<<g, dim3(32, 8), 0, stream>>>(panel, K, N, Kp, scales, out);
+    else
+        dequantize_kernel<kInt4><<<g, dim3(32, 8), 0, stream>>>(panel, K, N, Kp, scales, out);
+    return cudaGetLastError();
+}
+
+}  // namespace zq
+
+namespace zq {
+
+// ---------------------------------------------------------------------------
+// INT4 panel -> INT8 panel with the same Kp (two codes per input byte), used
+// by the prefill GEMM for INT4 weights.  Each thread expands 16 packed bytes
+// into 32 codes with the shared nibble unpack.
+// ---------------------------------------------------------------------------
+__global__ void expand_int4_kernel(const uint4* __restrict__ src, size_t chunks, uint4* __restrict__ dst) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < chunks;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const uint4 w = src[i];
+        uint32_t e[4], o[4];
+        zq_unpack_int4x8(w.x, e[0], o[0]);
+        zq_unpack_int4x8(w.y, e[1], o[1]);
+        zq_unpack_int4x8(w.z, e[2], o[2]);
+        zq_unpack_int4x8(w.w, e[3], o[3]);
+        // interleave even/odd codes back into linear k order
+        uint4 a, b;
+        a.x = __byte_perm(e[0], o[0], 0x5140);
+        a.y = __byte_perm(e[0], o[0], 0x7362);
+        a.z = __byte_perm(e[1], o[1], 0x5140);
+        a.w = __byte_perm(e[1], o[1], 0x7362);
+        b.x = __byte_perm(e[2], o[2], 0x5140);
+        b.y = __byte_perm(e[2], o[2], 0x7362);
+        b.z = __byte_perm(e[3], o[3], 0x5140);
+        b.w = __byte_perm(e[3], o[3], 0x7362);
+        dst[2 * i] = a;
+        dst[2 * i + 1] = b;
+    }
+}
+
+cudaError_t launch_expand_int4(const uint8_t* panel4, int N, int Kp, int8_t* panel8, cudaStream_t stream) {
+    const size_t chunks = (size_t)N * (size_t)(Kp >> 1) / 16;
+    const int threads = 256;
+    const size_t want = (chunks + threads - 1) / threads;
+    const int blocks = (int)(want < 148 * 32 ? want : 148 * 32);
+    expand_int4_kernel<<<blocks > 0 ? blocks : 1, threads, 0, stream>>>(
+        reinterpret_cast<const uint4*>(panel4), chunks, reinterpret_cast<uint4*>(panel8));
+    return cudaGetLastError();
+}
+
+}  // namespace zq

@@ -209,7 +209,7 @@ def run_ours(args, rank, world, local_rank):
     del w_f32
     torch.cuda.empty_cache()
     y = torch.empty((M, n_loc), dtype=torch.float32, device=dev)
-    y_full = torch.empty((world, M, n_loc), dtype=torch.float32, device=dev) if world > 1 else None
+    y_full = torch.empty((world * M, n_loc), dtype=torch.float32, device=dev) if world > 1 else None
     ws_bytes = L.zq_matmul_workspace_bytes(W.handle, M)
     ws = torch.empty(ws_bytes + 256, dtype=torch.uint8, device=dev)
     ws_ptr = (ws.data_ptr() + 255) & ~255

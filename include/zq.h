@@ -77,6 +77,11 @@ zq_status zq_weight_create(int type, size_t rows, size_t cols, const float* scal
 zq_status zq_weight_quantize(const float* w_dev, size_t rows, size_t cols, int type, void* stream,
                              zq_weight** out);
 
+/* quantize() from host memory: w_host is fp32 row-major [rows][cols]; it is
+ * copied to the current device and quantized there.  Synchronous. */
+zq_status zq_weight_quantize_host(const float* w_host, size_t rows, size_t cols, int type, void* stream,
+                                  zq_weight** out);
+
 /* Parse one .zyq record from memory and upload it (QuantizedMatrix::load(istream),
  * quantization.cpp:269-311: same checks, same order, same messages).  On
  * success *consumed is the number of bytes of the record. */
@@ -144,6 +149,10 @@ zq_status zq_matmul_host(const zq_weight* w, const float* x_host, size_t m, cons
 /* QuantizedMatrix::dequantize() (quantization.cpp:164-175): out is fp32
  * row-major [rows][cols] on the device. */
 zq_status zq_dequantize(const zq_weight* w, float* out, void* stream);
+
+/* dequantize() into host memory: out_host is fp32 row-major [rows][cols].
+ * Synchronous. */
+zq_status zq_dequantize_host(const zq_weight* w, float* out_host, void* stream);
 
 /* Synchronise `stream`, then read and clear the current device's error word
  * (0 = none; otherwise which bounded wait gave up).  Returns

@@ -83,6 +83,8 @@ SIGNATURES = {
     "zq_abi_version": (C.c_int, []),
     "zq_weight_create": (st, [C.c_int, sz, sz, vp, vp, sz, vp, C.POINTER(vp)]),
     "zq_weight_quantize": (st, [vp, sz, sz, C.c_int, vp, C.POINTER(vp)]),
+    "zq_weight_quantize_host": (st, [vp, sz, sz, C.c_int, vp, C.POINTER(vp)]),
+    "zq_dequantize_host": (st, [vp, vp, vp]),
     "zq_weight_load_zyq": (st, [vp, sz, C.POINTER(sz), vp, C.POINTER(vp)]),
     "zq_weight_save_zyq": (st, [vp, vp, sz, C.POINTER(sz), vp]),
     "zq_weight_info": (st, [vp, C.POINTER(C.c_int), C.POINTER(sz), C.POINTER(sz), C.POINTER(sz),

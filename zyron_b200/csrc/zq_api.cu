@@ -15,6 +15,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <limits>
 #include <mutex>
@@ -209,6 +210,16 @@ zq_status download_payload(const zq_weight* w, void* payload, cudaStream_t st) {
     return ZQ_OK;
 }
 
+// GEMM tile-order group size (M-tiles per group); ZQ_GEMM_GROUP_M overrides
+// the default for tuning sweeps.
+int gemm_group_m() {
+    static const int g = [] {
+        const char* e = std::getenv("ZQ_GEMM_GROUP_M");
+        return e ? std::atoi(e) : 16;
+    }();
+    return g;
+}
+
 int tile_index(int block_n) { return block_n == 256 ? 2 : (block_n == 128 ? 1 : 0); }
 
 // Per-thread device buffers of zq_matmul_host.
@@ -303,6 +314,28 @@ zq_status zq_weight_quantize(const float* w_dev, size_t rows, size_t cols, int t
     }
     *out = w;
     return ZQ_OK;
+}
+
+zq_status zq_weight_quantize_host(const float* w_host, size_t rows, size_t cols, int type, void* stream,
+                                  zq_weight** out) {
+    if (!out) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null output handle");
+    *out = nullptr;
+    if (type != ZQ_TYPE_INT8 && type != ZQ_TYPE_INT4)
+        return fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON quantization: unsupported type");
+    zq_status s = check_dims(rows, cols);
+    if (s != ZQ_OK) return s;
+    if (!w_host) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null weights");
+    float* tmp = nullptr;
+    cudaStream_t st = as_stream(stream);
+    ZQ_CUDA(cudaMalloc(&tmp, rows * cols * sizeof(float)));
+    cudaError_t e = cudaMemcpyAsync(tmp, w_host, rows * cols * sizeof(float), cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) {
+        cudaFree(tmp);
+        return cuda_fail(e, "weight copy");
+    }
+    s = zq_weight_quantize(tmp, rows, cols, type, stream, out);
+    cudaFree(tmp);
+    return s;
 }
 
 zq_status zq_weight_load_zyq(const void* bytes, size_t len, size_t* consumed, void* stream, zq_weight** out) {
@@ -516,7 +549,7 @@ zq_status run_codes(const zq_weight* w, const int8_t* codes, const float* rs, si
         tmap_b = &tmap_b_local;
         pdl = true;  // the GEMM follows the expand kernel directly
     }
-    zq::GemmArgs g{&tmap_a, tmap_b, M, N, Kp, bn, rs, w->scales, bias, y, err};
+    zq::GemmArgs g{&tmap_a, tmap_b, M, N, Kp, bn, rs, w->scales, bias, y, err, gemm_group_m()};
     ZQ_CUDA(zq::launch_gemm(g, st, pdl));
     return ZQ_OK;
 }
@@ -594,6 +627,21 @@ zq_status zq_dequantize(const zq_weight* w, float* out, void* stream) {
     if (!w) return fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON quantization: weights are empty");
     if (!out) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null output");
     ZQ_CUDA(zq::launch_dequantize(w->panel, w->type, (int)w->K, (int)w->N, w->Kp, w->scales, out, as_stream(stream)));
+    return ZQ_OK;
+}
+
+zq_status zq_dequantize_host(const zq_weight* w, float* out_host, void* stream) {
+    if (!w) return fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON quantization: weights are empty");
+    if (!out_host) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null output");
+    cudaStream_t st = as_stream(stream);
+    const size_t bytes = w->K * w->N * sizeof(float);
+    float* tmp = nullptr;
+    ZQ_CUDA(cudaMalloc(&tmp, bytes));
+    cudaError_t e = zq::launch_dequantize(w->panel, w->type, (int)w->K, (int)w->N, w->Kp, w->scales, tmp, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out_host, tmp, bytes, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    cudaFree(tmp);
+    if (e != cudaSuccess) return cuda_fail(e, "dequantize to host");
     return ZQ_OK;
 }
 

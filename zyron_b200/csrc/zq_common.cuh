@@ -52,14 +52,37 @@ __device__ __forceinline__ int zq_quantize_value(float v, float scale, int limit
     return (int)r;
 }
 
+// NaN bit patterns of the reference's x86-64 SSE arithmetic: an invalid
+// operation (0 * inf, inf - inf) yields the "default NaN" 0xFFC00000, and a
+// NaN operand propagates its own payload, quieted (the first operand's when
+// both are NaN).  The GPU's canonical NaN differs, so every place where the
+// reference can produce a NaN restates this rule to stay bit-identical.
+constexpr uint32_t kX86DefaultNaN = 0xFFC00000u;
+
+__device__ __forceinline__ float x86_mul(float a, float b) {
+    const float r = __fmul_rn(a, b);
+    if (!isnan(r)) return r;
+    if (isnan(a)) return __uint_as_float(__float_as_uint(a) | 0x00400000u);
+    if (isnan(b)) return __uint_as_float(__float_as_uint(b) | 0x00400000u);
+    return __uint_as_float(kX86DefaultNaN);
+}
+
+__device__ __forceinline__ float x86_add(float a, float b) {
+    const float r = __fadd_rn(a, b);
+    if (!isnan(r)) return r;
+    if (isnan(a)) return __uint_as_float(__float_as_uint(a) | 0x00400000u);
+    if (isnan(b)) return __uint_as_float(__float_as_uint(b) | 0x00400000u);
+    return __uint_as_float(kX86DefaultNaN);
+}
+
 // y = float(acc) * s_row * s_col, evaluated left to right (quantization.cpp:231-232).
 __device__ __forceinline__ float zq_epilogue(int32_t acc, float s_row, float s_col) {
-    return __fmul_rn(__fmul_rn(__int2float_rn(acc), s_row), s_col);
+    return x86_mul(x86_mul(__int2float_rn(acc), s_row), s_col);
 }
 
 // + bias as the separate pass of QuantizedLinear::forward (quantized_linear.cpp:44-48).
 __device__ __forceinline__ float zq_epilogue_bias(int32_t acc, float s_row, float s_col, float b) {
-    return __fadd_rn(zq_epilogue(acc, s_row, s_col), b);
+    return x86_add(zq_epilogue(acc, s_row, s_col), b);
 }
 
 // Sign-extend the eight 4-bit codes of a 32-bit word into two words of four

@@ -108,12 +108,25 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Tile order: groups of `group_m` M-tiles; inside a group the M-tile index
+// runs fastest, then the N-tile.  The CTAs running at the same time then
+// share a few A panels (activation rows) and B panels (weight columns) in L2.
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int group_m, int& mt, int& nt) {
+    const int per_group = group_m * n_tiles;
+    const int g = t / per_group;
+    const int first_m = g * group_m;
+    const int gm = min(m_tiles - first_m, group_m);
+    const int r = t - g * per_group;
+    mt = first_m + r % gm;
+    nt = r / gm;
+}
+
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    int M, int N, int Kp, const float* __restrict__ row_scale,
                    const float* __restrict__ col_scale, const float* __restrict__ bias,
-                   float* __restrict__ y, uint32_t* __restrict__ err) {
+                   float* __restrict__ y, uint32_t* __restrict__ err, int group_m) {
     using S = Smem<BN, STAGES>;
     constexpr uint32_t kTmemCols = 2 * BN;  // power of two >= 32 for BN in {64,128,256}
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -174,8 +187,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int s = 0; s < STAGES; ++s) issued[s] = 0, last_phase[s] = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-                const int mt = t % m_tiles;
-                const int nt = t / m_tiles;
+                int mt, nt;
+                tile_coords(t, m_tiles, n_tiles, group_m, mt, nt);
                 for (int kb = 0; kb < k_blocks; ++kb) {
                     if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, err, kDevErrTimeoutProducer)) {
                         ok = false;
@@ -239,8 +252,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t acc_phase = 0;
         const bool vec_ok = ((N & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15u) == 0);
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-            const int mt = t % m_tiles;
-            const int nt = t / m_tiles;
+            int mt, nt;
+            tile_coords(t, m_tiles, n_tiles, group_m, mt, nt);
             if (!mbar_wait_bounded(&tfull[acc], acc_phase, err, kDevErrTimeoutEpilogue)) break;
             tmem_fence_after();
             const int row = mt * kBM + quarter * 32 + lane;
@@ -326,8 +339,11 @@ cudaError_t launch_gemm_t(const GemmArgs& a, cudaStream_t stream, bool pdl) {
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    const int m_tiles = (a.M + kBM - 1) / kBM;
+    int group_m = a.group_m > 0 ? a.group_m : m_tiles;
+    if (group_m > m_tiles) group_m = m_tiles;
     return cudaLaunchKernelEx(&cfg, kern, *a.tmap_a, *a.tmap_b, a.M, a.N, a.Kp, a.row_scale, a.col_scale, a.bias,
-                              a.y, a.err);
+                              a.y, a.err, group_m);
 }
 
 }  // namespace

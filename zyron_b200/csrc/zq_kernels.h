@@ -38,6 +38,7 @@ struct GemmArgs {
     const float* bias;
     float* y;
     uint32_t* err;
+    int group_m;  // tile-order group size in M-tiles (0 = all M-tiles)
 };
 
 cudaError_t launch_quantize_rows(const float* x, int M, int K, int Kp, int8_t* q, float* row_scale,

@@ -284,7 +284,7 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const uint8_t* __restri
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const int k = k0 + ty + 8 * j;
-        if (k < K) out[(size_t)k * N + n] = __fmul_rn((float)tile[tx][ty + 8 * j], s);
+        if (k < K) out[(size_t)k * N + n] = x86_mul((float)tile[tx][ty + 8 * j], s);
     }
 }
 

@@ -215,7 +215,7 @@ zq_status download_payload(const zq_weight* w, void* payload, cudaStream_t st) {
 int gemm_group_m() {
     static const int g = [] {
         const char* e = std::getenv("ZQ_GEMM_GROUP_M");
-        return e ? std::atoi(e) : 16;
+        return e ? std::atoi(e) : 32;
     }();
     return g;
 }
@@ -554,23 +554,39 @@ zq_status run_codes(const zq_weight* w, const int8_t* codes, const float* rs, si
     return ZQ_OK;
 }
 
-}  // namespace
-
-extern "C" {
-
-zq_status zq_matmul(const zq_weight* w, const float* x, size_t m, const float* bias, float* y, void* workspace,
-                    size_t workspace_bytes, void* stream) {
-    if (!w) return fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON quantization: weights are empty");
-    if (m == 0) return ZQ_OK;
-    zq_status s = validate_matmul(w, m, x, y, workspace, workspace_bytes);
-    if (s != ZQ_OK) return s;
-    cudaStream_t st = as_stream(stream);
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
+// Quantizer + dot/epilogue with all scratch in `ws` (already validated:
+// 256-byte aligned, zq_matmul_workspace_bytes(w, m) bytes).
+zq_status matmul_in_workspace(const zq_weight* w, const float* x, size_t m, const float* bias, float* y,
+                              uint8_t* ws, cudaStream_t st) {
     int8_t* codes = reinterpret_cast<int8_t*>(ws);
     float* rs = reinterpret_cast<float*>(ws + align256(m * (size_t)w->Kp));
     uint8_t* scratch = ws + align256(m * (size_t)w->Kp) + align256(m * sizeof(float));
     ZQ_CUDA(zq::launch_quantize_rows(x, (int)m, (int)w->K, w->Kp, codes, rs, st));
     return run_codes(w, codes, rs, m, bias, y, scratch, st, true);
+}
+
+}  // namespace
+
+namespace zq {
+
+zq_status matmul_with_scratch(const zq_weight* w, const float* x, size_t m, const float* bias, float* y,
+                              void* scratch, size_t scratch_bytes, void* stream) {
+    if (!w) return fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON quantization: weights are empty");
+    if (m == 0) return ZQ_OK;
+    zq_status s = validate_matmul(w, m, x, y, scratch, scratch_bytes);
+    if (s != ZQ_OK) return s;
+    return matmul_in_workspace(w, x, m, bias, y, static_cast<uint8_t*>(scratch), as_stream(stream));
+}
+
+zq_status set_error(zq_status s, const char* msg) { return fail(s, msg); }
+
+}  // namespace zq
+
+extern "C" {
+
+zq_status zq_matmul(const zq_weight* w, const float* x, size_t m, const float* bias, float* y, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+    return zq::matmul_with_scratch(w, x, m, bias, y, workspace, workspace_bytes, stream);
 }
 
 zq_status zq_matmul_codes(const zq_weight* w, const int8_t* q, const float* row_scale, size_t m, const float* bias,

@@ -7,6 +7,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "zq.h"
+
 namespace zq {
 
 constexpr int kGemvMaxRows = 8;
@@ -56,6 +58,13 @@ size_t gemv_smem_bytes(int M, int Kp);
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl);
 
 int gemm_block_n(int M, int N);
+
+// zq_matmul with caller-supplied scratch (validated here: 256-byte aligned and
+// at least zq_matmul_workspace_bytes(w, m) bytes).  Defined in zq_api.cu.
+zq_status matmul_with_scratch(const zq_weight* w, const float* x, size_t m, const float* bias, float* y,
+                              void* scratch, size_t scratch_bytes, void* stream);
+// Records `msg` as the calling thread's last error and returns `s`.
+zq_status set_error(zq_status s, const char* msg);
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream, bool pdl);
 
 }  // namespace zq

@@ -66,9 +66,80 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restr
     }
 }
 
+// Register-resident variant: a row is held by kWarpsPerRow warps, each lane
+// keeping up to kVec float4 in registers, so x is read from memory exactly
+// once (absmax and codes come from the same registers).  Used when K is a
+// multiple of 4 and K/4 <= 32 * kWarpsPerRow * kVec.
+template <int kWarpsPerRow, int kVec>
+__global__ void __launch_bounds__(256) quantize_rows_reg_kernel(const float* __restrict__ x, int M, int K, int Kp,
+                                                                int8_t* __restrict__ q,
+                                                                float* __restrict__ row_scale) {
+    pdl_launch_dependents();
+    constexpr int kRowsPerBlock = 8 / kWarpsPerRow;
+    constexpr int kT = 32 * kWarpsPerRow;
+    __shared__ float part[8];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * kRowsPerBlock + warp / kWarpsPerRow;
+    const int t = (warp % kWarpsPerRow) * 32 + lane;
+    const int k4 = K >> 2;
+    float4 v[kVec];
+    float m = 0.0f;
+    if (row < M) {
+        const float4* x4 = reinterpret_cast<const float4*>(x + (size_t)row * K);
+#pragma unroll
+        for (int i = 0; i < kVec; ++i) {
+            const int idx = t + i * kT;
+            v[i] = idx < k4 ? __ldg(x4 + idx) : make_float4(0.f, 0.f, 0.f, 0.f);
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (kWarpsPerRow > 1) {
+        if (lane == 0) part[warp] = m;
+        __syncthreads();
+        const int first = (warp / kWarpsPerRow) * kWarpsPerRow;
+#pragma unroll
+        for (int w = 0; w < kWarpsPerRow; ++w) m = fmaxf(m, part[first + w]);
+    }
+    if (row >= M) return;
+    const float s = zq_scale_from_absmax(m, 127.0f);
+    if (t == 0) row_scale[row] = s;
+    uint32_t* q4 = reinterpret_cast<uint32_t*>(q + (size_t)row * Kp);
+#pragma unroll
+    for (int i = 0; i < kVec; ++i) {
+        const int idx = t + i * kT;
+        if (idx < k4) {
+            const uint32_t b0 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value(v[i].x, s, 127);
+            const uint32_t b1 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value(v[i].y, s, 127);
+            const uint32_t b2 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value(v[i].z, s, 127);
+            const uint32_t b3 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value(v[i].w, s, 127);
+            q4[idx] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+        }
+    }
+    for (int i = k4 + t; i < (Kp >> 2); i += kT) q4[i] = 0u;
+}
+
 cudaError_t launch_quantize_rows(const float* x, int M, int K, int Kp, int8_t* q, float* row_scale,
                                  cudaStream_t stream) {
     if (M <= 0) return cudaSuccess;
+    const bool aligned = (K % 4 == 0) && (Kp % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) &&
+                         ((reinterpret_cast<uintptr_t>(q) & 3u) == 0);
+    const int k4 = K / 4;
+    if (aligned && k4 <= 2048) {
+        int wpr = 1;
+        while (wpr < 8 && k4 > 32 * wpr * 8) wpr *= 2;
+        const int rows_per_block = 8 / wpr;
+        const dim3 grid((M + rows_per_block - 1) / rows_per_block);
+        switch (wpr) {
+            case 1: quantize_rows_reg_kernel<1, 8><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale); break;
+            case 2: quantize_rows_reg_kernel<2, 8><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale); break;
+            case 4: quantize_rows_reg_kernel<4, 8><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale); break;
+            default: quantize_rows_reg_kernel<8, 8><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale); break;
+        }
+        return cudaGetLastError();
+    }
     const int rows_per_block = 8;
     const dim3 grid((M + rows_per_block - 1) / rows_per_block);
     const bool vec = (K % 4 == 0) && (Kp % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) &&

@@ -140,6 +140,21 @@ zq_status zq_matmul(const zq_weight* w, const float* x, size_t m, const float* b
 zq_status zq_matmul_codes(const zq_weight* w, const int8_t* q, const float* row_scale, size_t m,
                           const float* bias, float* y, void* workspace, size_t workspace_bytes, void* stream);
 
+/* zq_matmul for callers that cannot allocate device memory or pass a
+ * workspace (plugin hosts that hand over only input and output buffers,
+ * pool allocators that forbid raw cudaMalloc, loops that must not
+ * synchronise on an allocation).  No counterpart in the reference: its
+ * matmul runs on the host.  Scratch comes from a fixed array compiled into
+ * the library (ZQ_NOALLOC_SCRATCH_BYTES per device, held until exit); calls
+ * needing more (zq_matmul_workspace_bytes(w, m) larger than that) fail with
+ * ZQ_ERR_INVALID_ARGUMENT.  Allocates nothing.  The first call on each device
+ * resolves the array's device address and should precede any stream capture.
+ * All calls on a device share the array: calls that may overlap on the GPU
+ * race and must be serialised.  Same results as zq_matmul. */
+#define ZQ_NOALLOC_SCRATCH_BYTES (8u << 20)
+zq_status zq_matmul_noalloc(const zq_weight* w, const float* x, size_t m, const float* bias, float* y,
+                            void* stream);
+
 /* The same computation from host buffers to host buffers: copies x (and
  * bias) to the device, runs zq_matmul, copies y back and synchronises the
  * stream.  Device buffers are cached per thread and grow as needed. */

@@ -97,6 +97,7 @@ SIGNATURES = {
     "zq_weight_padded_k": (sz, [vp]),
     "zq_matmul_codes": (st, [vp, vp, vp, sz, vp, vp, vp, sz, vp]),
     "zq_matmul": (st, [vp, vp, sz, vp, vp, vp, sz, vp]),
+    "zq_matmul_noalloc": (st, [vp, vp, sz, vp, vp, vp]),
     "zq_matmul_host": (st, [vp, vp, sz, vp, vp, vp]),
     "zq_dequantize": (st, [vp, vp, vp]),
     "zq_device_error": (st, [vp, C.POINTER(C.c_uint32)]),

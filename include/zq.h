@@ -174,6 +174,48 @@ zq_status zq_dequantize_host(const zq_weight* w, float* out_host, void* stream);
  * ZQ_ERR_DEVICE_TIMEOUT when the word was set. */
 zq_status zq_device_error(void* stream, uint32_t* code);
 
+/* ---- quantized language model (device-resident decode) ----------------- */
+
+/* A QuantizedLanguageModel with weights, KV cache and activations resident on
+ * one device (replaces the host model of
+ * include/zyron/model/quantized_language_model.hpp:17-89). */
+typedef struct zq_lm zq_lm;
+
+/* transformer::Config of the loaded model (include/zyron/transformer/
+ * config.hpp:10-25) plus the type and the byte counts of
+ * QuantizedLanguageModel::quantized_bytes / float_reference_bytes. */
+typedef struct zq_lm_info {
+    size_t vocab_size, hidden_size, num_layers, num_heads, num_kv_heads, intermediate_size, max_sequence_length;
+    float norm_eps;
+    int use_rms_norm, causal, use_rope, tie_word_embeddings;
+    float rope_theta;
+    int type;
+    size_t quantized_bytes, float_reference_bytes;
+} zq_lm_info;
+
+/* Parse a .zyqmodel image (QuantizedLanguageModel::save/load format,
+ * src/model/quantized_language_model.cpp:615-642: same checks and messages)
+ * and upload it to the current device. */
+zq_status zq_lm_load(const void* bytes, size_t len, void* stream, zq_lm** out);
+
+zq_status zq_lm_get_info(const zq_lm* lm, zq_lm_info* info);
+
+/* QuantizedLanguageModel::generate with GenerationConfig{top_k = 1} (greedy;
+ * quantized_language_model.cpp:496-547).  Writes prompt + new tokens to
+ * out_tokens (capacity out_cap) and their count to *out_len; generation stops
+ * after max_new_tokens or when the sequence reaches max_sequence_length, as in
+ * the reference.  Ties between equal logits go to the lowest id.  When
+ * step_logits is not NULL it receives, for every new token, the vocab_size
+ * logits it was chosen from (parity testing; runs without CUDA graphs).
+ * Synchronous.  Runs on `stream` (which must not be a default stream, since
+ * the decode steps are captured as a CUDA graph), or on the model's own
+ * stream when `stream` is NULL. */
+zq_status zq_lm_generate_greedy(zq_lm* lm, const int64_t* prompt, size_t prompt_len, size_t max_new_tokens,
+                                int64_t* out_tokens, size_t out_cap, size_t* out_len, float* step_logits,
+                                void* stream);
+
+zq_status zq_lm_destroy(zq_lm* lm);
+
 #ifdef __cplusplus
 }
 #endif

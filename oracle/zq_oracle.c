@@ -24,6 +24,7 @@
 #include <math.h>
 #include <stdint.h>
 #include <stddef.h>
+#include <stdlib.h>
 #include <string.h>
 
 #define ZO_INT8 1
@@ -117,17 +118,22 @@ void zo_quantize_rows(const float* x, size_t M, size_t K, int8_t* q, float* row_
 void zo_matmul_codes(const int8_t* q, const float* row_scale, size_t M, size_t K,
                      int type, const void* payload, const float* col_scale, size_t N,
                      const float* bias, int32_t* acc, float* y) {
-    for (size_t m = 0; m < M; ++m) {
-        const int8_t* qr = q + m * K;
-        for (size_t c = 0; c < N; ++c) {
+    /* Column-outer loop: the column's codes (INT4 unpacked once, as value()
+     * would return them) are reused for every row.  Integer sums are exact,
+     * so the loop order does not change any result. */
+    int8_t* col = (int8_t*)malloc(K ? K : 1);
+    for (size_t c = 0; c < N; ++c) {
+        const int8_t* wc;
+        if (type == ZO_INT8) {
+            wc = (const int8_t*)payload + c * K;
+        } else {
+            for (size_t k = 0; k < K; ++k) col[k] = zo_weight_code(type, payload, K, c, k);
+            wc = col;
+        }
+        for (size_t m = 0; m < M; ++m) {
+            const int8_t* qr = q + m * K;
             int32_t a = 0;
-            if (type == ZO_INT8) {
-                const int8_t* wc = (const int8_t*)payload + c * K;
-                for (size_t k = 0; k < K; ++k) a += (int32_t)qr[k] * (int32_t)wc[k];
-            } else {
-                for (size_t k = 0; k < K; ++k)
-                    a += (int32_t)qr[k] * (int32_t)zo_weight_code(type, payload, K, c, k);
-            }
+            for (size_t k = 0; k < K; ++k) a += (int32_t)qr[k] * (int32_t)wc[k];
             if (acc) acc[m * N + c] = a;
             volatile float t = (float)a * row_scale[m];
             volatile float v = t * col_scale[c];
@@ -135,6 +141,7 @@ void zo_matmul_codes(const int8_t* q, const float* row_scale, size_t M, size_t K
             y[m * N + c] = v;
         }
     }
+    free(col);
 }
 
 /* matmul(): quantization.cpp:177-238 (row quant then dot + epilogue).

@@ -101,7 +101,21 @@ SIGNATURES = {
     "zq_matmul_host": (st, [vp, vp, sz, vp, vp, vp]),
     "zq_dequantize": (st, [vp, vp, vp]),
     "zq_device_error": (st, [vp, C.POINTER(C.c_uint32)]),
+    "zq_lm_load": (st, [vp, sz, vp, C.POINTER(vp)]),
+    "zq_lm_get_info": (st, [vp, vp]),
+    "zq_lm_generate_greedy": (st, [vp, vp, sz, sz, vp, sz, C.POINTER(sz), vp, vp]),
+    "zq_lm_destroy": (st, [vp]),
 }
+
+
+class LmInfo(C.Structure):
+    """zq_lm_info (include/zq.h)."""
+
+    _fields_ = [(n, C.c_size_t) for n in ("vocab_size", "hidden_size", "num_layers", "num_heads", "num_kv_heads",
+                                          "intermediate_size", "max_sequence_length")] + [
+        ("norm_eps", C.c_float), ("use_rms_norm", C.c_int), ("causal", C.c_int), ("use_rope", C.c_int),
+        ("tie_word_embeddings", C.c_int), ("rope_theta", C.c_float), ("type", C.c_int),
+        ("quantized_bytes", C.c_size_t), ("float_reference_bytes", C.c_size_t)]
 
 
 def header_symbols():

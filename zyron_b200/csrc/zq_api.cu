@@ -6,6 +6,7 @@
 // device error word.  No entry point falls back to the CPU.
 #include "zq.h"
 #include "zq_common.cuh"
+#include "zq_internal.h"
 #include "zq_kernels.h"
 
 #include <cuda.h>
@@ -25,20 +26,6 @@
 // Error word written by bounded device waits (see mbar_wait_bounded).  One
 // per device; the host reads and clears it in zq_device_error().
 __device__ uint32_t g_zq_device_error = 0;
-
-struct zq_weight {
-    int type = 0;
-    size_t K = 0, N = 0;
-    int Kp = 0;
-    int device = 0;
-    uint8_t* panel = nullptr;  // [N][Kp] int8 or [N][Kp/2] packed int4
-    float* scales = nullptr;   // [N]
-    size_t panel_bytes = 0;
-    // Tensor maps over the INT8 panel, one per GEMM tile width (64/128/256).
-    std::mutex mu;
-    CUtensorMap tmap_b[3];
-    bool tmap_ready[3] = {false, false, false};
-};
 
 namespace {
 
@@ -341,48 +328,11 @@ zq_status zq_weight_quantize_host(const float* w_host, size_t rows, size_t cols,
 zq_status zq_weight_load_zyq(const void* bytes, size_t len, size_t* consumed, void* stream, zq_weight** out) {
     if (!out) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null output handle");
     *out = nullptr;
-    const uint8_t* p = static_cast<const uint8_t*>(bytes);
-    size_t off = 0;
-    auto read = [&](void* dst, size_t n) -> bool {
-        if (!p || len - off < n || off > len) return false;
-        std::memcpy(dst, p + off, n);
-        off += n;
-        return true;
-    };
-    const char* corrupted = "ZYRON quantization: corrupted file";
-    uint32_t magic = 0, version = 0, type = 0;
-    uint64_t rows = 0, cols = 0, scale_count = 0, payload = 0;
-    // quantization.cpp:270-272 (short-circuit: the version is read only when
-    // the magic matches)
-    if (!read(&magic, 4)) return fail(ZQ_ERR_RUNTIME, corrupted);
-    if (magic != kZyqMagic) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: unsupported format");
-    if (!read(&version, 4)) return fail(ZQ_ERR_RUNTIME, corrupted);
-    if (version != kZyqVersion) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: unsupported format");
-    // 275-279
-    if (!read(&type, 4)) return fail(ZQ_ERR_RUNTIME, corrupted);
-    if (type != ZQ_TYPE_INT8 && type != ZQ_TYPE_INT4) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: invalid type");
-    // 280-289
-    if (!read(&rows, 8) || !read(&cols, 8)) return fail(ZQ_ERR_RUNTIME, corrupted);
-    if (rows == 0 || cols == 0) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: invalid matrix dimensions");
-    if (mul_overflows((size_t)rows, (size_t)cols)) return fail(ZQ_ERR_OVERFLOW, "ZYRON quantization: matrix size overflow");
-    // 291-297
-    if (!read(&scale_count, 8)) return fail(ZQ_ERR_RUNTIME, corrupted);
-    if (scale_count != cols) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: invalid scale count");
-    if (mul_overflows((size_t)cols, sizeof(float)) || len - off < cols * sizeof(float))
-        return fail(ZQ_ERR_RUNTIME, corrupted);
-    std::vector<float> scales((size_t)cols);
-    read(scales.data(), cols * sizeof(float));
-    for (float s : scales)
-        if (!(s > 0.0f) || !std::isfinite(s)) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: invalid scale");
-    // 299-309
-    if (!read(&payload, 8)) return fail(ZQ_ERR_RUNTIME, corrupted);
-    const size_t expected = ref_payload_bytes((int)type, (size_t)rows, (size_t)cols);
-    if (payload != expected) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: invalid payload size");
-    if (len - off < expected) return fail(ZQ_ERR_RUNTIME, corrupted);
-    const void* pay = p + off;
-    off += expected;
-    zq_status s = zq_weight_create((int)type, (size_t)rows, (size_t)cols, scales.data(), pay, expected, stream, out);
-    if (s == ZQ_OK && consumed) *consumed = off;
+    zq::ZyqRecord rec;
+    zq_status s = zq::parse_zyq(bytes, len, &rec);
+    if (s != ZQ_OK) return s;
+    s = zq_weight_create(rec.type, rec.rows, rec.cols, rec.scales.data(), rec.payload, rec.payload_bytes, stream, out);
+    if (s == ZQ_OK && consumed) *consumed = rec.consumed;
     return s;
 }
 
@@ -579,6 +529,86 @@ zq_status matmul_with_scratch(const zq_weight* w, const float* x, size_t m, cons
 }
 
 zq_status set_error(zq_status s, const char* msg) { return fail(s, msg); }
+
+zq_status parse_zyq(const void* bytes, size_t len, ZyqRecord* rec) {
+    const uint8_t* p = static_cast<const uint8_t*>(bytes);
+    size_t off = 0;
+    auto read = [&](void* dst, size_t n) -> bool {
+        if (!p || off > len || len - off < n) return false;
+        std::memcpy(dst, p + off, n);
+        off += n;
+        return true;
+    };
+    const char* corrupted = "ZYRON quantization: corrupted file";
+    uint32_t magic = 0, version = 0, type = 0;
+    uint64_t rows = 0, cols = 0, scale_count = 0, payload = 0;
+    // quantization.cpp:270-272 (short-circuit: the version is read only when
+    // the magic matches)
+    if (!read(&magic, 4)) return fail(ZQ_ERR_RUNTIME, corrupted);
+    if (magic != kZyqMagic) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: unsupported format");
+    if (!read(&version, 4)) return fail(ZQ_ERR_RUNTIME, corrupted);
+    if (version != kZyqVersion) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: unsupported format");
+    // 275-279
+    if (!read(&type, 4)) return fail(ZQ_ERR_RUNTIME, corrupted);
+    if (type != ZQ_TYPE_INT8 && type != ZQ_TYPE_INT4) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: invalid type");
+    // 280-289
+    if (!read(&rows, 8) || !read(&cols, 8)) return fail(ZQ_ERR_RUNTIME, corrupted);
+    if (rows == 0 || cols == 0) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: invalid matrix dimensions");
+    if (mul_overflows((size_t)rows, (size_t)cols)) return fail(ZQ_ERR_OVERFLOW, "ZYRON quantization: matrix size overflow");
+    // 291-297
+    if (!read(&scale_count, 8)) return fail(ZQ_ERR_RUNTIME, corrupted);
+    if (scale_count != cols) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: invalid scale count");
+    if (mul_overflows((size_t)cols, sizeof(float)) || len - off < cols * sizeof(float))
+        return fail(ZQ_ERR_RUNTIME, corrupted);
+    rec->scales.resize((size_t)cols);
+    read(rec->scales.data(), cols * sizeof(float));
+    for (float sc : rec->scales)
+        if (!(sc > 0.0f) || !std::isfinite(sc)) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: invalid scale");
+    // 299-309
+    if (!read(&payload, 8)) return fail(ZQ_ERR_RUNTIME, corrupted);
+    const size_t expected = ref_payload_bytes((int)type, (size_t)rows, (size_t)cols);
+    if (payload != expected) return fail(ZQ_ERR_RUNTIME, "ZYRON quantization: invalid payload size");
+    if (len - off < expected) return fail(ZQ_ERR_RUNTIME, corrupted);
+    rec->type = (int)type;
+    rec->rows = (size_t)rows;
+    rec->cols = (size_t)cols;
+    rec->payload = p + off;
+    rec->payload_bytes = expected;
+    rec->consumed = off + expected;
+    return ZQ_OK;
+}
+
+zq_status concat_cols(zq_weight* const* parts, int n, void* stream, zq_weight** out) {
+    *out = nullptr;
+    if (n < 1) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: nothing to concatenate");
+    size_t N = 0;
+    for (int i = 0; i < n; ++i) {
+        if (!parts[i] || parts[i]->type != parts[0]->type || parts[i]->K != parts[0]->K)
+            return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: column concatenation needs equal type and rows");
+        N += parts[i]->N;
+    }
+    zq_weight* r = nullptr;
+    zq_status s = new_weight(parts[0]->type, parts[0]->K, N, &r);
+    if (s != ZQ_OK) return s;
+    cudaStream_t st = as_stream(stream);
+    size_t col = 0;
+    cudaError_t e = cudaSuccess;
+    for (int i = 0; i < n && e == cudaSuccess; ++i) {
+        e = cudaMemcpyAsync(r->panel + col * col_bytes(r), parts[i]->panel, parts[i]->panel_bytes, cudaMemcpyDefault, st);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(r->scales + col, parts[i]->scales, parts[i]->N * sizeof(float), cudaMemcpyDefault, st);
+        col += parts[i]->N;
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+        zq_weight_destroy(r);
+        return cuda_fail(e, "column concatenation");
+    }
+    *out = r;
+    return ZQ_OK;
+}
+
+zq_status cuda_error(cudaError_t e, const char* what) { return cuda_fail(e, what); }
 
 }  // namespace zq
 

@@ -1,0 +1,995 @@
+// zq_lm.cu -- device-resident decode loop of ZYRON's QuantizedLanguageModel.
+//
+// The reference (src/model/quantized_language_model.cpp) recomputes the whole
+// prefix on the host for every generated token (generate_batch 503-547 ->
+// forward 468-494 -> forward_block 412-461) and runs each QuantizedLinear
+// through quantization::matmul.  Here weights, the KV cache and all
+// activations stay in HBM and one decode step is a fixed chain of kernels
+// that reads the position and token from device memory, so a step is
+// captured once as a CUDA graph and replayed for every position:
+//
+//   embed            token_lookup (271-282) [+ sinusoidal PE (488-490)]
+//   per block        norm1 -> q|k|v QuantizedLinear (one fused matmul over the
+//                    concatenated columns) -> RoPE + KV-cache append + causal
+//                    GQA attention for the new row (421-451) -> out_proj +
+//                    residual (453-454) -> norm2 -> ff_up + GELU -> ff_down +
+//                    residual (456-460)
+//   head             final RMS norm (492) -> lm_head (493) -> greedy argmax
+//                    (sample_next 82-174 with top_k = 1)
+//
+// Every QuantizedLinear keeps the reference's quantized arithmetic exactly:
+// the row of activations is quantized per row (absmax / 127, round half away
+// from zero), dotted in int32 against the INT8/INT4 column codes and rescaled
+// as float(acc) * s_row * s_col + bias.  The fp32 parts (norm reductions,
+// softmax, tanh-GELU, attention sums) follow the reference's formulas with a
+// parallel reduction order, so logits agree within a tolerance rather than
+// bit for bit, and an int8 code can flip where a value sits on a rounding
+// boundary.
+#include "zq.h"
+#include "zq_common.cuh"
+#include "zq_dot.cuh"
+#include "zq_internal.h"
+#include "zq_kernels.h"
+
+#include <cmath>
+#include <cstdio>
+#include <algorithm>
+#include <cstring>
+#include <limits>
+#include <string>
+#include <vector>
+
+namespace zq {
+namespace lm {
+
+constexpr int kThreads = 256;
+constexpr int kAttnThreads = 128;
+constexpr int kMaxHeadDim = 128;
+
+// Position state in device memory: the step kernels read it, the argmax
+// kernel advances it, so one captured step serves every position.
+struct State {
+    int pos;         // position whose logits this step computes
+    int prompt_len;  // positions < prompt_len - 1 are prefill (no logits needed)
+    int pad[2];
+};
+
+enum Prologue { kProNone = 0, kProRms = 1, kProLayer = 2 };
+enum Epilogue { kEpiStore = 0, kEpiGelu = 1, kEpiResidual = 2 };
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Block-wide reductions (all threads get the result).  `sh` holds >= 32 floats.
+template <int kN>
+__device__ float block_sum(float v, float* sh) {
+    v = warp_sum(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) sh[w] = v;
+    __syncthreads();
+    float t = (threadIdx.x < kN / 32) ? sh[threadIdx.x] : 0.0f;
+    if (w == 0) t = warp_sum(t);
+    if (threadIdx.x == 0) sh[0] = t;
+    __syncthreads();
+    return sh[0];
+}
+template <int kN>
+__device__ float block_max(float v, float* sh) {
+    v = warp_max(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) sh[w] = v;
+    __syncthreads();
+    float t = (threadIdx.x < kN / 32) ? sh[threadIdx.x] : -INFINITY;
+    if (w == 0) t = warp_max(t);
+    if (threadIdx.x == 0) sh[0] = t;
+    __syncthreads();
+    return sh[0];
+}
+
+// tanh-approximation GELU as the reference evaluates it (gelu 321-331):
+// 0.5f * x * (1 + tanh(kInvSqrt2Pi * (x + kC * x^3))), each operation rounded.
+__device__ __forceinline__ float gelu_ref(float x) {
+    const float kC = 0.044715f;
+    const float kInvSqrt2Pi = 0.7978845608028654f;
+    const float x3 = __fmul_rn(__fmul_rn(x, x), x);
+    const float inner = __fmul_rn(kInvSqrt2Pi, __fadd_rn(x, __fmul_rn(kC, x3)));
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+// ---------------------------------------------------------------------------
+// token_lookup (271-282): h[j] = float(code(j, token)) * scale[j]; the
+// embedding is quantized with vocab rows and hidden columns, so a token's
+// vector is one code from each hidden column.  Optional sinusoidal PE add.
+// ---------------------------------------------------------------------------
+__global__ void embed_kernel(const uint8_t* __restrict__ panel, int type, int Kp, const float* __restrict__ scales,
+                             int hidden, const int32_t* __restrict__ tokens, const State* __restrict__ st,
+                             const float* __restrict__ pe, float* __restrict__ h) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= hidden) return;
+    const int pos = st->pos;
+    const int tok = tokens[pos];
+    int code;
+    if (type == kInt8) {
+        code = (int8_t)panel[(size_t)j * Kp + tok];
+    } else {
+        const uint8_t b = panel[(size_t)j * (Kp >> 1) + (tok >> 1)];
+        const int nib = (tok & 1) ? (b >> 4) : (b & 0x0F);
+        code = nib < 8 ? nib : nib - 16;
+    }
+    float v = x86_mul((float)code, scales[j]);
+    if (pe) v = x86_add(v, pe[(size_t)pos * hidden + j]);
+    h[j] = v;
+}
+
+// ---------------------------------------------------------------------------
+// One QuantizedLinear on a single activation row, with the operations around
+// it fused:
+//   prologue  optional RMSNorm / LayerNorm of x (norm 284-319), then the
+//             per-row activation quantizer (quantization.cpp:202-212); every
+//             block computes it redundantly from x (K <= a few thousand), so
+//             no separate launch and no grid-wide sync are needed.
+//   body      warp-per-column int8 dot (dp4a) over the weight panel.
+//   epilogue  float(acc) * s_row * s_col + bias, then store / GELU / residual
+//             add (y = y + out, the reference's math::add(input, attended)).
+// `skip_prefill`: the lm_head skips positions whose logits nobody reads.
+// ---------------------------------------------------------------------------
+template <int kType, int kPro, int kEpi>
+__global__ void __launch_bounds__(kThreads) linear_kernel(const float* __restrict__ x, int K, int Kp,
+                                                          const float* __restrict__ nw, const float* __restrict__ nb,
+                                                          float eps, const uint8_t* __restrict__ panel,
+                                                          const float* __restrict__ scales, int N,
+                                                          const float* __restrict__ bias, float* y,
+                                                          const State* __restrict__ st, int skip_prefill) {
+    extern __shared__ __align__(16) float lsm[];
+    float* xs = lsm;                                          // [Kp] fp32 (normalised) activations
+    int8_t* qs = reinterpret_cast<int8_t*>(lsm + Kp);         // [Kp] codes
+    __shared__ float red[32];
+    if (skip_prefill && st->pos + 1 < st->prompt_len) return;
+
+    for (int i = threadIdx.x; i < Kp; i += kThreads) xs[i] = i < K ? x[i] : 0.0f;
+    __syncthreads();
+    if (kPro == kProRms) {
+        float ss = 0.0f;
+        for (int i = threadIdx.x; i < K; i += kThreads) ss = __fadd_rn(ss, __fmul_rn(xs[i], xs[i]));
+        ss = block_sum<kThreads>(ss, red);
+        const float var = __fdiv_rn(ss, (float)K);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+        for (int i = threadIdx.x; i < K; i += kThreads) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), nw[i]);
+        __syncthreads();
+    } else if (kPro == kProLayer) {
+        float sm = 0.0f;
+        for (int i = threadIdx.x; i < K; i += kThreads) sm = __fadd_rn(sm, xs[i]);
+        sm = block_sum<kThreads>(sm, red);
+        const float mean = __fdiv_rn(sm, (float)K);
+        float ss = 0.0f;
+        for (int i = threadIdx.x; i < K; i += kThreads) {
+            const float c = __fsub_rn(xs[i], mean);
+            ss = __fadd_rn(ss, __fmul_rn(c, c));
+        }
+        ss = block_sum<kThreads>(ss, red);
+        const float var = __fdiv_rn(ss, (float)K);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+        for (int i = threadIdx.x; i < K; i += kThreads)
+            xs[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xs[i], mean), inv), nw[i]), nb[i]);
+        __syncthreads();
+    }
+    float m = 0.0f;
+    for (int i = threadIdx.x; i < K; i += kThreads) m = fmaxf(m, fabsf(xs[i]));
+    m = block_max<kThreads>(m, red);
+    const float s = zq_scale_from_absmax(m, 127.0f);
+    for (int i = threadIdx.x; i < Kp; i += kThreads) {
+        const int8_t code = i < K ? (int8_t)zq_quantize_value(xs[i], s, 127) : (int8_t)0;
+        if (kType == kInt8) {
+            qs[i] = code;
+        } else {
+            // even/odd split per group of 8 codes, matching the nibble unpack
+            const int g = i & ~7, r = i & 7;
+            qs[g + ((r & 1) ? 4 + (r >> 1) : (r >> 1))] = code;
+        }
+    }
+    __syncthreads();
+
+    const int lane = threadIdx.x & 31;
+    const int warps_total = gridDim.x * (kThreads / 32);
+    const size_t cb = kType == kInt8 ? (size_t)Kp : (size_t)(Kp >> 1);
+    const int chunks = (int)(cb >> 4);
+    for (int col = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); col < N; col += warps_total) {
+        const uint8_t* wc = panel + (size_t)col * cb;
+        int acc[1] = {0};
+        for (int c = lane; c < chunks; c += 32) {
+            const uint4 w = ld_stream_u4(wc + (size_t)c * 16);
+            if (kType == kInt8)
+                dot16_int8<1>(w, qs, Kp, c * 16, acc);
+            else
+                dot16_int4<1>(w, qs, Kp, c * 32, acc);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], o);
+        if (lane == 0) {
+            float v = zq_epilogue(acc[0], s, scales[col]);
+            if (bias) v = x86_add(v, bias[col]);
+            if (kEpi == kEpiStore) y[col] = v;
+            else if (kEpi == kEpiGelu) y[col] = gelu_ref(v);
+            else y[col] = x86_add(y[col], v);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Attention for the newest row, one block per query head (forward_block
+// 424-451 restricted to the last query, which is all the next token needs):
+// RoPE on q and on the new key with the reference's cos/sin factors
+// (apply_rope 347-384, precomputed on the host with the same float formula),
+// append k/v to the cache (written once per KV head), scores = (q . k_j) *
+// 1/sqrt(head_dim) for j <= pos, softmax (44-64), context = sum_j p_j v_j.
+// GQA: query head h reads KV head h / (heads / kv_heads) (repeat_kv_heads
+// 386-410).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const float* __restrict__ qkv, int heads,
+                                                                 int kv_heads, int hd, float* kc, float* vc,
+                                                                 int max_seq, const float* __restrict__ rcos,
+                                                                 const float* __restrict__ rsin,
+                                                                 const State* __restrict__ st, float scale,
+                                                                 float* __restrict__ ctx) {
+    extern __shared__ float asm_[];
+    float* q = asm_;                 // [hd]
+    float* kn = q + kMaxHeadDim;     // [hd]
+    float* vn = kn + kMaxHeadDim;    // [hd]
+    float* sc = vn + kMaxHeadDim;    // [max_seq]
+    __shared__ float red[32];
+    const int h = blockIdx.x;
+    const int rep = heads / kv_heads;
+    const int kvh = h / rep;
+    const int pos = st->pos;
+    const int tid = threadIdx.x;
+    const float* qsrc = qkv + (size_t)h * hd;
+    const float* ksrc = qkv + (size_t)heads * hd + (size_t)kvh * hd;
+    const float* vsrc = qkv + (size_t)(heads + kv_heads) * hd + (size_t)kvh * hd;
+    const int half = hd >> 1;
+    if (rcos) {
+        if (tid < half) {
+            const float c = rcos[(size_t)pos * half + tid];
+            const float sn = rsin[(size_t)pos * half + tid];
+            const float qe = qsrc[2 * tid], qo = qsrc[2 * tid + 1];
+            q[2 * tid] = __fsub_rn(__fmul_rn(qe, c), __fmul_rn(qo, sn));
+            q[2 * tid + 1] = __fadd_rn(__fmul_rn(qe, sn), __fmul_rn(qo, c));
+            const float ke = ksrc[2 * tid], ko = ksrc[2 * tid + 1];
+            kn[2 * tid] = __fsub_rn(__fmul_rn(ke, c), __fmul_rn(ko, sn));
+            kn[2 * tid + 1] = __fadd_rn(__fmul_rn(ke, sn), __fmul_rn(ko, c));
+        }
+    } else if (tid < hd) {
+        q[tid] = qsrc[tid];
+        kn[tid] = ksrc[tid];
+    }
+    if (tid < hd) vn[tid] = vsrc[tid];
+    __syncthreads();
+    float* kc_head = kc + (size_t)kvh * max_seq * hd;
+    float* vc_head = vc + (size_t)kvh * max_seq * hd;
+    if (h % rep == 0 && tid < hd) {
+        kc_head[(size_t)pos * hd + tid] = kn[tid];
+        vc_head[(size_t)pos * hd + tid] = vn[tid];
+    }
+
+    float mx = -INFINITY;
+    for (int j = tid; j <= pos; j += kAttnThreads) {
+        const float* kj = j == pos ? kn : kc_head + (size_t)j * hd;
+        float dot = 0.0f;
+        for (int d = 0; d < hd; ++d) dot = __fadd_rn(dot, __fmul_rn(q[d], kj[d]));
+        const float v = __fmul_rn(dot, scale);
+        sc[j] = v;
+        mx = fmaxf(mx, v);
+    }
+    mx = block_max<kAttnThreads>(mx, red);
+    float sum = 0.0f;
+    for (int j = tid; j <= pos; j += kAttnThreads) {
+        const float e = expf(__fsub_rn(sc[j], mx));
+        sc[j] = e;
+        sum = __fadd_rn(sum, e);
+    }
+    sum = block_sum<kAttnThreads>(sum, red);
+    const float inv = sum > 0.0f ? __fdiv_rn(1.0f, sum) : 0.0f;
+    for (int j = tid; j <= pos; j += kAttnThreads) sc[j] = __fmul_rn(sc[j], inv);
+    __syncthreads();
+    if (tid < hd) {
+        float acc = 0.0f;
+        for (int j = 0; j <= pos; ++j) {
+            const float vj = j == pos ? vn[tid] : vc_head[(size_t)j * hd + tid];
+            acc = __fadd_rn(acc, __fmul_rn(sc[j], vj));
+        }
+        ctx[(size_t)h * hd + tid] = acc;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Greedy choice (sample_next with top_k = 1, 82-174): the highest logit,
+// lowest id on ties.  The reference returns token 0 when its softmax
+// denominator is not finite (any NaN logit, or a maximum of +-inf).  During
+// prefill the step only advances the position.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int V, int32_t* tokens,
+                                                      State* st) {
+    __shared__ float bv[32];
+    __shared__ int bi[32];
+    __shared__ int bnan[32];
+    const int pos = st->pos;
+    if (pos + 1 < st->prompt_len) {
+        __syncthreads();
+        if (threadIdx.x == 0) st->pos = pos + 1;
+        return;
+    }
+    float best = -INFINITY;
+    int idx = V;
+    int nan = 0;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const float v = logits[i];
+        if (isnan(v)) nan = 1;
+        else if (v > best || (v == best && i < idx)) best = v, idx = i;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        nan |= __shfl_xor_sync(0xffffffffu, nan, o);
+        if (ov > best || (ov == best && oi < idx)) best = ov, idx = oi;
+    }
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) bv[w] = best, bi[w] = idx, bnan[w] = nan;
+    __syncthreads();
+    if (w == 0) {
+        const int nw = blockDim.x >> 5;
+        best = l < nw ? bv[l] : -INFINITY;
+        idx = l < nw ? bi[l] : V;
+        nan = l < nw ? bnan[l] : 0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+            nan |= __shfl_xor_sync(0xffffffffu, nan, o);
+            if (ov > best || (ov == best && oi < idx)) best = ov, idx = oi;
+        }
+        if (l == 0) {
+            const int next = (nan || isinf(best) || idx >= V) ? 0 : idx;
+            tokens[pos + 1] = next;
+            st->pos = pos + 1;
+        }
+    }
+}
+
+}  // namespace lm
+}  // namespace zq
+
+// ===========================================================================
+// Host side
+// ===========================================================================
+
+namespace {
+
+using zq::lm::State;
+
+constexpr uint32_t kModelMagic = 0x4d4c5a51u;  // "QZLM" (quantized_language_model.cpp:557)
+constexpr uint32_t kModelVersion = 1;          // 558
+
+struct HostTensor {
+    std::vector<size_t> dims;
+    std::vector<float> data;  // empty tensor: no dims, no data
+    size_t size() const { return data.size(); }
+};
+
+struct HostLinear {
+    zq::ZyqRecord w;
+    HostTensor bias;
+};
+
+struct HostBlock {
+    bool rms1 = true, rms2 = true;
+    HostTensor n1w, n1b, n2w, n2b;
+    HostLinear q, k, v, o, up, down;
+};
+
+struct LmStatus {
+    zq_status s = ZQ_OK;
+    std::string msg;
+};
+
+class Reader {
+public:
+    Reader(const uint8_t* p, size_t n) : p_(p), n_(n) {}
+    bool read(void* dst, size_t k) {
+        if (!p_ || off_ > n_ || n_ - off_ < k) return false;
+        std::memcpy(dst, p_ + off_, k);
+        off_ += k;
+        return true;
+    }
+    const uint8_t* here() const { return p_ + off_; }
+    size_t left() const { return n_ - off_; }
+    void skip(size_t k) { off_ += k; }
+
+private:
+    const uint8_t* p_;
+    size_t n_, off_ = 0;
+};
+
+const char* kCorrupted = "ZYRON quantized model: corrupted file";
+
+struct ParseError {
+    zq_status s;
+    std::string msg;
+};
+
+uint32_t rd_u32(Reader& r) {
+    uint32_t v;
+    if (!r.read(&v, 4)) throw ParseError{ZQ_ERR_RUNTIME, kCorrupted};
+    return v;
+}
+uint64_t rd_u64(Reader& r) {
+    uint64_t v;
+    if (!r.read(&v, 8)) throw ParseError{ZQ_ERR_RUNTIME, kCorrupted};
+    return v;
+}
+float rd_f32(Reader& r) {
+    float v;
+    if (!r.read(&v, 4)) throw ParseError{ZQ_ERR_RUNTIME, kCorrupted};
+    return v;
+}
+
+// qread_tensor (quantized_language_model.cpp:605-612 region): rank, dims,
+// size, data; rank 0 with size 0 is the empty tensor.
+HostTensor rd_tensor(Reader& r) {
+    HostTensor t;
+    const uint64_t rank = rd_u64(r);
+    if (rank > 16) throw ParseError{ZQ_ERR_RUNTIME, "ZYRON quantized model: invalid tensor rank"};
+    size_t expect = 1;
+    for (uint64_t i = 0; i < rank; ++i) {
+        const uint64_t d = rd_u64(r);
+        if (d == 0) throw ParseError{ZQ_ERR_INVALID_ARGUMENT, "ZYRON Shape: dimensions must be > 0"};
+        if (expect > std::numeric_limits<size_t>::max() / d)
+            throw ParseError{ZQ_ERR_OVERFLOW, "ZYRON Shape: element count overflow"};
+        expect *= (size_t)d;
+        t.dims.push_back((size_t)d);
+    }
+    const uint64_t size = rd_u64(r);
+    if (rank == 0 && size == 0) return HostTensor{};
+    if (size != expect) throw ParseError{ZQ_ERR_RUNTIME, "ZYRON quantized model: tensor size mismatch"};
+    if (size > r.left() / sizeof(float)) throw ParseError{ZQ_ERR_RUNTIME, kCorrupted};
+    t.data.resize((size_t)size);
+    r.read(t.data.data(), (size_t)size * sizeof(float));
+    return t;
+}
+
+HostLinear rd_linear(Reader& r) {
+    HostLinear l;
+    zq_status s = zq::parse_zyq(r.here(), r.left(), &l.w);
+    if (s != ZQ_OK) throw ParseError{s, zq_last_error()};
+    r.skip(l.w.consumed);
+    l.bias = rd_tensor(r);
+    // QuantizedLinear(QuantizedMatrix, Tensor) checks (quantized_linear.cpp:8-14)
+    if (l.bias.size() != 0 && (l.bias.dims.size() != 1 || l.bias.size() != l.w.cols))
+        throw ParseError{ZQ_ERR_INVALID_ARGUMENT, "ZYRON QuantizedLinear: bias shape mismatch"};
+    return l;
+}
+
+// transformer::Config::validate (include/zyron/transformer/config.hpp:32-68).
+void validate_config(const zq_lm_info& c, size_t qat_bits, float dropout) {
+    const size_t kvh = c.num_kv_heads == 0 ? c.num_heads : c.num_kv_heads;
+    if (c.vocab_size == 0 || c.hidden_size == 0 || c.num_layers == 0 || c.num_heads == 0 ||
+        c.intermediate_size == 0 || c.max_sequence_length == 0)
+        throw ParseError{ZQ_ERR_INVALID_ARGUMENT, "ZYRON Transformer: dimensions must be > 0"};
+    if (c.hidden_size % c.num_heads != 0)
+        throw ParseError{ZQ_ERR_INVALID_ARGUMENT, "ZYRON Transformer: hidden_size must be divisible by num_heads"};
+    if (kvh == 0 || kvh > c.num_heads || c.num_heads % kvh != 0)
+        throw ParseError{ZQ_ERR_INVALID_ARGUMENT,
+                         "ZYRON Transformer: num_kv_heads must divide num_heads and be <= num_heads"};
+    if (c.use_rope && ((c.hidden_size / c.num_heads) % 2 != 0))
+        throw ParseError{ZQ_ERR_INVALID_ARGUMENT, "ZYRON Transformer: RoPE requires an even attention head dimension"};
+    if (!(c.norm_eps > 0.0f)) throw ParseError{ZQ_ERR_INVALID_ARGUMENT, "ZYRON Transformer: norm_eps must be > 0"};
+    if (!(c.rope_theta > 0.0f) || !std::isfinite(c.rope_theta))
+        throw ParseError{ZQ_ERR_INVALID_ARGUMENT, "ZYRON Transformer: rope_theta must be finite and > 0"};
+    if (!(dropout >= 0.0f) || dropout >= 1.0f || !std::isfinite(dropout))
+        throw ParseError{ZQ_ERR_INVALID_ARGUMENT, "ZYRON Transformer: dropout must be finite and in [0, 1)"};
+    if (qat_bits != 4 && qat_bits != 8)
+        throw ParseError{ZQ_ERR_INVALID_ARGUMENT, "ZYRON Transformer: qat_bits must be 4 or 8"};
+}
+
+size_t tensor_bytes(const HostTensor& t) { return t.size() * sizeof(float); }
+size_t zyq_bytes(const zq::ZyqRecord& w) { return w.payload_bytes + w.cols * sizeof(float); }
+
+struct DevLayer {
+    bool rms1 = true, rms2 = true;
+    float *n1w = nullptr, *n1b = nullptr, *n2w = nullptr, *n2b = nullptr;
+    zq_weight *qkv = nullptr, *out = nullptr, *up = nullptr, *down = nullptr;
+    float *b_qkv = nullptr, *b_out = nullptr, *b_up = nullptr, *b_down = nullptr;
+};
+
+}  // namespace
+
+struct zq_lm {
+    zq_lm_info info{};
+    int device = 0;
+    zq_weight* emb = nullptr;
+    float* pe = nullptr;
+    float* final_w = nullptr;
+    std::vector<DevLayer> layers;
+    zq_weight* head = nullptr;
+    float* b_head = nullptr;
+    // runtime buffers
+    float *h = nullptr, *qkv = nullptr, *ctx = nullptr, *ff = nullptr, *logits = nullptr;
+    float *kc = nullptr, *vc = nullptr;
+    float *rcos = nullptr, *rsin = nullptr;
+    int32_t* tokens = nullptr;
+    State* state = nullptr;
+    std::vector<void*> allocations;
+    cudaGraphExec_t graph_one = nullptr;
+    cudaGraphExec_t graph_chunk = nullptr;
+    int chunk = 16;
+    // Used when the caller passes no stream: graph capture needs a stream
+    // that is not a default stream.
+    cudaStream_t own_stream = nullptr;
+    ~zq_lm();
+};
+
+zq_lm::~zq_lm() {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    if (cur != device) cudaSetDevice(device);
+    if (graph_one) cudaGraphExecDestroy(graph_one);
+    if (graph_chunk) cudaGraphExecDestroy(graph_chunk);
+    if (own_stream) cudaStreamDestroy(own_stream);
+    zq_weight_destroy(emb);
+    zq_weight_destroy(head);
+    for (auto& l : layers) {
+        zq_weight_destroy(l.qkv);
+        zq_weight_destroy(l.out);
+        zq_weight_destroy(l.up);
+        zq_weight_destroy(l.down);
+    }
+    for (void* p : allocations) cudaFree(p);
+    if (cur != device) cudaSetDevice(cur);
+}
+
+namespace {
+
+template <class T>
+cudaError_t dev_alloc(zq_lm* lm, T** p, size_t count) {
+    void* q = nullptr;
+    cudaError_t e = cudaMalloc(&q, count * sizeof(T) > 0 ? count * sizeof(T) : 16);
+    if (e == cudaSuccess) {
+        lm->allocations.push_back(q);
+        *p = static_cast<T*>(q);
+    }
+    return e;
+}
+
+cudaError_t upload_tensor(zq_lm* lm, const HostTensor& t, float** out, cudaStream_t st) {
+    *out = nullptr;
+    if (t.size() == 0) return cudaSuccess;
+    cudaError_t e = dev_alloc(lm, out, t.size());
+    if (e == cudaSuccess) e = cudaMemcpyAsync(*out, t.data.data(), t.size() * sizeof(float), cudaMemcpyHostToDevice, st);
+    return e;
+}
+
+zq_status make_weight(const zq::ZyqRecord& r, void* stream, zq_weight** out) {
+    return zq_weight_create(r.type, r.rows, r.cols, r.scales.data(), r.payload, r.payload_bytes, stream, out);
+}
+
+#define LM_CUDA(call)                                             \
+    do {                                                          \
+        cudaError_t _e = (call);                                  \
+        if (_e != cudaSuccess) return zq::cuda_error(_e, #call);  \
+    } while (0)
+
+#define LM_OK(call)                      \
+    do {                                 \
+        zq_status _s = (call);           \
+        if (_s != ZQ_OK) return _s;      \
+    } while (0)
+
+size_t linear_smem(int Kp) { return (size_t)Kp * sizeof(float) + (size_t)Kp; }
+
+constexpr size_t kMaxLinearSmem = 200 * 1024;
+
+template <int kType, int kPro, int kEpi>
+cudaError_t prepare_linear_t() {
+    return cudaFuncSetAttribute(zq::lm::linear_kernel<kType, kPro, kEpi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)kMaxLinearSmem);
+}
+
+template <int kType>
+cudaError_t prepare_type() {
+    using namespace zq::lm;
+    cudaError_t e = prepare_linear_t<kType, kProNone, kEpiStore>();
+    if (e == cudaSuccess) e = prepare_linear_t<kType, kProNone, kEpiGelu>();
+    if (e == cudaSuccess) e = prepare_linear_t<kType, kProNone, kEpiResidual>();
+    if (e == cudaSuccess) e = prepare_linear_t<kType, kProRms, kEpiStore>();
+    if (e == cudaSuccess) e = prepare_linear_t<kType, kProRms, kEpiGelu>();
+    if (e == cudaSuccess) e = prepare_linear_t<kType, kProRms, kEpiResidual>();
+    if (e == cudaSuccess) e = prepare_linear_t<kType, kProLayer, kEpiStore>();
+    if (e == cudaSuccess) e = prepare_linear_t<kType, kProLayer, kEpiGelu>();
+    if (e == cudaSuccess) e = prepare_linear_t<kType, kProLayer, kEpiResidual>();
+    return e;
+}
+
+// Kernel attributes are set once at load, outside any stream capture.
+cudaError_t prepare_kernels() {
+    cudaError_t e = prepare_type<ZQ_TYPE_INT8>();
+    if (e == cudaSuccess) e = prepare_type<ZQ_TYPE_INT4>();
+    return e;
+}
+
+template <int kType, int kPro, int kEpi>
+cudaError_t launch_linear_t(const float* x, const float* nw, const float* nb, float eps, const zq_weight* w,
+                            const float* bias, float* y, const State* st, int skip_prefill, cudaStream_t s) {
+    auto kern = zq::lm::linear_kernel<kType, kPro, kEpi>;
+    const size_t smem = linear_smem(w->Kp);
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int blocks = (int)((w->N + 7) / 8);
+    if (blocks > 2 * sms) blocks = 2 * sms;
+    kern<<<blocks, zq::lm::kThreads, smem, s>>>(x, (int)w->K, w->Kp, nw, nb, eps, w->panel, w->scales, (int)w->N,
+                                                bias, y, st, skip_prefill);
+    return cudaGetLastError();
+}
+
+template <int kPro, int kEpi>
+cudaError_t launch_linear(const float* x, const float* nw, const float* nb, float eps, const zq_weight* w,
+                          const float* bias, float* y, const State* st, int skip_prefill, cudaStream_t s) {
+    return w->type == ZQ_TYPE_INT8
+               ? launch_linear_t<ZQ_TYPE_INT8, kPro, kEpi>(x, nw, nb, eps, w, bias, y, st, skip_prefill, s)
+               : launch_linear_t<ZQ_TYPE_INT4, kPro, kEpi>(x, nw, nb, eps, w, bias, y, st, skip_prefill, s);
+}
+
+template <int kEpi>
+cudaError_t launch_normed(bool rms, const float* x, const float* nw, const float* nb, float eps, const zq_weight* w,
+                          const float* bias, float* y, const State* st, int skip, cudaStream_t s) {
+    return rms ? launch_linear<zq::lm::kProRms, kEpi>(x, nw, nb, eps, w, bias, y, st, skip, s)
+               : launch_linear<zq::lm::kProLayer, kEpi>(x, nw, nb, eps, w, bias, y, st, skip, s);
+}
+
+// Enqueue one decode step (all kernels) on `s`.
+cudaError_t enqueue_step(zq_lm* lm, cudaStream_t s) {
+    const zq_lm_info& c = lm->info;
+    const int hd = (int)(c.hidden_size / c.num_heads);
+    const int kvh = (int)(c.num_kv_heads == 0 ? c.num_heads : c.num_kv_heads);
+    const float eps = c.norm_eps;
+    const int hidden = (int)c.hidden_size;
+    zq::lm::embed_kernel<<<(hidden + 255) / 256, 256, 0, s>>>(lm->emb->panel, lm->emb->type, lm->emb->Kp,
+                                                            lm->emb->scales, hidden, lm->tokens, lm->state, lm->pe,
+                                                            lm->h);
+    cudaError_t e = cudaGetLastError();
+    const size_t cache_layer = (size_t)kvh * c.max_sequence_length * hd;
+    const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
+    const size_t attn_smem = (3 * zq::lm::kMaxHeadDim + c.max_sequence_length) * sizeof(float);
+    for (size_t li = 0; li < lm->layers.size() && e == cudaSuccess; ++li) {
+        const DevLayer& L = lm->layers[li];
+        e = launch_normed<zq::lm::kEpiStore>(L.rms1, lm->h, L.n1w, L.n1b, eps, L.qkv, L.b_qkv, lm->qkv, lm->state, 0, s);
+        if (e != cudaSuccess) break;
+        zq::lm::attention_kernel<<<(int)c.num_heads, zq::lm::kAttnThreads, attn_smem, s>>>(
+            lm->qkv, (int)c.num_heads, kvh, hd, lm->kc + li * cache_layer, lm->vc + li * cache_layer,
+            (int)c.max_sequence_length, c.use_rope ? lm->rcos : nullptr, c.use_rope ? lm->rsin : nullptr, lm->state,
+            scale, lm->ctx);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) break;
+        e = launch_linear<zq::lm::kProNone, zq::lm::kEpiResidual>(lm->ctx, nullptr, nullptr, eps, L.out, L.b_out, lm->h,
+                                                                  lm->state, 0, s);
+        if (e != cudaSuccess) break;
+        e = launch_normed<zq::lm::kEpiGelu>(L.rms2, lm->h, L.n2w, L.n2b, eps, L.up, L.b_up, lm->ff, lm->state, 0, s);
+        if (e != cudaSuccess) break;
+        e = launch_linear<zq::lm::kProNone, zq::lm::kEpiResidual>(lm->ff, nullptr, nullptr, eps, L.down, L.b_down,
+                                                                  lm->h, lm->state, 0, s);
+    }
+    if (e != cudaSuccess) return e;
+    // final norm is always RMS without bias (forward 492)
+    e = launch_linear<zq::lm::kProRms, zq::lm::kEpiStore>(lm->h, lm->final_w, nullptr, eps, lm->head, lm->b_head,
+                                                          lm->logits, lm->state, 1, s);
+    if (e != cudaSuccess) return e;
+    zq::lm::argmax_kernel<<<1, 1024, 0, s>>>(lm->logits, (int)c.vocab_size, lm->tokens, lm->state);
+    return cudaGetLastError();
+}
+
+cudaError_t build_graph(zq_lm* lm, int steps, cudaGraphExec_t* out, cudaStream_t s) {
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) return e;
+    for (int i = 0; i < steps && e == cudaSuccess; ++i) e = enqueue_step(lm, s);
+    cudaError_t e2 = cudaStreamEndCapture(s, &g);
+    if (e == cudaSuccess) e = e2;
+    if (e == cudaSuccess) e = cudaGraphInstantiate(out, g, 0);
+    if (g) cudaGraphDestroy(g);
+    return e;
+}
+
+zq_status fail_lm(zq_status s, const std::string& msg) { return zq::set_error(s, msg.c_str()); }
+
+}  // namespace
+
+extern "C" {
+
+zq_status zq_lm_load(const void* bytes, size_t len, void* stream, zq_lm** out) {
+    if (!out) return fail_lm(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null output handle");
+    *out = nullptr;
+    Reader r(static_cast<const uint8_t*>(bytes), len);
+    zq_lm_info c{};
+    int type = 0;
+    std::vector<HostBlock> blocks;
+    zq::ZyqRecord emb;
+    HostTensor pe, final_w;
+    HostLinear head;
+    try {
+        // QuantizedLanguageModel::load (quantized_language_model.cpp:627-642)
+        if (rd_u32(r) != kModelMagic || rd_u32(r) != kModelVersion)
+            throw ParseError{ZQ_ERR_RUNTIME, "ZYRON quantized model: unsupported format"};
+        type = (int)rd_u32(r);
+        if (type != 1 && type != 2) throw ParseError{ZQ_ERR_RUNTIME, "ZYRON quantized model: invalid type"};
+        // q_read_config (581-587)
+        c.vocab_size = rd_u64(r);
+        c.hidden_size = rd_u64(r);
+        c.num_layers = rd_u64(r);
+        c.num_heads = rd_u64(r);
+        c.num_kv_heads = rd_u64(r);
+        c.intermediate_size = rd_u64(r);
+        c.max_sequence_length = rd_u64(r);
+        c.norm_eps = rd_f32(r);
+        c.use_rms_norm = rd_u32(r) != 0;
+        c.causal = rd_u32(r) != 0;
+        c.use_rope = rd_u32(r) != 0;
+        c.tie_word_embeddings = rd_u32(r) != 0;
+        c.rope_theta = rd_f32(r);
+        const float dropout = rd_f32(r);
+        (void)rd_u32(r);  // use_qat
+        const uint64_t qat_bits = rd_u64(r);
+        validate_config(c, (size_t)qat_bits, dropout);
+        zq_status s = zq::parse_zyq(r.here(), r.left(), &emb);
+        if (s != ZQ_OK) throw ParseError{s, zq_last_error()};
+        r.skip(emb.consumed);
+        pe = rd_tensor(r);
+        final_w = rd_tensor(r);
+        const uint64_t nblocks = rd_u64(r);
+        if (nblocks != c.num_layers) throw ParseError{ZQ_ERR_RUNTIME, "ZYRON quantized model: layer count mismatch"};
+        for (uint64_t i = 0; i < nblocks; ++i) {
+            HostBlock b;
+            b.rms1 = rd_u32(r) != 0;
+            b.n1w = rd_tensor(r);
+            b.n1b = rd_tensor(r);
+            b.rms2 = rd_u32(r) != 0;
+            b.n2w = rd_tensor(r);
+            b.n2b = rd_tensor(r);
+            b.q = rd_linear(r);
+            b.k = rd_linear(r);
+            b.v = rd_linear(r);
+            b.o = rd_linear(r);
+            b.up = rd_linear(r);
+            b.down = rd_linear(r);
+            blocks.push_back(std::move(b));
+        }
+        head = rd_linear(r);
+    } catch (const ParseError& pe_) {
+        return fail_lm(pe_.s, pe_.msg);
+    }
+    c.type = type;
+
+    // Shape consistency the device kernels rely on (the reference would fail
+    // later, inside forward()).
+    const size_t H = c.hidden_size, V = c.vocab_size, F = c.intermediate_size;
+    const size_t kvh = c.num_kv_heads == 0 ? c.num_heads : c.num_kv_heads;
+    const size_t hd = H / c.num_heads;
+    auto bad = [](const char* what) { return fail_lm(ZQ_ERR_INVALID_ARGUMENT, std::string("zyron_b200: ") + what); };
+    if (hd > (size_t)zq::lm::kMaxHeadDim) return bad("head dimension above 128 is not supported on the device");
+    if ((3 * zq::lm::kMaxHeadDim + c.max_sequence_length) * sizeof(float) > 200 * 1024)
+        return bad("max_sequence_length above 50000 is not supported on the device");
+    if (linear_smem(zq::padded_k(type, (int)std::max(H, F))) > kMaxLinearSmem)
+        return bad("hidden or intermediate size too large for the device decode kernels");
+    if (emb.rows != V || emb.cols != H) return bad("token embedding shape does not match the config");
+    if (head.w.rows != H || head.w.cols != V) return bad("lm_head shape does not match the config");
+    if (final_w.size() != H) return bad("final norm weight size does not match the config");
+    if (!c.use_rope && pe.size() != c.max_sequence_length * H) return bad("positional encoding shape mismatch");
+    for (const auto& b : blocks) {
+        if (b.q.w.rows != H || b.q.w.cols != H || b.k.w.rows != H || b.k.w.cols != kvh * hd || b.v.w.rows != H ||
+            b.v.w.cols != kvh * hd || b.o.w.rows != H || b.o.w.cols != H || b.up.w.rows != H || b.up.w.cols != F ||
+            b.down.w.rows != F || b.down.w.cols != H)
+            return bad("block projection shapes do not match the config");
+        if (b.n1w.size() != H || b.n2w.size() != H || (!b.rms1 && b.n1b.size() != H) || (!b.rms2 && b.n2b.size() != H))
+            return bad("block norm shapes do not match the config");
+        if (b.q.w.type != type || b.k.w.type != type || b.v.w.type != type)
+            return bad("q/k/v projections must share one quantization type");
+    }
+
+    // quantized_bytes / float_reference_bytes as load() computes them (636-641, 644-664)
+    size_t qb = zyq_bytes(emb) + tensor_bytes(pe) + tensor_bytes(final_w) + zyq_bytes(head.w) + tensor_bytes(head.bias);
+    size_t fb = emb.rows * emb.cols * 4 + tensor_bytes(pe) + tensor_bytes(final_w) + head.w.rows * head.w.cols * 4 +
+                tensor_bytes(head.bias);
+    for (const auto& b : blocks) {
+        qb += tensor_bytes(b.n1w) + tensor_bytes(b.n1b) + tensor_bytes(b.n2w) + tensor_bytes(b.n2b);
+        fb += tensor_bytes(b.n1w) + tensor_bytes(b.n1b) + tensor_bytes(b.n2w) + tensor_bytes(b.n2b);
+        for (const HostLinear* l : {&b.q, &b.k, &b.v, &b.o, &b.up, &b.down}) {
+            qb += zyq_bytes(l->w);
+            fb += l->w.rows * l->w.cols * 4 + tensor_bytes(l->bias);
+        }
+    }
+    c.quantized_bytes = qb;
+    c.float_reference_bytes = fb;
+
+    // ---- upload ---------------------------------------------------------
+    auto* lm = new (std::nothrow) zq_lm;
+    if (!lm) return fail_lm(ZQ_ERR_RUNTIME, "zyron_b200: out of host memory");
+    lm->info = c;
+    cudaGetDevice(&lm->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
+    auto cleanup = [&](zq_status s) {
+        delete lm;
+        return s;
+    };
+    cudaError_t e0 = prepare_kernels();
+    if (e0 != cudaSuccess) return cleanup(zq::cuda_error(e0, "kernel attributes"));
+    zq_status s = make_weight(emb, stream, &lm->emb);
+    if (s != ZQ_OK) return cleanup(s);
+    s = make_weight(head.w, stream, &lm->head);
+    if (s != ZQ_OK) return cleanup(s);
+    cudaError_t e = upload_tensor(lm, head.bias, &lm->b_head, st);
+    if (e == cudaSuccess) e = upload_tensor(lm, final_w, &lm->final_w, st);
+    if (e == cudaSuccess && !c.use_rope) e = upload_tensor(lm, pe, &lm->pe, st);
+    for (const auto& b : blocks) {
+        if (e != cudaSuccess) break;
+        DevLayer d;
+        d.rms1 = b.rms1;
+        d.rms2 = b.rms2;
+        zq_weight *wq = nullptr, *wk = nullptr, *wv = nullptr;
+        s = make_weight(b.q.w, stream, &wq);
+        if (s == ZQ_OK) s = make_weight(b.k.w, stream, &wk);
+        if (s == ZQ_OK) s = make_weight(b.v.w, stream, &wv);
+        if (s == ZQ_OK) {
+            zq_weight* parts[3] = {wq, wk, wv};
+            s = zq::concat_cols(parts, 3, stream, &d.qkv);
+        }
+        zq_weight_destroy(wq);
+        zq_weight_destroy(wk);
+        zq_weight_destroy(wv);
+        if (s == ZQ_OK) s = make_weight(b.o.w, stream, &d.out);
+        if (s == ZQ_OK) s = make_weight(b.up.w, stream, &d.up);
+        if (s == ZQ_OK) s = make_weight(b.down.w, stream, &d.down);
+        lm->layers.push_back(d);  // owned weights are released by ~zq_lm
+        if (s != ZQ_OK) return cleanup(s);
+        DevLayer& L = lm->layers.back();
+        e = upload_tensor(lm, b.n1w, &L.n1w, st);
+        if (e == cudaSuccess) e = upload_tensor(lm, b.n1b, &L.n1b, st);
+        if (e == cudaSuccess) e = upload_tensor(lm, b.n2w, &L.n2w, st);
+        if (e == cudaSuccess) e = upload_tensor(lm, b.n2b, &L.n2b, st);
+        // concatenated q|k|v bias; a missing bias adds zeros
+        if (e == cudaSuccess && (b.q.bias.size() || b.k.bias.size() || b.v.bias.size())) {
+            HostTensor cat;
+            const size_t nq = b.q.w.cols, nk = b.k.w.cols, nv = b.v.w.cols;
+            cat.dims = {nq + nk + nv};
+            cat.data.assign(nq + nk + nv, 0.0f);
+            if (b.q.bias.size()) std::memcpy(cat.data.data(), b.q.bias.data.data(), nq * 4);
+            if (b.k.bias.size()) std::memcpy(cat.data.data() + nq, b.k.bias.data.data(), nk * 4);
+            if (b.v.bias.size()) std::memcpy(cat.data.data() + nq + nk, b.v.bias.data.data(), nv * 4);
+            e = upload_tensor(lm, cat, &L.b_qkv, st);
+        }
+        if (e == cudaSuccess) e = upload_tensor(lm, b.o.bias, &L.b_out, st);
+        if (e == cudaSuccess) e = upload_tensor(lm, b.up.bias, &L.b_up, st);
+        if (e == cudaSuccess) e = upload_tensor(lm, b.down.bias, &L.b_down, st);
+    }
+    // runtime buffers
+    const size_t T = c.max_sequence_length;
+    if (e == cudaSuccess) e = dev_alloc(lm, &lm->h, H);
+    if (e == cudaSuccess) e = dev_alloc(lm, &lm->qkv, H + 2 * kvh * hd);
+    if (e == cudaSuccess) e = dev_alloc(lm, &lm->ctx, H);
+    if (e == cudaSuccess) e = dev_alloc(lm, &lm->ff, F);
+    if (e == cudaSuccess) e = dev_alloc(lm, &lm->logits, V);
+    if (e == cudaSuccess) e = dev_alloc(lm, &lm->kc, c.num_layers * kvh * T * hd);
+    if (e == cudaSuccess) e = dev_alloc(lm, &lm->vc, c.num_layers * kvh * T * hd);
+    if (e == cudaSuccess) e = dev_alloc(lm, &lm->tokens, T + 2);
+    if (e == cudaSuccess) e = dev_alloc(lm, &lm->state, 1);
+    if (e == cudaSuccess && c.use_rope) {
+        // apply_rope factors (quantized_language_model.cpp:367-374), computed
+        // with the same float formula: angle = pos / pow(theta, 2p / hd).
+        const size_t half = hd / 2;
+        std::vector<float> cs(T * half), sn(T * half);
+        for (size_t p = 0; p < T; ++p) {
+            const float absolute = static_cast<float>(p);
+            for (size_t pair = 0; pair < half; ++pair) {
+                const float exponent = (2.0f * static_cast<float>(pair)) / static_cast<float>(hd);
+                const float angle = absolute / std::pow(c.rope_theta, exponent);
+                cs[p * half + pair] = std::cos(angle);
+                sn[p * half + pair] = std::sin(angle);
+            }
+        }
+        e = dev_alloc(lm, &lm->rcos, T * half);
+        if (e == cudaSuccess) e = dev_alloc(lm, &lm->rsin, T * half);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(lm->rcos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(lm->rsin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&lm->own_stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return cleanup(zq::cuda_error(e, "language model upload"));
+    *out = lm;
+    return ZQ_OK;
+}
+
+zq_status zq_lm_get_info(const zq_lm* lm, zq_lm_info* info) {
+    if (!lm || !info) return fail_lm(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null argument");
+    *info = lm->info;
+    return ZQ_OK;
+}
+
+zq_status zq_lm_generate_greedy(zq_lm* lm, const int64_t* prompt, size_t prompt_len, size_t max_new_tokens,
+                                int64_t* out_tokens, size_t out_cap, size_t* out_len, float* step_logits,
+                                void* stream) {
+    if (!lm) return fail_lm(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null model");
+    const zq_lm_info& c = lm->info;
+    // generate_batch checks (quantized_language_model.cpp:503-517)
+    if (prompt_len == 0 || !prompt) return fail_lm(ZQ_ERR_INVALID_ARGUMENT, "ZYRON QuantizedLanguageModel: empty prompt");
+    if (prompt_len > c.max_sequence_length)
+        return fail_lm(ZQ_ERR_INVALID_ARGUMENT, "ZYRON QuantizedLanguageModel: prompt exceeds context");
+    for (size_t i = 0; i < prompt_len; ++i)
+        if (prompt[i] < 0 || (uint64_t)prompt[i] >= c.vocab_size)
+            return fail_lm(ZQ_ERR_OUT_OF_RANGE, "ZYRON QuantizedLanguageModel: token id out of range");
+    // tokens stop growing once they reach max_sequence_length (539-545)
+    size_t n_new = 0;
+    if (max_new_tokens > 0) {
+        const size_t room = c.max_sequence_length > prompt_len ? c.max_sequence_length - prompt_len : 1;
+        n_new = max_new_tokens < room ? max_new_tokens : room;
+    }
+    const size_t total = prompt_len + n_new;
+    if (out_len) *out_len = total;
+    if (!out_tokens || out_cap < total)
+        return fail_lm(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: output token buffer too small");
+    for (size_t i = 0; i < prompt_len; ++i) out_tokens[i] = prompt[i];
+    if (n_new == 0) return ZQ_OK;
+
+    int cur = 0;
+    LM_CUDA(cudaGetDevice(&cur));
+    if (cur != lm->device) return fail_lm(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: model lives on another device");
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : lm->own_stream;
+    std::vector<int32_t> tok(c.max_sequence_length + 2, 0);
+    for (size_t i = 0; i < prompt_len; ++i) tok[i] = (int32_t)prompt[i];
+    State s0{0, (int)prompt_len, {0, 0}};
+    LM_CUDA(cudaMemcpyAsync(lm->tokens, tok.data(), tok.size() * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    LM_CUDA(cudaMemcpyAsync(lm->state, &s0, sizeof s0, cudaMemcpyHostToDevice, st));
+
+    const size_t steps = prompt_len - 1 + n_new;  // last step produces the last new token
+    if (step_logits) {
+        // parity mode: per step, copy the logits that chose each new token
+        for (size_t i = 0; i < steps; ++i) {
+            LM_CUDA(enqueue_step(lm, st));
+            if (i + 1 >= prompt_len) {
+                const size_t g = i + 1 - prompt_len;
+                LM_CUDA(cudaMemcpyAsync(step_logits + g * c.vocab_size, lm->logits, c.vocab_size * sizeof(float),
+                                        cudaMemcpyDeviceToHost, st));
+            }
+        }
+    } else {
+        if (!lm->graph_one) LM_CUDA(build_graph(lm, 1, &lm->graph_one, st));
+        if (!lm->graph_chunk && steps >= (size_t)lm->chunk) LM_CUDA(build_graph(lm, lm->chunk, &lm->graph_chunk, st));
+        size_t done = 0;
+        while (steps - done >= (size_t)lm->chunk && lm->graph_chunk) {
+            LM_CUDA(cudaGraphLaunch(lm->graph_chunk, st));
+            done += lm->chunk;
+        }
+        while (done < steps) {
+            LM_CUDA(cudaGraphLaunch(lm->graph_one, st));
+            ++done;
+        }
+    }
+    LM_CUDA(cudaMemcpyAsync(tok.data(), lm->tokens, total * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    LM_CUDA(cudaStreamSynchronize(st));
+    for (size_t i = prompt_len; i < total; ++i) out_tokens[i] = tok[i];
+    return ZQ_OK;
+}
+
+zq_status zq_lm_destroy(zq_lm* lm) {
+    delete lm;
+    return ZQ_OK;
+}
+
+}  // extern "C"

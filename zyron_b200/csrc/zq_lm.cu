@@ -17,6 +17,14 @@
 //   head             final RMS norm (492) -> lm_head (493) -> greedy argmax
 //                    (sample_next 82-174 with top_k = 1)
 //
+// Kernels are chained with programmatic dependent launch, so several later
+// kernels of the chain can already be resident on an SM while earlier ones
+// run.  griddepcontrol.wait makes the producer's writes visible in L2, but an
+// SM's L1 may still hold lines another resident kernel loaded before those
+// writes; every read of data produced by another kernel (activations,
+// position state, tokens, KV cache, logits) therefore goes through L2 only
+// (ld.global.cg).  Constant data (weights, norms, RoPE tables) may use L1.
+//
 // Every QuantizedLinear keeps the reference's quantized arithmetic exactly:
 // the row of activations is quantized per row (absmax / 127, round half away
 // from zero), dotted in int32 against the INT8/INT4 column codes and rescaled
@@ -43,8 +51,9 @@ namespace zq {
 namespace lm {
 
 constexpr int kThreads = 256;
-constexpr int kAttnThreads = 128;
+constexpr int kAttnThreads = 256;
 constexpr int kMaxHeadDim = 128;
+constexpr int kAttnChunk = 64;  // positions per attention block
 
 // Position state in device memory: the step kernels read it, the argmax
 // kernel advances it, so one captured step serves every position.
@@ -114,10 +123,12 @@ __device__ __forceinline__ float gelu_ref(float x) {
 __global__ void embed_kernel(const uint8_t* __restrict__ panel, int type, int Kp, const float* __restrict__ scales,
                              int hidden, const int32_t* __restrict__ tokens, const State* __restrict__ st,
                              const float* __restrict__ pe, float* __restrict__ h) {
+    pdl_launch_dependents();
+    pdl_wait_primary();
     const int j = blockIdx.x * blockDim.x + threadIdx.x;
     if (j >= hidden) return;
-    const int pos = st->pos;
-    const int tok = tokens[pos];
+    const int pos = __ldcg(&st->pos);
+    const int tok = __ldcg(tokens + pos);
     int code;
     if (type == kInt8) {
         code = (int8_t)panel[(size_t)j * Kp + tok];
@@ -154,9 +165,28 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const float* __restric
     float* xs = lsm;                                          // [Kp] fp32 (normalised) activations
     int8_t* qs = reinterpret_cast<int8_t*>(lsm + Kp);         // [Kp] codes
     __shared__ float red[32];
-    if (skip_prefill && st->pos + 1 < st->prompt_len) return;
+    constexpr int kPre = 4;  // 16-byte weight chunks per lane fetched before the dependency wait
+    const int lane = threadIdx.x & 31;
+    const int warps_total = gridDim.x * (kThreads / 32);
+    const size_t cb = kType == kInt8 ? (size_t)Kp : (size_t)(Kp >> 1);
+    const int chunks = (int)(cb >> 4);
+    const int first_col = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
 
-    for (int i = threadIdx.x; i < Kp; i += kThreads) xs[i] = i < K ? x[i] : 0.0f;
+    // Weights do not depend on earlier kernels: start fetching this warp's
+    // first column, then let the next kernel launch, then wait for the
+    // producer of x (programmatic dependent launch).
+    uint4 pre[kPre];
+#pragma unroll
+    for (int u = 0; u < kPre; ++u) {
+        const int c = lane + 32 * u;
+        pre[u] = (first_col < N && c < chunks) ? ld_stream_u4(panel + (size_t)first_col * cb + (size_t)c * 16)
+                                               : make_uint4(0, 0, 0, 0);
+    }
+    pdl_launch_dependents();
+    pdl_wait_primary();
+    if (skip_prefill && __ldcg(&st->pos) + 1 < __ldcg(&st->prompt_len)) return;
+
+    for (int i = threadIdx.x; i < Kp; i += kThreads) xs[i] = i < K ? __ldcg(x + i) : 0.0f;
     __syncthreads();
     if (kPro == kProRms) {
         float ss = 0.0f;
@@ -199,14 +229,22 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const float* __restric
     }
     __syncthreads();
 
-    const int lane = threadIdx.x & 31;
-    const int warps_total = gridDim.x * (kThreads / 32);
-    const size_t cb = kType == kInt8 ? (size_t)Kp : (size_t)(Kp >> 1);
-    const int chunks = (int)(cb >> 4);
-    for (int col = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); col < N; col += warps_total) {
+    for (int col = first_col; col < N; col += warps_total) {
         const uint8_t* wc = panel + (size_t)col * cb;
+        const bool have_pre = col == first_col;
         int acc[1] = {0};
-        for (int c = lane; c < chunks; c += 32) {
+#pragma unroll
+        for (int u = 0; u < kPre; ++u) {
+            const int c = lane + 32 * u;
+            if (c < chunks) {
+                const uint4 w = have_pre ? pre[u] : ld_stream_u4(wc + (size_t)c * 16);
+                if (kType == kInt8)
+                    dot16_int8<1>(w, qs, Kp, c * 16, acc);
+                else
+                    dot16_int4<1>(w, qs, Kp, c * 32, acc);
+            }
+        }
+        for (int c = lane + 32 * kPre; c < chunks; c += 32) {
             const uint4 w = ld_stream_u4(wc + (size_t)c * 16);
             if (kType == kInt8)
                 dot16_int8<1>(w, qs, Kp, c * 16, acc);
@@ -220,38 +258,53 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const float* __restric
             if (bias) v = x86_add(v, bias[col]);
             if (kEpi == kEpiStore) y[col] = v;
             else if (kEpi == kEpiGelu) y[col] = gelu_ref(v);
-            else y[col] = x86_add(y[col], v);
+            else y[col] = x86_add(__ldcg(y + col), v);
         }
     }
 }
 
 // ---------------------------------------------------------------------------
-// Attention for the newest row, one block per query head (forward_block
-// 424-451 restricted to the last query, which is all the next token needs):
-// RoPE on q and on the new key with the reference's cos/sin factors
-// (apply_rope 347-384, precomputed on the host with the same float formula),
-// append k/v to the cache (written once per KV head), scores = (q . k_j) *
-// 1/sqrt(head_dim) for j <= pos, softmax (44-64), context = sum_j p_j v_j.
-// GQA: query head h reads KV head h / (heads / kv_heads) (repeat_kv_heads
-// 386-410).
+// Attention for the newest row (forward_block 424-451 restricted to the last
+// query, which is all the next token needs): RoPE on q and on the new key
+// with the reference's cos/sin factors (apply_rope 347-384, precomputed on the
+// host with the same float formula), append k/v to the cache, scores =
+// (q . k_j) * 1/sqrt(head_dim) for j <= pos, softmax (44-64), context =
+// sum_j p_j v_j.  GQA: query head h reads KV head h / (heads / kv_heads)
+// (repeat_kv_heads 386-410).
+//
+// Split over positions: block (h, s) takes a contiguous chunk of at most
+// kAttnChunk positions (one thread per position, 128-bit key loads), keeps a
+// local max m_s, sum l_s and context c_s, and writes them to `part`.  The
+// block that finishes last for head h (threadfence + atomic ticket; nothing
+// waits) merges the chunks: M = max m_s, L = sum l_s e^(m_s - M),
+// context = (sum c_s e^(m_s - M)) / L, and resets the ticket.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const float* __restrict__ qkv, int heads,
                                                                  int kv_heads, int hd, float* kc, float* vc,
                                                                  int max_seq, const float* __restrict__ rcos,
                                                                  const float* __restrict__ rsin,
                                                                  const State* __restrict__ st, float scale,
+                                                                 float* part, unsigned int* tickets,
                                                                  float* __restrict__ ctx) {
-    extern __shared__ float asm_[];
-    float* q = asm_;                 // [hd]
-    float* kn = q + kMaxHeadDim;     // [hd]
-    float* vn = kn + kMaxHeadDim;    // [hd]
-    float* sc = vn + kMaxHeadDim;    // [max_seq]
+    constexpr int kWarps = kAttnThreads / 32;
+    constexpr int kPerLane = kMaxHeadDim / 32;
+    __shared__ __align__(16) float q[kMaxHeadDim];
+    __shared__ __align__(16) float kn[kMaxHeadDim];
+    __shared__ __align__(16) float vn[kMaxHeadDim];
+    __shared__ float p_sh[kAttnChunk];
+    __shared__ float wpart[kWarps][kMaxHeadDim];
     __shared__ float red[32];
+    __shared__ int is_last;
+    pdl_launch_dependents();
+    pdl_wait_primary();
     const int h = blockIdx.x;
+    const int split = blockIdx.y;
+    const int nsplit = gridDim.y;
     const int rep = heads / kv_heads;
     const int kvh = h / rep;
-    const int pos = st->pos;
+    const int pos = __ldcg(&st->pos);
     const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
     const float* qsrc = qkv + (size_t)h * hd;
     const float* ksrc = qkv + (size_t)heads * hd + (size_t)kvh * hd;
     const float* vsrc = qkv + (size_t)(heads + kv_heads) * hd + (size_t)kvh * hd;
@@ -260,54 +313,113 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const float* __
         if (tid < half) {
             const float c = rcos[(size_t)pos * half + tid];
             const float sn = rsin[(size_t)pos * half + tid];
-            const float qe = qsrc[2 * tid], qo = qsrc[2 * tid + 1];
+            const float qe = __ldcg(qsrc + 2 * tid), qo = __ldcg(qsrc + 2 * tid + 1);
             q[2 * tid] = __fsub_rn(__fmul_rn(qe, c), __fmul_rn(qo, sn));
             q[2 * tid + 1] = __fadd_rn(__fmul_rn(qe, sn), __fmul_rn(qo, c));
-            const float ke = ksrc[2 * tid], ko = ksrc[2 * tid + 1];
+            const float ke = __ldcg(ksrc + 2 * tid), ko = __ldcg(ksrc + 2 * tid + 1);
             kn[2 * tid] = __fsub_rn(__fmul_rn(ke, c), __fmul_rn(ko, sn));
             kn[2 * tid + 1] = __fadd_rn(__fmul_rn(ke, sn), __fmul_rn(ko, c));
         }
     } else if (tid < hd) {
-        q[tid] = qsrc[tid];
-        kn[tid] = ksrc[tid];
+        q[tid] = __ldcg(qsrc + tid);
+        kn[tid] = __ldcg(ksrc + tid);
     }
-    if (tid < hd) vn[tid] = vsrc[tid];
+    if (tid < hd) vn[tid] = __ldcg(vsrc + tid);
     __syncthreads();
     float* kc_head = kc + (size_t)kvh * max_seq * hd;
     float* vc_head = vc + (size_t)kvh * max_seq * hd;
-    if (h % rep == 0 && tid < hd) {
+    if (h % rep == 0 && split == 0 && tid < hd) {
         kc_head[(size_t)pos * hd + tid] = kn[tid];
         vc_head[(size_t)pos * hd + tid] = vn[tid];
     }
 
-    float mx = -INFINITY;
-    for (int j = tid; j <= pos; j += kAttnThreads) {
-        const float* kj = j == pos ? kn : kc_head + (size_t)j * hd;
-        float dot = 0.0f;
-        for (int d = 0; d < hd; ++d) dot = __fadd_rn(dot, __fmul_rn(q[d], kj[d]));
-        const float v = __fmul_rn(dot, scale);
-        sc[j] = v;
-        mx = fmaxf(mx, v);
-    }
-    mx = block_max<kAttnThreads>(mx, red);
-    float sum = 0.0f;
-    for (int j = tid; j <= pos; j += kAttnThreads) {
-        const float e = expf(__fsub_rn(sc[j], mx));
-        sc[j] = e;
-        sum = __fadd_rn(sum, e);
-    }
-    sum = block_sum<kAttnThreads>(sum, red);
-    const float inv = sum > 0.0f ? __fdiv_rn(1.0f, sum) : 0.0f;
-    for (int j = tid; j <= pos; j += kAttnThreads) sc[j] = __fmul_rn(sc[j], inv);
-    __syncthreads();
-    if (tid < hd) {
-        float acc = 0.0f;
-        for (int j = 0; j <= pos; ++j) {
-            const float vj = j == pos ? vn[tid] : vc_head[(size_t)j * hd + tid];
-            acc = __fadd_rn(acc, __fmul_rn(sc[j], vj));
+    const int total = pos + 1;
+    const int chunk = (total + nsplit - 1) / nsplit;  // <= kAttnChunk by the launch's choice of nsplit
+    const int begin = split * chunk;
+    const int end = min(begin + chunk, total);
+    const int n = end > begin ? end - begin : 0;
+
+    // scores, one thread per position
+    float v = -INFINITY;
+    if (tid < n) {
+        const int j = begin + tid;
+        float d = 0.0f;
+        if (j == pos) {  // the new key, in shared memory
+            for (int i = 0; i < hd; ++i) d = __fadd_rn(d, __fmul_rn(q[i], kn[i]));
+        } else {
+            const float* kj = kc_head + (size_t)j * hd;  // global (KV cache)
+            if ((hd & 3) == 0) {  // rows start on 16-byte boundaries
+                for (int i = 0; i < hd; i += 4) {
+                    const float4 k4 = __ldcg(reinterpret_cast<const float4*>(kj + i));
+                    d = __fadd_rn(d, __fmul_rn(q[i], k4.x));
+                    d = __fadd_rn(d, __fmul_rn(q[i + 1], k4.y));
+                    d = __fadd_rn(d, __fmul_rn(q[i + 2], k4.z));
+                    d = __fadd_rn(d, __fmul_rn(q[i + 3], k4.w));
+                }
+            } else {
+                for (int i = 0; i < hd; ++i) d = __fadd_rn(d, __fmul_rn(q[i], __ldcg(kj + i)));
+            }
         }
-        ctx[(size_t)h * hd + tid] = acc;
+        v = __fmul_rn(d, scale);
     }
+    const float m_s = block_max<kAttnThreads>(v, red);
+    const float e = tid < n ? expf(__fsub_rn(v, m_s)) : 0.0f;
+    if (tid < kAttnChunk) p_sh[tid] = e;
+    const float l_s = block_sum<kAttnThreads>(e, red);  // also orders the p_sh writes
+
+    // chunk context: warps over positions, lanes over the head dimension
+    float acc[kPerLane];
+#pragma unroll
+    for (int r = 0; r < kPerLane; ++r) acc[r] = 0.0f;
+    for (int t = warp; t < n; t += kWarps) {
+        const int j = begin + t;
+        const float p = p_sh[t];
+        const float* vj = vc_head + (size_t)j * hd;  // global unless j == pos
+#pragma unroll
+        for (int r = 0; r < kPerLane; ++r) {
+            const int i = lane + 32 * r;
+            if (i < hd) acc[r] = __fadd_rn(acc[r], __fmul_rn(p, j == pos ? vn[i] : __ldcg(vj + i)));
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < kPerLane; ++r) {
+        const int i = lane + 32 * r;
+        if (i < hd) wpart[warp][i] = acc[r];
+    }
+    __syncthreads();
+    float* mine = part + ((size_t)h * nsplit + split) * (kMaxHeadDim + 2);
+    if (tid < hd) {
+        float c = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) c = __fadd_rn(c, wpart[w][tid]);
+        mine[2 + tid] = c;
+    }
+    if (tid == 0) {
+        mine[0] = m_s;
+        mine[1] = l_s;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) is_last = atomicAdd(tickets + h, 1u) == (unsigned)(nsplit - 1);
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    const float* hp = part + (size_t)h * nsplit * (kMaxHeadDim + 2);
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < nsplit; ++s2) M = fmaxf(M, __ldcg(hp + (size_t)s2 * (kMaxHeadDim + 2)));
+    float L = 0.0f;
+    float c = 0.0f;
+    for (int s2 = 0; s2 < nsplit; ++s2) {
+        const float* ps = hp + (size_t)s2 * (kMaxHeadDim + 2);
+        const float ls = __ldcg(ps + 1);
+        if (ls == 0.0f) continue;  // empty chunk
+        const float f = expf(__fsub_rn(__ldcg(ps), M));
+        L = __fadd_rn(L, __fmul_rn(ls, f));
+        if (tid < hd) c = __fadd_rn(c, __fmul_rn(__ldcg(ps + 2 + tid), f));
+    }
+    const float inv = L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f;
+    if (tid < hd) ctx[(size_t)h * hd + tid] = __fmul_rn(c, inv);
+    if (tid == 0) tickets[h] = 0u;
 }
 
 // ---------------------------------------------------------------------------
@@ -321,8 +433,10 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
     __shared__ float bv[32];
     __shared__ int bi[32];
     __shared__ int bnan[32];
-    const int pos = st->pos;
-    if (pos + 1 < st->prompt_len) {
+    pdl_launch_dependents();
+    pdl_wait_primary();
+    const int pos = __ldcg(&st->pos);
+    if (pos + 1 < __ldcg(&st->prompt_len)) {
         __syncthreads();
         if (threadIdx.x == 0) st->pos = pos + 1;
         return;
@@ -331,7 +445,7 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
     int idx = V;
     int nan = 0;
     for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        const float v = logits[i];
+        const float v = __ldcg(logits + i);
         if (isnan(v)) nan = 1;
         else if (v > best || (v == best && i < idx)) best = v, idx = i;
     }
@@ -525,6 +639,9 @@ struct zq_lm {
     float *h = nullptr, *qkv = nullptr, *ctx = nullptr, *ff = nullptr, *logits = nullptr;
     float *kc = nullptr, *vc = nullptr;
     float *rcos = nullptr, *rsin = nullptr;
+    float* attn_part = nullptr;          // [heads][splits][128 + 2] chunk partials
+    unsigned int* attn_tickets = nullptr;  // [heads], zero between launches
+    int attn_splits = 1;
     int32_t* tokens = nullptr;
     State* state = nullptr;
     std::vector<void*> allocations;
@@ -595,6 +712,27 @@ zq_status make_weight(const zq::ZyqRecord& r, void* stream, zq_weight** out) {
 
 size_t linear_smem(int Kp) { return (size_t)Kp * sizeof(float) + (size_t)Kp; }
 
+// Every decode-step kernel is launched with programmatic dependent launch:
+// it may start (and prefetch constant weights) while its predecessor runs,
+// and waits in griddepcontrol.wait before reading anything the predecessor
+// writes.
+template <class... Params, class... Args>
+cudaError_t launch_pdl(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<Params>(args)...);
+}
+
+
+
 constexpr size_t kMaxLinearSmem = 200 * 1024;
 
 template <int kType, int kPro, int kEpi>
@@ -635,9 +773,8 @@ cudaError_t launch_linear_t(const float* x, const float* nw, const float* nb, fl
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     int blocks = (int)((w->N + 7) / 8);
     if (blocks > 2 * sms) blocks = 2 * sms;
-    kern<<<blocks, zq::lm::kThreads, smem, s>>>(x, (int)w->K, w->Kp, nw, nb, eps, w->panel, w->scales, (int)w->N,
-                                                bias, y, st, skip_prefill);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3(blocks), dim3(zq::lm::kThreads), smem, s, x, (int)w->K, w->Kp, nw, nb, eps,
+                      (const uint8_t*)w->panel, (const float*)w->scales, (int)w->N, bias, y, st, skip_prefill);
 }
 
 template <int kPro, int kEpi>
@@ -662,22 +799,21 @@ cudaError_t enqueue_step(zq_lm* lm, cudaStream_t s) {
     const int kvh = (int)(c.num_kv_heads == 0 ? c.num_heads : c.num_kv_heads);
     const float eps = c.norm_eps;
     const int hidden = (int)c.hidden_size;
-    zq::lm::embed_kernel<<<(hidden + 255) / 256, 256, 0, s>>>(lm->emb->panel, lm->emb->type, lm->emb->Kp,
-                                                            lm->emb->scales, hidden, lm->tokens, lm->state, lm->pe,
-                                                            lm->h);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(zq::lm::embed_kernel, dim3((hidden + 255) / 256), dim3(256), 0, s,
+                               (const uint8_t*)lm->emb->panel, lm->emb->type, lm->emb->Kp,
+                               (const float*)lm->emb->scales, hidden, (const int32_t*)lm->tokens,
+                               (const State*)lm->state, (const float*)lm->pe, lm->h);
     const size_t cache_layer = (size_t)kvh * c.max_sequence_length * hd;
     const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
-    const size_t attn_smem = (3 * zq::lm::kMaxHeadDim + c.max_sequence_length) * sizeof(float);
     for (size_t li = 0; li < lm->layers.size() && e == cudaSuccess; ++li) {
         const DevLayer& L = lm->layers[li];
         e = launch_normed<zq::lm::kEpiStore>(L.rms1, lm->h, L.n1w, L.n1b, eps, L.qkv, L.b_qkv, lm->qkv, lm->state, 0, s);
         if (e != cudaSuccess) break;
-        zq::lm::attention_kernel<<<(int)c.num_heads, zq::lm::kAttnThreads, attn_smem, s>>>(
-            lm->qkv, (int)c.num_heads, kvh, hd, lm->kc + li * cache_layer, lm->vc + li * cache_layer,
-            (int)c.max_sequence_length, c.use_rope ? lm->rcos : nullptr, c.use_rope ? lm->rsin : nullptr, lm->state,
-            scale, lm->ctx);
-        e = cudaGetLastError();
+        e = launch_pdl(zq::lm::attention_kernel, dim3((unsigned)c.num_heads, (unsigned)lm->attn_splits),
+                       dim3(zq::lm::kAttnThreads), 0, s, (const float*)lm->qkv, (int)c.num_heads, kvh, hd,
+                       lm->kc + li * cache_layer, lm->vc + li * cache_layer, (int)c.max_sequence_length,
+                       (const float*)(c.use_rope ? lm->rcos : nullptr), (const float*)(c.use_rope ? lm->rsin : nullptr),
+                       (const State*)lm->state, scale, lm->attn_part, lm->attn_tickets, lm->ctx);
         if (e != cudaSuccess) break;
         e = launch_linear<zq::lm::kProNone, zq::lm::kEpiResidual>(lm->ctx, nullptr, nullptr, eps, L.out, L.b_out, lm->h,
                                                                   lm->state, 0, s);
@@ -692,8 +828,8 @@ cudaError_t enqueue_step(zq_lm* lm, cudaStream_t s) {
     e = launch_linear<zq::lm::kProRms, zq::lm::kEpiStore>(lm->h, lm->final_w, nullptr, eps, lm->head, lm->b_head,
                                                           lm->logits, lm->state, 1, s);
     if (e != cudaSuccess) return e;
-    zq::lm::argmax_kernel<<<1, 1024, 0, s>>>(lm->logits, (int)c.vocab_size, lm->tokens, lm->state);
-    return cudaGetLastError();
+    return launch_pdl(zq::lm::argmax_kernel, dim3(1), dim3(1024), 0, s, (const float*)lm->logits, (int)c.vocab_size,
+                      lm->tokens, lm->state);
 }
 
 cudaError_t build_graph(zq_lm* lm, int steps, cudaGraphExec_t* out, cudaStream_t s) {
@@ -784,8 +920,6 @@ zq_status zq_lm_load(const void* bytes, size_t len, void* stream, zq_lm** out) {
     const size_t hd = H / c.num_heads;
     auto bad = [](const char* what) { return fail_lm(ZQ_ERR_INVALID_ARGUMENT, std::string("zyron_b200: ") + what); };
     if (hd > (size_t)zq::lm::kMaxHeadDim) return bad("head dimension above 128 is not supported on the device");
-    if ((3 * zq::lm::kMaxHeadDim + c.max_sequence_length) * sizeof(float) > 200 * 1024)
-        return bad("max_sequence_length above 50000 is not supported on the device");
     if (linear_smem(zq::padded_k(type, (int)std::max(H, F))) > kMaxLinearSmem)
         return bad("hidden or intermediate size too large for the device decode kernels");
     if (emb.rows != V || emb.cols != H) return bad("token embedding shape does not match the config");
@@ -887,6 +1021,11 @@ zq_status zq_lm_load(const void* bytes, size_t len, void* stream, zq_lm** out) {
     if (e == cudaSuccess) e = dev_alloc(lm, &lm->logits, V);
     if (e == cudaSuccess) e = dev_alloc(lm, &lm->kc, c.num_layers * kvh * T * hd);
     if (e == cudaSuccess) e = dev_alloc(lm, &lm->vc, c.num_layers * kvh * T * hd);
+    lm->attn_splits = (int)((T + zq::lm::kAttnChunk - 1) / zq::lm::kAttnChunk);
+    if (e == cudaSuccess)
+        e = dev_alloc(lm, &lm->attn_part, c.num_heads * (size_t)lm->attn_splits * (zq::lm::kMaxHeadDim + 2));
+    if (e == cudaSuccess) e = dev_alloc(lm, &lm->attn_tickets, c.num_heads);
+    if (e == cudaSuccess) e = cudaMemsetAsync(lm->attn_tickets, 0, c.num_heads * sizeof(unsigned int), st);
     if (e == cudaSuccess) e = dev_alloc(lm, &lm->tokens, T + 2);
     if (e == cudaSuccess) e = dev_alloc(lm, &lm->state, 1);
     if (e == cudaSuccess && c.use_rope) {

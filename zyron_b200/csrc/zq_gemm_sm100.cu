@@ -30,6 +30,9 @@
 
 #include <cuda.h>
 
+#include <mutex>
+#include <unordered_map>
+
 namespace zq {
 
 namespace {
@@ -321,11 +324,9 @@ template <int BN, int STAGES>
 cudaError_t launch_gemm_t(const GemmArgs& a, cudaStream_t stream, bool pdl) {
     using S = Smem<BN, STAGES>;
     auto kern = gemm_i8_kernel<BN, STAGES>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
+    cudaError_t e = ensure_smem_attr(kern, S::kTotal);
     if (e != cudaSuccess) return e;
-    int dev = 0, sms = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int sms = sm_count();
     const int tiles = ((a.M + kBM - 1) / kBM) * ((a.N + BN - 1) / BN);
     const int grid = tiles < sms ? tiles : sms;
 
@@ -347,6 +348,30 @@ cudaError_t launch_gemm_t(const GemmArgs& a, cudaStream_t stream, bool pdl) {
 }
 
 }  // namespace
+
+cudaError_t ensure_smem_attr_ptr(const void* kern, size_t bytes) {
+    static std::mutex mu;
+    static std::unordered_map<const void*, size_t> done;
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = done.find(kern);
+    if (it != done.end() && it->second >= bytes) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) done[kern] = bytes;
+    return e;
+}
+
+int sm_count() {
+    static int cached[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (!cached[dev]) {
+        int sms = 0;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cached[dev] = sms > 0 ? sms : 148;
+    }
+    return cached[dev];
+}
 
 int gemm_block_n(int M, int N) {
     // Wide tiles when there are enough of them to fill the GPU; narrower

@@ -24,9 +24,74 @@ namespace zq {
 namespace {
 
 constexpr int kGemvThreads = 256;
-constexpr int kUnroll = 4;  // 16-byte weight chunks in flight per lane
+constexpr int kUnroll = 4;  // 16-byte weight chunks in flight per lane per column
 
-template <int kType, int kM>
+// One group of kCols columns for one warp: dp4a over all chunks (kUnroll
+// 16-byte loads per lane per column in flight), warp-shuffle reduction, exact
+// epilogue.
+template <int kType, int kM, int kCols>
+__device__ __forceinline__ void gemv_group(int g, const uint8_t* __restrict__ panel,
+                                           int N, int Kp, size_t col_bytes, int chunks, const int8_t* __restrict__ sq,
+                                           const float* __restrict__ col_scale, const float (&srow)[kM],
+                                           const float* __restrict__ bias, float* __restrict__ y, int M, int lane) {
+    const int col0 = g * kCols;
+    int acc[kCols][kM];
+#pragma unroll
+    for (int c = 0; c < kCols; ++c)
+#pragma unroll
+        for (int m = 0; m < kM; ++m) acc[c][m] = 0;
+
+    for (int base = lane; base < chunks; base += 32 * kUnroll) {
+        uint4 w[kCols][kUnroll];
+#pragma unroll
+        for (int c = 0; c < kCols; ++c) {
+            const uint8_t* wc = panel + (size_t)min(col0 + c, N - 1) * col_bytes;
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int ch = base + 32 * u;
+                w[c][u] = ch < chunks ? ld_stream_u4(wc + (size_t)ch * 16) : make_uint4(0, 0, 0, 0);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int ch = base + 32 * u;
+            if (ch < chunks) {
+#pragma unroll
+                for (int c = 0; c < kCols; ++c) {
+                    if (kType == kInt8)
+                        dot16_int8<kM>(w[c][u], sq, Kp, ch * 16, acc[c]);
+                    else
+                        dot16_int4<kM>(w[c][u], sq, Kp, ch * 32, acc[c]);
+                }
+            }
+        }
+    }
+
+#pragma unroll
+    for (int c = 0; c < kCols; ++c) {
+#pragma unroll
+        for (int m = 0; m < kM; ++m) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc[c][m] += __shfl_xor_sync(0xffffffffu, acc[c][m], o);
+        }
+        const int col = col0 + c;
+        if (col < N) {
+            const float sc = __ldg(col_scale + col);
+            const float b = bias ? __ldg(bias + col) : 0.0f;
+#pragma unroll
+            for (int m = 0; m < kM; ++m) {
+                if (lane == m && m < M) {
+                    y[(size_t)m * N + col] = bias ? zq_epilogue_bias(acc[c][m], srow[m], sc, b)
+                                                  : zq_epilogue(acc[c][m], srow[m], sc);
+                }
+            }
+        }
+    }
+}
+
+// kCols columns per warp iteration: each shared-memory activation read feeds
+// kCols columns' dp4a (M >= 4 is dp4a/LDS-heavy; M <= 2 is purely HBM-bound).
+template <int kType, int kM, int kCols>
 __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const uint8_t* __restrict__ panel, int N, int Kp,
                                                             const float* __restrict__ col_scale,
                                                             const int8_t* __restrict__ q,
@@ -38,12 +103,18 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const uint8_t* __res
     const int warp_global = (blockIdx.x * kGemvThreads + threadIdx.x) >> 5;
     const int warps_total = (gridDim.x * kGemvThreads) >> 5;
     const size_t col_bytes = kType == kInt8 ? (size_t)Kp : (size_t)(Kp >> 1);
+    const int groups = (N + kCols - 1) / kCols;
 
-    // Warm L2 with this warp's first column while the quantizer finishes.
-    if (warp_global < N) {
-        const uint8_t* c0 = panel + (size_t)warp_global * col_bytes;
-        for (size_t off = (size_t)lane * 128; off < col_bytes; off += 32 * 128)
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(c0 + off));
+    const int chunks = (int)(col_bytes >> 4);  // 16-byte chunks per column
+    // Warm L2 with this warp's first columns while the quantizer finishes.
+    if (warp_global < groups) {
+        for (int c = 0; c < kCols; ++c) {
+            const int col = warp_global * kCols + c;
+            if (col >= N) break;
+            const uint8_t* c0 = panel + (size_t)col * col_bytes;
+            for (size_t off = (size_t)lane * 128; off < col_bytes; off += 32 * 128)
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(c0 + off));
+        }
     }
     pdl_wait_primary();
 
@@ -77,67 +148,26 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const uint8_t* __res
 #pragma unroll
     for (int m = 0; m < kM; ++m) srow[m] = m < M ? row_scale[m] : 0.0f;
 
-    for (int col = warp_global; col < N; col += warps_total) {
-        const uint8_t* wc = panel + (size_t)col * col_bytes;
-        int acc[kM];
-#pragma unroll
-        for (int m = 0; m < kM; ++m) acc[m] = 0;
-
-        const int chunks = (int)(col_bytes >> 4);  // 16-byte chunks in the column
-        int c = lane;
-        for (; c + 32 * (kUnroll - 1) < chunks; c += 32 * kUnroll) {
-            uint4 w[kUnroll];
-#pragma unroll
-            for (int u = 0; u < kUnroll; ++u) w[u] = ld_stream_u4(wc + (size_t)(c + 32 * u) * 16);
-#pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
-                if (kType == kInt8)
-                    dot16_int8<kM>(w[u], sq, Kp, (c + 32 * u) * 16, acc);
-                else
-                    dot16_int4<kM>(w[u], sq, Kp, (c + 32 * u) * 32, acc);
-            }
-        }
-        for (; c < chunks; c += 32) {
-            const uint4 w = ld_stream_u4(wc + (size_t)c * 16);
-            if (kType == kInt8)
-                dot16_int8<kM>(w, sq, Kp, c * 16, acc);
-            else
-                dot16_int4<kM>(w, sq, Kp, c * 32, acc);
-        }
-
-#pragma unroll
-        for (int m = 0; m < kM; ++m) {
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
-        }
-        const float sc = __ldg(col_scale + col);
-        const float b = bias ? __ldg(bias + col) : 0.0f;
-#pragma unroll
-        for (int m = 0; m < kM; ++m) {
-            if (lane == m && m < M) {
-                y[(size_t)m * N + col] = bias ? zq_epilogue_bias(acc[m], srow[m], sc, b)
-                                              : zq_epilogue(acc[m], srow[m], sc);
-            }
-        }
-    }
+    for (int g = warp_global; g < groups; g += warps_total)
+        gemv_group<kType, kM, kCols>(g, panel, N, Kp, col_bytes, chunks, sq, col_scale, srow, bias, y, M, lane);
 }
 
-template <int kType, int kM>
+template <int kType, int kM, int kCols>
 cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
     const size_t smem = (size_t)kM * a.Kp;
-    auto kern = gemv_kernel<kType, kM>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    auto kern = gemv_kernel<kType, kM, kCols>;
+    cudaError_t e = ensure_smem_attr(kern, smem);
     if (e != cudaSuccess) return e;
-    int dev = 0, sms = 0, per_sm = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int sms = sm_count();
+    int per_sm = 0;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGemvThreads, smem);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
-    const int warps_needed = a.N;
-    int blocks = sms * per_sm;
-    const int blocks_needed = (warps_needed + (kGemvThreads / 32) - 1) / (kGemvThreads / 32);
-    if (blocks > blocks_needed) blocks = blocks_needed;
+    // As many resident warps as occupancy allows: under load the HBM needs
+    // many loads in flight per SM, and warps are what carry them.
+    const int groups = (a.N + kCols - 1) / kCols;
+    const int needed = (groups + kGemvThreads / 32 - 1) / (kGemvThreads / 32);
+    const int blocks = sms * per_sm < needed ? sms * per_sm : needed;
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(blocks);
@@ -156,11 +186,11 @@ cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
 template <int kType>
 cudaError_t dispatch_m(const GemvArgs& a, cudaStream_t stream, bool pdl) {
     switch (a.M) {
-        case 1: return launch_gemv_t<kType, 1>(a, stream, pdl);
-        case 2: return launch_gemv_t<kType, 2>(a, stream, pdl);
+        case 1: return launch_gemv_t<kType, 1, 1>(a, stream, pdl);
+        case 2: return launch_gemv_t<kType, 2, 1>(a, stream, pdl);
         case 3:
-        case 4: return launch_gemv_t<kType, 4>(a, stream, pdl);
-        default: return launch_gemv_t<kType, 8>(a, stream, pdl);
+        case 4: return launch_gemv_t<kType, 4, 2>(a, stream, pdl);
+        default: return launch_gemv_t<kType, 8, 2>(a, stream, pdl);
     }
 }
 

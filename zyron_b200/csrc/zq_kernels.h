@@ -59,6 +59,18 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl);
 
 int gemm_block_n(int M, int N);
 
+// Multiprocessor count of the current device (cached per device).
+int sm_count();
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) at most once per kernel
+// (keyed by the kernel's address) and size: host-side launch overhead matters
+// for microsecond kernels.
+cudaError_t ensure_smem_attr_ptr(const void* kern, size_t bytes);
+template <class K>
+cudaError_t ensure_smem_attr(K kern, size_t bytes) {
+    return ensure_smem_attr_ptr(reinterpret_cast<const void*>(kern), bytes);
+}
+
 // zq_matmul with caller-supplied scratch (validated here: 256-byte aligned and
 // at least zq_matmul_workspace_bytes(w, m) bytes).  Defined in zq_api.cu.
 zq_status matmul_with_scratch(const zq_weight* w, const float* x, size_t m, const float* bias, float* y,

@@ -175,3 +175,20 @@ def test_slice_cols_and_odd_k_int4_roundtrip(zb):
         full = zb.matmul(torch.from_numpy(x).cuda(), W).cpu().numpy()
         part = zb.matmul(torch.from_numpy(x).cuda(), S).cpu().numpy()
         assert_bits_equal(part, full[:, 2:N - 1], "column shard")
+
+
+@pytest.mark.parametrize("qt", [1, 2])
+@pytest.mark.parametrize("M,K,N", [(2048, 256, 4864), (2000, 200, 4900)])
+def test_pair_tile_gemm_bit_exact(zb, qt, M, K, N):
+    """Shapes with >= 148 tiles of 256 x 256 select the 2-SM (cluster pair)
+    GEMM; the second one is ragged in M, K and N."""
+    import torch
+
+    rng = np.random.default_rng(M + N + qt)
+    x, w = make(rng, M, K, N)
+    pay, sc = O.quantize_weights(w, qt)
+    W = zb.QuantizedMatrix.from_parts(qt, K, N, sc, pay)
+    b = rng.standard_normal(N).astype(np.float32)
+    y = zb.matmul(torch.from_numpy(x).cuda(), W, bias=torch.from_numpy(b).cuda()).cpu().numpy()
+    assert_bits_equal(y, O.matmul(x, qt, pay, sc, N, b)[3], f"pair gemm t{qt} {M}x{K}x{N}")
+    assert zb.device_error() == 0

@@ -207,7 +207,13 @@ int gemm_group_m() {
     return g;
 }
 
-int tile_index(int block_n) { return block_n == 256 ? 2 : (block_n == 128 ? 1 : 0); }
+int tile_index(int block_n) {
+    return block_n == zq::kPairBlockN ? 3 : (block_n == 256 ? 2 : (block_n == 128 ? 1 : 0));
+}
+
+// Rows of the weight box one CTA loads: the 2-SM kernel splits its 256 tile
+// columns between the two CTAs of a pair.
+int box_rows_b(int block_n) { return block_n == zq::kPairBlockN ? 128 : block_n; }
 
 // Per-thread device buffers of zq_matmul_host.
 struct HostStaging {
@@ -486,7 +492,7 @@ zq_status run_codes(const zq_weight* w, const int8_t* codes, const float* rs, si
         std::lock_guard<std::mutex> lk(mw->mu);
         const int ti = tile_index(bn);
         if (!mw->tmap_ready[ti]) {
-            s = encode_kmajor(&mw->tmap_b[ti], w->panel, w->N, Kp, bn);
+            s = encode_kmajor(&mw->tmap_b[ti], w->panel, w->N, Kp, box_rows_b(bn));
             if (s != ZQ_OK) return s;
             mw->tmap_ready[ti] = true;
         }
@@ -494,7 +500,7 @@ zq_status run_codes(const zq_weight* w, const int8_t* codes, const float* rs, si
     } else {
         int8_t* panel8 = reinterpret_cast<int8_t*>(scratch);
         ZQ_CUDA(zq::launch_expand_int4(w->panel, N, Kp, panel8, st));
-        s = encode_kmajor(&tmap_b_local, panel8, w->N, Kp, bn);
+        s = encode_kmajor(&tmap_b_local, panel8, w->N, Kp, box_rows_b(bn));
         if (s != ZQ_OK) return s;
         tmap_b = &tmap_b_local;
         pdl = true;  // the GEMM follows the expand kernel directly

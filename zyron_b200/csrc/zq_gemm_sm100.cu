@@ -347,6 +347,316 @@ cudaError_t launch_gemm_t(const GemmArgs& a, cudaStream_t stream, bool pdl) {
                               a.y, a.err, group_m);
 }
 
+
+// ===========================================================================
+// 2-SM variant for large problems: a cluster of two CTAs on two SMs computes
+// a 256 x 256 output tile with tcgen05.mma.cta_group::2 (M = 256).  Each CTA
+// loads its own 128 activation rows and its own half (128 weight columns) of
+// the tile's B operand, so an SM fills 32 KiB of shared memory per k-block
+// instead of 48 KiB and six stages fit -- more bytes in flight against L2 and
+// DRAM latency, a third less L2 -> SM traffic.  The even CTA (leader) issues
+// the MMAs; its commits arrive on both CTAs' barriers (CTA mask 0b11).  Each
+// CTA's accumulator rows live in its own TMEM, so the epilogue is unchanged.
+// ===========================================================================
+constexpr int kStages2 = 6;
+
+struct Smem2 {
+    static constexpr int kABytes = 128 * kBK;  // this CTA's 128 rows of A
+    static constexpr int kBBytes = 128 * kBK;  // this CTA's 128 rows (columns of W) of B
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kBarrierBytes = 8 * (2 * kStages2 + 4 + 1) + 16;
+    static constexpr int kTotal = 1024 + kStages2 * kStageBytes + kBarrierBytes;
+};
+
+__host__ __device__ constexpr uint32_t make_idesc_i8_m256() {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// TMA load whose completion bytes count on the pair leader's barrier.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* tmap, uint64_t* bar_local, int x, int y) {
+    const uint32_t bar = smem_u32(bar_local) & 0xFEFFFFFFu;  // peer bit cleared: the leader's copy of `bar`
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(tmap), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_i8_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Completion of this thread's MMAs arrives on `bar` in both CTAs of the pair.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"((uint16_t)0x3)
+        : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                        int M, int N, int Kp, const float* __restrict__ row_scale,
+                        const float* __restrict__ col_scale, const float* __restrict__ bias,
+                        float* __restrict__ y, uint32_t* __restrict__ err, int group_m) {
+    using S = Smem2;
+    constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* stage_base = smem;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages2 * S::kStageBytes);
+    uint64_t* full = bars;                       // leader's copy used
+    uint64_t* empty = bars + kStages2;           // both copies used
+    uint64_t* tfull = bars + 2 * kStages2;       // both copies used
+    uint64_t* tempty = bars + 2 * kStages2 + 2;  // leader's copy used
+    uint64_t* mma_done = bars + 2 * kStages2 + 4;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages2 + 5);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int m_tiles = (M + 255) / 256;
+    const int n_tiles = (N + 255) / 256;
+    const int num_tiles = m_tiles * n_tiles;
+    const int k_blocks = (Kp + kBK - 1) / kBK;
+    const int cluster = blockIdx.x >> 1;
+    const int clusters = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages2; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 2 * kEpilogueThreads);  // both CTAs' epilogue threads
+        }
+        mbar_init(mma_done, 1);
+        fence_mbar_init();
+        tma_prefetch_desc(&tmap_a);
+        tma_prefetch_desc(&tmap_b);
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tmem_fence_before();
+    cluster_sync_all();  // barriers initialised and TMEM allocated in both CTAs
+    tmem_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    pdl_wait_primary();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int issued[kStages2];
+            uint32_t last_phase[kStages2];
+#pragma unroll
+            for (int s = 0; s < kStages2; ++s) issued[s] = 0, last_phase[s] = 0;
+            bool ok = true;
+            for (int t = cluster; t < num_tiles && ok; t += clusters) {
+                int mt, nt;
+                tile_coords(t, m_tiles, n_tiles, group_m, mt, nt);
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, err, kDevErrTimeoutProducer)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* sa = stage_base + stage * S::kStageBytes;
+                    uint8_t* sb = sa + S::kABytes;
+                    // the leader expects both CTAs' bytes on its barrier
+                    if (leader) mbar_arrive_expect_tx(&full[stage], 2 * S::kStageBytes);
+                    tma_load_2d_pair(sa, &tmap_a, &full[stage], kb * kBK, mt * 256 + (int)rank * 128);
+                    tma_load_2d_pair(sb, &tmap_b, &full[stage], kb * kBK, nt * 256 + (int)rank * 128);
+                    issued[stage] = 1;
+                    last_phase[stage] = phase;
+                    if (++stage == kStages2) stage = 0, phase ^= 1u;
+                }
+            }
+            // Drain: the leader can see every copy of the pair complete on its
+            // full barriers; the peer's copies land before the leader's MMAs
+            // release the stage (empty), so the peer waits on empty instead.
+            for (int s = 0; s < kStages2; ++s) {
+                if (!issued[s]) continue;
+                if (leader)
+                    mbar_wait_bounded(&full[s], last_phase[s], err, kDevErrTimeoutDrain);
+                else
+                    mbar_wait_bounded(&empty[s], last_phase[s], err, kDevErrTimeoutDrain);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = make_idesc_i8_m256();
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int t = cluster; t < num_tiles && ok; t += clusters) {
+                if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, err, kDevErrTimeoutMma)) break;
+                tmem_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(acc * 256);
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    if (!mbar_wait_bounded(&full[stage], phase, err, kDevErrTimeoutMma)) {
+                        ok = false;
+                        break;
+                    }
+                    tmem_fence_after();
+                    const uint32_t sa = smem_u32(stage_base + stage * S::kStageBytes);
+                    const uint32_t sb = sa + S::kABytes;
+#pragma unroll
+                    for (int kk = 0; kk < kBK / kUmmaK; ++kk)
+                        umma_i8_pair(d, make_sw128_desc(sa + kk * kUmmaK), make_sw128_desc(sb + kk * kUmmaK), idesc,
+                                     (kb > 0 || kk > 0) ? 1u : 0u);
+                    umma_commit_pair(&empty[stage]);
+                    if (++stage == kStages2) stage = 0, phase ^= 1u;
+                }
+                if (!ok) break;
+                umma_commit_pair(&tfull[acc]);
+                if (++acc == 2) acc = 0, acc_phase ^= 1u;
+            }
+            umma_commit_pair(mma_done);
+            mbar_wait_bounded(mma_done, 0, err, kDevErrTimeoutDrain);
+        } else if (lane == 0) {
+            // peer: its TMEM is written by the leader's MMAs; wait for them to
+            // finish before the final barrier frees TMEM
+            mbar_wait_bounded(mma_done, 0, err, kDevErrTimeoutDrain);
+        }
+    } else {
+        const int quarter = warp & 3;
+        const uint32_t tempty_leader = map_to_rank(&tempty[0], 0);
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        const bool vec_ok = ((N & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15u) == 0);
+        for (int t = cluster; t < num_tiles; t += clusters) {
+            int mt, nt;
+            tile_coords(t, m_tiles, n_tiles, group_m, mt, nt);
+            if (!mbar_wait_bounded(&tfull[acc], acc_phase, err, kDevErrTimeoutEpilogue)) break;
+            tmem_fence_after();
+            const int row = mt * 256 + (int)rank * 128 + quarter * 32 + lane;
+            const bool row_ok = row < M;
+            const float sr = row_ok ? __ldg(row_scale + row) : 0.0f;
+            float* yrow = y + (size_t)(row_ok ? row : 0) * N;
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * 256);
+#pragma unroll 1
+            for (int c = 0; c < 256 / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(taddr + c * 32, r);
+                tmem_ld_wait();
+                const int n0 = nt * 256 + c * 32;
+                if (!row_ok || n0 >= N) continue;
+                const float4* cs4 = reinterpret_cast<const float4*>(col_scale + n0);
+                if (vec_ok && n0 + 32 <= N) {
+                    const float4* b4 = bias ? reinterpret_cast<const float4*>(bias + n0) : nullptr;
+                    float4* dst = reinterpret_cast<float4*>(yrow + n0);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float4 s4 = __ldg(cs4 + j);
+                        float4 o;
+                        if (b4) {
+                            const float4 b = __ldg(b4 + j);
+                            o.x = zq_epilogue_bias((int32_t)r[4 * j + 0], sr, s4.x, b.x);
+                            o.y = zq_epilogue_bias((int32_t)r[4 * j + 1], sr, s4.y, b.y);
+                            o.z = zq_epilogue_bias((int32_t)r[4 * j + 2], sr, s4.z, b.z);
+                            o.w = zq_epilogue_bias((int32_t)r[4 * j + 3], sr, s4.w, b.w);
+                        } else {
+                            o.x = zq_epilogue((int32_t)r[4 * j + 0], sr, s4.x);
+                            o.y = zq_epilogue((int32_t)r[4 * j + 1], sr, s4.y);
+                            o.z = zq_epilogue((int32_t)r[4 * j + 2], sr, s4.z);
+                            o.w = zq_epilogue((int32_t)r[4 * j + 3], sr, s4.w);
+                        }
+                        dst[j] = o;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int n = n0 + j;
+                        if (n < N) {
+                            const float sc = __ldg(col_scale + n);
+                            yrow[n] = bias ? zq_epilogue_bias((int32_t)r[j], sr, sc, __ldg(bias + n))
+                                           : zq_epilogue((int32_t)r[j], sr, sc);
+                        }
+                    }
+                }
+            }
+            tmem_fence_before();
+            mbar_arrive_cluster(tempty_leader + (uint32_t)(acc * sizeof(uint64_t)));
+            if (++acc == 2) acc = 0, acc_phase ^= 1u;
+        }
+    }
+
+    tmem_fence_before();
+    cluster_sync_all();  // no CTA leaves while its peer may still signal its barriers
+    tmem_fence_after();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                     : "memory");
+    }
+}
+
+cudaError_t launch_gemm_pair(const GemmArgs& a, cudaStream_t stream, bool pdl) {
+    using S = Smem2;
+    auto kern = gemm_i8_pair_kernel;
+    cudaError_t e = ensure_smem_attr(kern, S::kTotal);
+    if (e != cudaSuccess) return e;
+    const int sms = sm_count();
+    const int tiles = ((a.M + 255) / 256) * ((a.N + 255) / 256);
+    int clusters = sms / 2;
+    if (clusters > tiles) clusters = tiles;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = S::kTotal;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    const int m_tiles = (a.M + 255) / 256;
+    int group_m = a.group_m > 0 ? (a.group_m + 1) / 2 : m_tiles;  // group size in 256-row tiles
+    if (group_m > m_tiles) group_m = m_tiles;
+    if (group_m < 1) group_m = 1;
+    return cudaLaunchKernelEx(&cfg, kern, *a.tmap_a, *a.tmap_b, a.M, a.N, a.Kp, a.row_scale, a.col_scale, a.bias,
+                              a.y, a.err, group_m);
+}
+
 }  // namespace
 
 cudaError_t ensure_smem_attr_ptr(const void* kern, size_t bytes) {
@@ -374,8 +684,11 @@ int sm_count() {
 }
 
 int gemm_block_n(int M, int N) {
-    // Wide tiles when there are enough of them to fill the GPU; narrower
-    // tiles spread small problems over more SMs.
+    // 2-SM 256 x 256 tiles when there are at least two per SM pair;
+    // otherwise wide 1-SM tiles when there are enough of them to fill the
+    // GPU, and narrower tiles to spread small problems over more SMs.
+    const long pair_tiles = (long)((M + 255) / 256) * ((N + 255) / 256);
+    if (pair_tiles >= 148) return kPairBlockN;
     const long tiles256 = (long)((M + kBM - 1) / kBM) * ((N + 255) / 256);
     if (tiles256 >= 148) return 256;
     const long tiles128 = (long)((M + kBM - 1) / kBM) * ((N + 127) / 128);
@@ -384,6 +697,7 @@ int gemm_block_n(int M, int N) {
 }
 
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream, bool pdl) {
+    if (a.block_n == kPairBlockN) return launch_gemm_pair(a, stream, pdl);
     switch (a.block_n) {
         case 256: return launch_gemm_t<256, 4>(a, stream, pdl);
         case 128: return launch_gemm_t<128, 6>(a, stream, pdl);

@@ -20,10 +20,11 @@ struct zq_weight {
     uint8_t* panel = nullptr;  // [N][Kp] int8 or [N][Kp/2] packed int4
     float* scales = nullptr;   // [N]
     size_t panel_bytes = 0;
-    // Tensor maps over the INT8 panel, one per GEMM tile width (64/128/256).
+    // Tensor maps over the INT8 panel, one per GEMM tile shape (64/128/256
+    // columns, and the 2-SM pair tile).
     std::mutex mu;
-    CUtensorMap tmap_b[3];
-    bool tmap_ready[3] = {false, false, false};
+    CUtensorMap tmap_b[4];
+    bool tmap_ready[4] = {false, false, false, false};
 };
 
 namespace zq {

@@ -12,6 +12,8 @@
 namespace zq {
 
 constexpr int kGemvMaxRows = 8;
+// GemmArgs::block_n value selecting the 2-SM (cluster pair) 256 x 256 tile kernel.
+constexpr int kPairBlockN = 512;
 
 // Codes per column on the device, rounded up so every column starts on a
 // 16-byte boundary (INT8: 16 codes, INT4: 32 codes).

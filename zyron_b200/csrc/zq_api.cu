@@ -215,9 +215,13 @@ int tile_index(int block_n) {
 // columns between the two CTAs of a pair.
 int box_rows_b(int block_n) { return block_n == zq::kPairBlockN ? 128 : block_n; }
 
-// Per-thread device buffers of zq_matmul_host.
+// Per-thread device buffers and copy streams of zq_matmul_host.
+constexpr int kHostChunks = 8;
 struct HostStaging {
     int device = -1;
+    cudaStream_t h2d = nullptr, d2h = nullptr;
+    cudaEvent_t in_done[kHostChunks] = {}, mm_done[kHostChunks] = {}, out_done = nullptr;
+    bool streams_ready = false;
     void* x = nullptr;
     size_t x_cap = 0;
     void* y = nullptr;
@@ -231,6 +235,27 @@ struct HostStaging {
         cudaFree(y);
         cudaFree(b);
         cudaFree(ws);
+        if (streams_ready) {
+            cudaStreamDestroy(h2d);
+            cudaStreamDestroy(d2h);
+            for (int i = 0; i < kHostChunks; ++i) {
+                cudaEventDestroy(in_done[i]);
+                cudaEventDestroy(mm_done[i]);
+            }
+            cudaEventDestroy(out_done);
+        }
+    }
+    cudaError_t init_streams() {
+        if (streams_ready) return cudaSuccess;
+        cudaError_t e = cudaStreamCreateWithFlags(&h2d, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&d2h, cudaStreamNonBlocking);
+        for (int i = 0; i < kHostChunks && e == cudaSuccess; ++i) {
+            e = cudaEventCreateWithFlags(&in_done[i], cudaEventDisableTiming);
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&mm_done[i], cudaEventDisableTiming);
+        }
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&out_done, cudaEventDisableTiming);
+        if (e == cudaSuccess) streams_ready = true;
+        return e;
     }
 };
 thread_local HostStaging t_staging;
@@ -656,7 +681,16 @@ zq_status zq_matmul_host(const zq_weight* w, const float* x_host, size_t m, cons
     }
     cudaStream_t st = as_stream(stream);
     const size_t xb = m * w->K * sizeof(float), yb = m * w->N * sizeof(float);
-    const size_t wsb = zq_matmul_workspace_bytes(w, m);
+    // Large calls run in row chunks on three streams: copy-in of chunk i+1
+    // and copy-out of chunk i-1 overlap the matmul of chunk i (host buffers
+    // must be pinned for the copies to overlap).
+    size_t chunks = xb / (32u << 20);
+    if (chunks < 1) chunks = 1;
+    if (chunks > (size_t)kHostChunks) chunks = kHostChunks;
+    if (chunks > m) chunks = m;
+    const size_t rows_per = (m + chunks - 1) / chunks;
+    chunks = (m + rows_per - 1) / rows_per;
+    const size_t wsb = zq_matmul_workspace_bytes(w, rows_per);
     ZQ_CUDA(ensure(h.x, h.x_cap, xb));
     ZQ_CUDA(ensure(h.y, h.y_cap, yb));
     ZQ_CUDA(ensure(h.ws, h.ws_cap, wsb));
@@ -666,11 +700,37 @@ zq_status zq_matmul_host(const zq_weight* w, const float* x_host, size_t m, cons
         bdev = static_cast<float*>(h.b);
         ZQ_CUDA(cudaMemcpyAsync(bdev, bias_host, w->N * sizeof(float), cudaMemcpyHostToDevice, st));
     }
-    ZQ_CUDA(cudaMemcpyAsync(h.x, x_host, xb, cudaMemcpyHostToDevice, st));
-    zq_status s = zq_matmul(w, static_cast<const float*>(h.x), m, bdev, static_cast<float*>(h.y), h.ws, h.ws_cap,
-                            stream);
-    if (s != ZQ_OK) return s;
-    ZQ_CUDA(cudaMemcpyAsync(y_host, h.y, yb, cudaMemcpyDeviceToHost, st));
+    if (chunks == 1) {
+        ZQ_CUDA(cudaMemcpyAsync(h.x, x_host, xb, cudaMemcpyHostToDevice, st));
+        zq_status s = zq_matmul(w, static_cast<const float*>(h.x), m, bdev, static_cast<float*>(h.y), h.ws, h.ws_cap,
+                                stream);
+        if (s != ZQ_OK) return s;
+        ZQ_CUDA(cudaMemcpyAsync(y_host, h.y, yb, cudaMemcpyDeviceToHost, st));
+    } else {
+        ZQ_CUDA(h.init_streams());
+        // copies must not start before earlier work on the caller's stream
+        ZQ_CUDA(cudaEventRecord(h.out_done, st));
+        ZQ_CUDA(cudaStreamWaitEvent(h.h2d, h.out_done, 0));
+        ZQ_CUDA(cudaStreamWaitEvent(h.d2h, h.out_done, 0));
+        const size_t K = w->K, N = w->N;
+        for (size_t c = 0; c < chunks; ++c) {
+            const size_t r0 = c * rows_per;
+            const size_t rows = (m - r0) < rows_per ? (m - r0) : rows_per;
+            const float* xh = x_host + r0 * K;
+            float* xd = static_cast<float*>(h.x) + r0 * K;
+            float* yd = static_cast<float*>(h.y) + r0 * N;
+            ZQ_CUDA(cudaMemcpyAsync(xd, xh, rows * K * sizeof(float), cudaMemcpyHostToDevice, h.h2d));
+            ZQ_CUDA(cudaEventRecord(h.in_done[c], h.h2d));
+            ZQ_CUDA(cudaStreamWaitEvent(st, h.in_done[c], 0));
+            zq_status s = zq_matmul(w, xd, rows, bdev, yd, h.ws, h.ws_cap, stream);
+            if (s != ZQ_OK) return s;
+            ZQ_CUDA(cudaEventRecord(h.mm_done[c], st));
+            ZQ_CUDA(cudaStreamWaitEvent(h.d2h, h.mm_done[c], 0));
+            ZQ_CUDA(cudaMemcpyAsync(y_host + r0 * N, yd, rows * N * sizeof(float), cudaMemcpyDeviceToHost, h.d2h));
+        }
+        ZQ_CUDA(cudaEventRecord(h.out_done, h.d2h));
+        ZQ_CUDA(cudaStreamWaitEvent(st, h.out_done, 0));
+    }
     uint32_t code = 0;
     return zq_device_error(stream, &code);
 }

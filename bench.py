@@ -209,16 +209,25 @@ def run_ours(args, rank, world, local_rank):
     del w_f32
     torch.cuda.empty_cache()
     y = torch.empty((M, n_loc), dtype=torch.float32, device=dev)
-    y_full = torch.empty((world * M, n_loc), dtype=torch.float32, device=dev) if world > 1 else None
     ws_bytes = L.zq_matmul_workspace_bytes(W.handle, M)
     ws = torch.empty(ws_bytes + 256, dtype=torch.uint8, device=dev)
     ws_ptr = (ws.data_ptr() + 255) & ~255
+    peer_out = None
+    if world > 1:
+        # Every rank ends a step with the full [M, N] output: the matmul
+        # epilogue stores each finished tile into all ranks' outputs over
+        # NVLink (zq_matmul_multi); a one-element all-reduce then marks the
+        # step complete on every rank.
+        from zyron_b200.sharded import PeerOutputs, sharded_matmul_gathered
+
+        peer_out = PeerOutputs(M, N, dev)
 
     def step():
-        _lib.check(L.zq_matmul(W.handle, C.c_void_p(x.data_ptr()), M, None, C.c_void_p(y.data_ptr()),
-                               C.c_void_p(ws_ptr), ws_bytes, sp))
-        if world > 1:
-            dist.all_gather_into_tensor(y_full, y)
+        if world == 1:
+            _lib.check(L.zq_matmul(W.handle, C.c_void_p(x.data_ptr()), M, None, C.c_void_p(y.data_ptr()),
+                                   C.c_void_p(ws_ptr), ws_bytes, sp))
+            return
+        sharded_matmul_gathered(x, W, peer_out, workspace=(ws_ptr, ws_bytes), stream=stream)
 
     def barrier():
         if world > 1:
@@ -351,11 +360,13 @@ def run_ours(args, rank, world, local_rank):
         "config": {"workload": WORKLOAD if (M, K, N) == (M_ROWS, K_DIM, N_COLS) else f"prefill_int8_gemm_M{M}_K{K}_N{N}",
                    "M": M, "K": K, "N": N, "weight": "int8 per-column (device quantize)",
                    "x": "N(0,1) fp32", "w": "N(0,0.02) fp32 before quantization",
-                   "parallelism": f"column-sharded x{world}" + (" + NCCL all-gather of outputs" if world > 1 else ""),
+                   "parallelism": f"column-sharded x{world}" + (
+                       " + all-gather of outputs fused into the matmul epilogue (NVLink peer stores)"
+                       if world > 1 else ""),
                    "l2": "inputs larger than L2 (x 256 MiB, W 512 MiB, y 2 GiB); no flush"},
         "gpu_launches": (2 * args.steps),
         "clocks": sampler.summary(),
-        "roofline": {"bound": "tensor", "kernel": "gemm_i8_kernel (tcgen05.mma kind::i8)",
+        "roofline": {"bound": "tensor", "kernel": "gemm_i8_pair_kernel (tcgen05.mma.cta_group::2.kind::i8, 2-SM 256x256 tiles)",
                      "achieved": gemm_tops, "peak": int8_peak, "unit": UNIT, "frac": gemm_tops / int8_peak,
                      "peak_source": peak_src, "traffic": traffic,
                      "ms_per_launch": gemm_ms, "ops_per_launch": ops(M, n_loc, K)},
@@ -371,6 +382,202 @@ def run_ours(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------
+# secondary workloads (not the default line): decode GEMV and LM decode
+# --------------------------------------------------------------------------
+def hbm_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured: MEASURED_PEAKS hbm_gbs"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback: 6.65 TB/s (earlier pool measurement)"
+
+
+def run_gemv_workload(args):
+    """Decode GEMV M in {1, 8}, K=4096, N=11008, INT8 and INT4 weights ~N(0,0.02),
+    x ~N(0,1).  Weight copies rotate so the streamed bytes exceed 2 x L2;
+    launches are replayed from a CUDA graph (device back to back)."""
+    import torch
+
+    import zyron_b200 as zb
+    from zyron_b200 import _lib
+
+    L = _lib.lib()
+    dev = torch.device("cuda:0")
+    K, N = 4096, 11008
+    peak, peak_src = hbm_peak()
+    s = torch.cuda.Stream()
+    cases = {}
+    for qt in (1, 2):
+        payload = K * N if qt == 1 else K * N // 2
+        copies = max(3, int(2 * 126e6 / payload) + 2)
+        g = torch.Generator(device=dev)
+        g.manual_seed(2 + qt)
+        Ws = []
+        for _ in range(copies):
+            w = torch.randn((K, N), generator=g, device=dev).mul_(0.02)
+            Ws.append(zb.quantize(w, zb.Type(qt)))
+            del w
+        torch.cuda.empty_cache()
+        Kp = L.zq_weight_padded_k(Ws[0].handle)
+        for M in (1, 8):
+            x = torch.randn((M, K), generator=g, device=dev)
+            q = torch.empty((M, Kp), dtype=torch.int8, device=dev)
+            rs = torch.empty(M, device=dev)
+            y = torch.empty((M, N), device=dev)
+            wsb = L.zq_matmul_workspace_bytes(Ws[0].handle, M)
+            ws = torch.empty(wsb + 256, dtype=torch.uint8, device=dev)
+            wp = (ws.data_ptr() + 255) & ~255
+            res = {}
+            with torch.cuda.stream(s):
+                sp = C.c_void_p(s.cuda_stream)
+                _lib.check(L.zq_quantize_rows(C.c_void_p(x.data_ptr()), M, K, C.c_void_p(q.data_ptr()), Kp,
+                                              C.c_void_p(rs.data_ptr()), sp))
+
+                def kernel_only(i):
+                    _lib.check(L.zq_matmul_codes(Ws[i % copies].handle, C.c_void_p(q.data_ptr()),
+                                                 C.c_void_p(rs.data_ptr()), M, None, C.c_void_p(y.data_ptr()),
+                                                 C.c_void_p(wp), wsb, sp))
+
+                def full_call(i):
+                    _lib.check(L.zq_matmul(Ws[i % copies].handle, C.c_void_p(x.data_ptr()), M, None,
+                                           C.c_void_p(y.data_ptr()), C.c_void_p(wp), wsb, sp))
+
+                for name, fn in (("gemv_kernel", kernel_only), ("matmul_call", full_call)):
+                    for i in range(copies):
+                        fn(i)
+                    s.synchronize()
+                    reps = 10 * copies
+                    graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(graph, stream=s):
+                        for i in range(reps):
+                            fn(i)
+                    for _ in range(args.warmup):
+                        graph.replay()
+                    s.synchronize()
+                    a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+                    a.record(s)
+                    for _ in range(args.steps):
+                        graph.replay()
+                    b.record(s)
+                    s.synchronize()
+                    us = a.elapsed_time(b) / (args.steps * reps) * 1e3
+                    byts = payload + 4 * N + M * Kp + 4 * M * N
+                    res[name] = {"us": us, "GBs": byts / us / 1e3, "frac_of_hbm": byts / us / 1e3 / peak}
+                    del graph
+            cases[f"{'int8' if qt == 1 else 'int4'}_M{M}"] = res
+    # end to end through the host entry point (M=1, INT8): pinned host x in, host y out
+    W0 = zb.quantize(torch.randn((K, N), device=dev).mul_(0.02), zb.Type.Int8)
+    xh = torch.randn((1, K)).pin_memory()
+    yh = torch.empty((1, N)).pin_memory()
+    for _ in range(args.warmup):
+        _lib.check(L.zq_matmul_host(W0.handle, C.c_void_p(xh.data_ptr()), 1, None, C.c_void_p(yh.data_ptr()), None))
+    import time
+    t0 = time.perf_counter()
+    for _ in range(args.steps * 10):
+        _lib.check(L.zq_matmul_host(W0.handle, C.c_void_p(xh.data_ptr()), 1, None, C.c_void_p(yh.data_ptr()), None))
+    e2e_us = (time.perf_counter() - t0) / (args.steps * 10) * 1e6
+    cpu = None
+    if not args.skip_cpu_baseline:
+        zyq = W0.save_bytes()
+        call, threads, kind, _keep = reference_cpu_timer(zyq, xh.numpy())
+        call()
+        tc = min(call() for _ in range(3))
+        cpu = {"value": (K * N) / tc / 1e9, "unit": "GB/s", "cores": 1, "kind": kind,
+               "sample": f"M=1 x K={K} x N={N} INT8, best of 3 (the reference splits work over rows, so M=1 runs on "
+                         f"one thread whatever the thread count)"}
+    head = cases["int8_M1"]["gemv_kernel"]
+    line = {"metric": "decode GEMV weight-stream bandwidth (quantization::matmul, M=1 INT8)", "value": head["GBs"],
+            "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["us"] / 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "decode_gemv_K4096_N11008", "M": [1, 8], "types": ["int8", "int4"],
+                       "l2": "weights rotate over enough copies to stream > 2 x L2 per pass"},
+            "roofline": {"bound": "hbm", "kernel": "gemv_kernel", "achieved": head["GBs"], "peak": peak,
+                         "unit": "GB/s", "frac": head["frac_of_hbm"], "peak_source": peak_src,
+                         "bytes_per_launch": K * N + 4 * N + 16 * ((K + 15) // 16) + 4 * N},
+            "cases": cases,
+            "e2e": {"value": (K * N) / e2e_us / 1e3, "unit": "GB/s", "us_per_step": e2e_us,
+                    "h2d_bytes_per_step": 4 * K, "d2h_bytes_per_step": 4 * N, "api": "zq_matmul_host"},
+            "cpu_baseline": cpu}
+    print(json.dumps(line), flush=True)
+
+
+def run_qlm_workload(args):
+    """QuantizedLanguageModel decode: d_model 768, 12 layers, 12 heads, 4 KV
+    heads, GELU FFN 3072, tied vocab 16384, INT8, batch 1, 64-token prompt,
+    512 greedy tokens (random init of that architecture)."""
+    import tempfile
+    import time
+
+    import numpy as np
+    import torch
+
+    from zyron_b200.qlm import Config, GenerationConfig, QuantizedLanguageModel, random_zyqmodel
+
+    cfg = Config(vocab_size=16384, hidden_size=768, num_layers=12, num_heads=12, num_kv_heads=4,
+                 intermediate_size=3072, max_sequence_length=576)
+    img = random_zyqmodel(cfg, seed=0)
+    lm = QuantizedLanguageModel.load_bytes(img)
+    prompt = np.random.default_rng(0).integers(0, 16384, 64).tolist()
+    lm.generate(prompt, GenerationConfig(max_new_tokens=512, top_k=1))  # builds the graphs
+    s = torch.cuda.Stream()
+
+    def timed(n):
+        best = None
+        for _ in range(max(1, args.warmup // 3)):
+            lm.generate(prompt, GenerationConfig(max_new_tokens=n, top_k=1), stream=s)
+        for _ in range(3):
+            a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+            a.record(s)
+            lm.generate(prompt, GenerationConfig(max_new_tokens=n, top_k=1), stream=s)
+            b.record(s)
+            s.synchronize()
+            t = a.elapsed_time(b) / 1e3
+            best = t if best is None else min(best, t)
+        return best
+
+    t1 = timed(1)
+    t512 = timed(512)
+    per_tok = (t512 - t1) / 511
+    weight_bytes = 12 * (768 * (768 + 256 + 256 + 768 + 3072) + 3072 * 768) + 768 * 16384
+    peak, peak_src = hbm_peak()
+    cpu = None
+    if not args.skip_cpu_baseline:
+        from oracle import oracle as O
+
+        if O.ref_available():
+            with tempfile.TemporaryDirectory() as d:
+                path = os.path.join(d, "m.zyqmodel")
+                with open(path, "wb") as f:
+                    f.write(img)
+                h = C.c_void_p()
+                if O.ref().ref_qlm_load(path.encode(), C.byref(h)) == 0:
+                    threads = O.ref_set_threads(os.cpu_count() or 1)
+                    ids = np.asarray(prompt, dtype=np.uint64)
+                    out = np.zeros(ids.size + 4, dtype=np.uint64)
+                    n = C.c_size_t()
+                    t0 = time.perf_counter()
+                    O.ref().ref_qlm_generate_greedy(h, C.c_void_p(ids.ctypes.data), ids.size, 2,
+                                                    C.c_void_p(out.ctypes.data), C.byref(n))
+                    tc = (time.perf_counter() - t0) / 2
+                    O.ref().ref_qlm_free(h)
+                    cpu = {"value": 1.0 / tc, "unit": "tok/s", "cores": threads, "kind": "reference",
+                           "sample": "2 greedy tokens after the 64-token prompt (the reference recomputes the whole "
+                                     "prefix for every token; later tokens cost more)"}
+    line = {"metric": "quantized-LM decode tok/s (QuantizedLanguageModel::generate, greedy)", "value": 1.0 / per_tok,
+            "unit": "tok/s", "n_gpus": 1, "steps": 512, "warmup": args.warmup, "ms_per_step": per_tok * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "qlm_decode_d768_L12_H12_KV4_F3072_V16384_prompt64_new512",
+                       "weights": "random init of the architecture (numpy), INT8"},
+            "roofline": {"bound": "hbm", "achieved": weight_bytes / per_tok / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": weight_bytes / per_tok / 1e9 / peak, "peak_source": peak_src,
+                         "note": "weight bytes per token / time per token; the 88 MB of weights fit in L2"},
+            "e2e": {"value": 512.0 / t512, "unit": "tok/s", "note": "whole generate call incl. 64-token prefill",
+                    "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "prefill_ms": t1 * 1e3, "cpu_baseline": cpu}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -378,6 +585,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["prefill", "gemv", "qlm"], default="prefill",
+                    help="prefill (default line), gemv (decode GEMV) or qlm (LM decode)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling runs)")
     ap.add_argument("--shape", type=lambda v: tuple(int(t) for t in v.split(",")),
                     default=(M_ROWS, K_DIM, N_COLS), help="M,K,N override for small profiling cases")
@@ -393,6 +602,12 @@ def main():
 
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
+        return
+    if args.workload == "gemv":
+        run_gemv_workload(args)
+        return
+    if args.workload == "qlm":
+        run_qlm_workload(args)
         return
 
     import torch

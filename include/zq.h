@@ -110,6 +110,21 @@ zq_status zq_weight_destroy(zq_weight* w);
 
 /* ---- compute ------------------------------------------------------------ */
 
+/* zq_matmul whose output goes to n_dst (1..8) buffers at once: element
+ * (r, c) of the [m][cols] result is stored at dsts[i][r*ldy + col_offset + c]
+ * for every i.  The buffers may be other GPUs' memory mapped into this process
+ * (CUDA IPC or peer access): each output tile is then written over NVLink as
+ * soon as the tensor cores finish it, so the all-gather of column-sharded
+ * outputs (rank g passes col_offset = g*cols and every rank's full [m][ldy]
+ * output) runs inside the matmul instead of after it.  Stores are complete
+ * when the kernel completes; synchronise with the peers (e.g. a collective
+ * barrier) before reading their columns.  m must exceed 8 (the tensor-core
+ * path).  Same workspace rule as zq_matmul.  No counterpart in the reference
+ * (which runs on one host). */
+zq_status zq_matmul_multi(const zq_weight* w, const float* x, size_t m, const float* bias, float* const* dsts,
+                          int n_dst, size_t ldy, size_t col_offset, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
 /* Device scratch needed by zq_matmul for `m` activation rows. */
 size_t zq_matmul_workspace_bytes(const zq_weight* w, size_t m);
 
@@ -168,6 +183,34 @@ zq_status zq_dequantize(const zq_weight* w, float* out, void* stream);
 /* dequantize() into host memory: out_host is fp32 row-major [rows][cols].
  * Synchronous. */
 zq_status zq_dequantize_host(const zq_weight* w, float* out_host, void* stream);
+
+/* ---- peer buffers (for zq_matmul_multi across processes) ---------------- */
+
+/* A device allocation exported from one process for another (CUDA IPC). */
+typedef struct zq_ipc_handle {
+    unsigned char handle[64];
+    uint64_t offset; /* of the exported pointer inside its allocation */
+    int device;
+    int pad;
+} zq_ipc_handle;
+
+/* Export the allocation that contains `dev_ptr` (memory from cudaMalloc or a
+ * pool built on it) for use by other processes. */
+zq_status zq_ipc_export(const void* dev_ptr, zq_ipc_handle* out);
+
+/* Map an exported allocation into this process so that kernels on the
+ * CURRENT device can read and write it (peer access over NVLink is enabled
+ * for the current device).  *dev_ptr is the exported pointer's address here. */
+zq_status zq_ipc_import(const zq_ipc_handle* h, void** dev_ptr);
+
+/* Unmap what zq_ipc_import mapped (pass the pointer it returned). */
+zq_status zq_ipc_close(void* dev_ptr);
+
+/* Keep `sms` streaming multiprocessors out of the matmul kernels' persistent
+ * grids (process-wide, default 0), so work running concurrently on other
+ * streams -- e.g. an NCCL collective of the previous output block -- finds
+ * free SMs.  Returns the previous value. */
+int zq_set_reserved_sms(int sms);
 
 /* Synchronise `stream`, then read and clear the current device's error word
  * (0 = none; otherwise which bounded wait gave up).  Returns

@@ -1,0 +1,69 @@
+"""Column-sharded matmul with the all-gather fused into the epilogue, on 2
+GPUs (one process per GPU, NCCL for the IPC-handle exchange and the
+completion barrier).  Skipped when fewer than two GPUs are visible.  Each rank
+checks its full gathered output against the oracle, bit for bit."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _rank(rank, world, port, q):
+    import sys
+
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    import zyron_b200 as zb
+    from oracle import oracle as O
+    from zyron_b200.sharded import PeerOutputs, column_ranges, sharded_matmul_gathered
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        M, K, N = 640, 512, 2048
+        rng = np.random.default_rng(11)
+        x = rng.standard_normal((M, K)).astype(np.float32)
+        w = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+        b, e = column_ranges(N, world)[rank]
+        W = zb.quantize(torch.from_numpy(np.ascontiguousarray(w[:, b:e])).to(dev), zb.Type.Int8)
+        out = PeerOutputs(M, N, dev)
+        y = sharded_matmul_gathered(torch.from_numpy(x).to(dev), W, out)
+        torch.cuda.synchronize(dev)
+        pay, sc = O.quantize_weights(w, O.INT8)  # per-column quantization: the shards' codes are the full matrix's
+        want = O.matmul(x, O.INT8, pay, sc, N)[3]
+        got = y.cpu().numpy()
+        q.put((rank, bool(np.array_equal(got.view(np.uint32), want.view(np.uint32))), zb.device_error()))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gathered_matmul_two_gpus():
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(180)
+        assert p.exitcode == 0
+    res = sorted(q.get(timeout=10) for _ in range(2))
+    assert res == [(0, True, 0), (1, True, 0)]

@@ -212,3 +212,36 @@ def test_host_entry_point_chunked(zb):
     assert_bits_equal(y_host, y_dev, "chunked host matmul")
     rows = [0, 1, 1249, 1250, M - 1]
     assert_bits_equal(y_host[rows], O.matmul(x[rows], 1, pay, sc, N)[3], "chunked host rows vs oracle")
+
+
+@pytest.mark.parametrize("M,K,N,pair", [(300, 256, 200, False), (2048, 256, 4864, True)])
+def test_matmul_multi_destinations(zb, M, K, N, pair):
+    """The epilogue writes every output element to several buffers at a row
+    stride and column offset (the gathered-output path); each buffer holds
+    exactly the single-output result in its columns and nothing else
+    changes.  The second shape selects the 2-SM kernel."""
+    import ctypes as C
+
+    import torch
+    from zyron_b200 import _lib
+
+    L = _lib.lib()
+    rng = np.random.default_rng(M + 3)
+    x, w = make(rng, M, K, N, edge=False)
+    pay, sc = O.quantize_weights(w, 1)
+    W = zb.QuantizedMatrix.from_parts(1, K, N, sc, pay)
+    xd = torch.from_numpy(x).cuda()
+    want = zb.matmul(xd, W).cpu().numpy()
+    ldy, off = N + 36, 20
+    outs = [torch.full((M, ldy), -7.0, device="cuda") for _ in range(3)]
+    ptrs = (C.c_void_p * 3)(*[o.data_ptr() for o in outs])
+    wsb = L.zq_matmul_workspace_bytes(W.handle, M)
+    ws = torch.empty(wsb + 256, dtype=torch.uint8, device="cuda")
+    wp = (ws.data_ptr() + 255) & ~255
+    _lib.check(L.zq_matmul_multi(W.handle, C.c_void_p(xd.data_ptr()), M, None, ptrs, 3, ldy, off, C.c_void_p(wp), wsb,
+                                 C.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    for o in outs:
+        h = o.cpu().numpy()
+        assert_bits_equal(h[:, off:off + N], want, "multi-destination output")
+        assert np.all(h[:, :off] == -7.0) and np.all(h[:, off + N:] == -7.0)
+    assert zb.device_error() == 0

@@ -98,14 +98,25 @@ SIGNATURES = {
     "zq_matmul_codes": (st, [vp, vp, vp, sz, vp, vp, vp, sz, vp]),
     "zq_matmul": (st, [vp, vp, sz, vp, vp, vp, sz, vp]),
     "zq_matmul_noalloc": (st, [vp, vp, sz, vp, vp, vp]),
+    "zq_matmul_multi": (st, [vp, vp, sz, vp, vp, C.c_int, sz, sz, vp, sz, vp]),
     "zq_matmul_host": (st, [vp, vp, sz, vp, vp, vp]),
     "zq_dequantize": (st, [vp, vp, vp]),
     "zq_device_error": (st, [vp, C.POINTER(C.c_uint32)]),
+    "zq_set_reserved_sms": (C.c_int, [C.c_int]),
+    "zq_ipc_export": (st, [vp, vp]),
+    "zq_ipc_import": (st, [vp, C.POINTER(vp)]),
+    "zq_ipc_close": (st, [vp]),
     "zq_lm_load": (st, [vp, sz, vp, C.POINTER(vp)]),
     "zq_lm_get_info": (st, [vp, vp]),
     "zq_lm_generate_greedy": (st, [vp, vp, sz, sz, vp, sz, C.POINTER(sz), vp, vp]),
     "zq_lm_destroy": (st, [vp]),
 }
+
+
+class IpcHandle(C.Structure):
+    """zq_ipc_handle (include/zq.h)."""
+
+    _fields_ = [("handle", C.c_ubyte * 64), ("offset", C.c_uint64), ("device", C.c_int), ("pad", C.c_int)]
 
 
 class LmInfo(C.Structure):

@@ -109,6 +109,7 @@ zq_status encode_kmajor(CUtensorMap* map, const void* base, size_t rows, int Kp,
 // ---- device error word ----------------------------------------------------
 std::mutex g_err_mu;
 uint32_t* g_err_ptr[64] = {nullptr};
+std::vector<std::pair<void*, void*>> g_ipc_bases;  // imported pointer -> mapped allocation base
 
 zq_status device_error_ptr(uint32_t** out) {
     int dev = 0;
@@ -495,13 +496,36 @@ zq_status validate_matmul(const zq_weight* w, size_t m, const void* in, const fl
 
 // Dot + epilogue on activation codes q [m][Kp] (row stride Kp) and row
 // scales rs.  `scratch` is where INT4 weights are expanded for the GEMM.
+zq::OutDesc single_output(float* y, size_t N) {
+    zq::OutDesc o{};
+    o.base[0] = y;
+    o.count = 1;
+    o.ldy = (long long)N;
+    o.col_offset = 0;
+    o.vec = ((N & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15u) == 0);
+    return o;
+}
+
+// Dot + epilogue on activation codes q [m][Kp] (row stride Kp) and row
+// scales rs; the GEMM path writes through `out` (several destinations when
+// gathering), the GEMV path to out.base[0] with row stride N.
+zq_status run_codes_out(const zq_weight* w, const int8_t* codes, const float* rs, size_t m, const float* bias,
+                        const zq::OutDesc& out, uint8_t* scratch, cudaStream_t st, bool pdl);
+
 zq_status run_codes(const zq_weight* w, const int8_t* codes, const float* rs, size_t m, const float* bias, float* y,
                     uint8_t* scratch, cudaStream_t st, bool pdl) {
+    return run_codes_out(w, codes, rs, m, bias, single_output(y, w->N), scratch, st, pdl);
+}
+
+zq_status run_codes_out(const zq_weight* w, const int8_t* codes, const float* rs, size_t m, const float* bias,
+                        const zq::OutDesc& out, uint8_t* scratch, cudaStream_t st, bool pdl) {
+    float* y = out.base[0];
     uint32_t* err = nullptr;
     zq_status s = device_error_ptr(&err);
     if (s != ZQ_OK) return s;
     const int M = (int)m, N = (int)w->N, Kp = w->Kp;
-    if (M <= zq::kGemvMaxRows && zq::gemv_smem_bytes(M, Kp) <= 200 * 1024) {
+    const bool plain = out.count == 1 && out.ldy == (long long)N && out.col_offset == 0;
+    if (plain && M <= zq::kGemvMaxRows && zq::gemv_smem_bytes(M, Kp) <= 200 * 1024) {
         zq::GemvArgs a{w->type, w->panel, N, Kp, w->scales, codes, rs, bias, y, M};
         ZQ_CUDA(zq::launch_gemv(a, st, pdl));
         return ZQ_OK;
@@ -530,20 +554,25 @@ zq_status run_codes(const zq_weight* w, const int8_t* codes, const float* rs, si
         tmap_b = &tmap_b_local;
         pdl = true;  // the GEMM follows the expand kernel directly
     }
-    zq::GemmArgs g{&tmap_a, tmap_b, M, N, Kp, bn, rs, w->scales, bias, y, err, gemm_group_m()};
+    zq::GemmArgs g{&tmap_a, tmap_b, M, N, Kp, bn, rs, w->scales, bias, out, err, gemm_group_m()};
     ZQ_CUDA(zq::launch_gemm(g, st, pdl));
     return ZQ_OK;
 }
 
 // Quantizer + dot/epilogue with all scratch in `ws` (already validated:
 // 256-byte aligned, zq_matmul_workspace_bytes(w, m) bytes).
-zq_status matmul_in_workspace(const zq_weight* w, const float* x, size_t m, const float* bias, float* y,
-                              uint8_t* ws, cudaStream_t st) {
+zq_status matmul_in_workspace_out(const zq_weight* w, const float* x, size_t m, const float* bias,
+                                  const zq::OutDesc& out, uint8_t* ws, cudaStream_t st) {
     int8_t* codes = reinterpret_cast<int8_t*>(ws);
     float* rs = reinterpret_cast<float*>(ws + align256(m * (size_t)w->Kp));
     uint8_t* scratch = ws + align256(m * (size_t)w->Kp) + align256(m * sizeof(float));
     ZQ_CUDA(zq::launch_quantize_rows(x, (int)m, (int)w->K, w->Kp, codes, rs, st));
-    return run_codes(w, codes, rs, m, bias, y, scratch, st, true);
+    return run_codes_out(w, codes, rs, m, bias, out, scratch, st, true);
+}
+
+zq_status matmul_in_workspace(const zq_weight* w, const float* x, size_t m, const float* bias, float* y,
+                              uint8_t* ws, cudaStream_t st) {
+    return matmul_in_workspace_out(w, x, m, bias, single_output(y, w->N), ws, st);
 }
 
 }  // namespace
@@ -650,6 +679,32 @@ zq_status zq_matmul(const zq_weight* w, const float* x, size_t m, const float* b
     return zq::matmul_with_scratch(w, x, m, bias, y, workspace, workspace_bytes, stream);
 }
 
+zq_status zq_matmul_multi(const zq_weight* w, const float* x, size_t m, const float* bias, float* const* dsts,
+                          int n_dst, size_t ldy, size_t col_offset, void* workspace, size_t workspace_bytes,
+                          void* stream) {
+    if (!w) return fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON quantization: weights are empty");
+    if (m == 0) return ZQ_OK;
+    if (!dsts || n_dst < 1 || n_dst > zq::kMaxOutputs)
+        return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: zq_matmul_multi needs 1 to 8 destinations");
+    if (m <= (size_t)zq::kGemvMaxRows)
+        return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: zq_matmul_multi needs m > 8 (tensor-core path)");
+    if (ldy < w->N || col_offset > ldy - w->N)
+        return fail(ZQ_ERR_OUT_OF_RANGE, "zyron_b200: output columns exceed the destination row stride");
+    zq::OutDesc out{};
+    out.count = n_dst;
+    out.ldy = (long long)ldy;
+    out.col_offset = (long long)col_offset;
+    out.vec = (ldy % 4 == 0) && (col_offset % 4 == 0) && (w->N % 4 == 0);
+    for (int i = 0; i < n_dst; ++i) {
+        if (!dsts[i]) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null destination");
+        out.base[i] = dsts[i];
+        if (reinterpret_cast<uintptr_t>(dsts[i]) & 15u) out.vec = 0;
+    }
+    zq_status s = validate_matmul(w, m, x, out.base[0], workspace, workspace_bytes);
+    if (s != ZQ_OK) return s;
+    return matmul_in_workspace_out(w, x, m, bias, out, static_cast<uint8_t*>(workspace), as_stream(stream));
+}
+
 zq_status zq_matmul_codes(const zq_weight* w, const int8_t* q, const float* row_scale, size_t m, const float* bias,
                           float* y, void* workspace, size_t workspace_bytes, void* stream) {
     if (!w) return fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON quantization: weights are empty");
@@ -754,6 +809,65 @@ zq_status zq_dequantize_host(const zq_weight* w, float* out_host, void* stream) 
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     cudaFree(tmp);
     if (e != cudaSuccess) return cuda_fail(e, "dequantize to host");
+    return ZQ_OK;
+}
+
+int zq_set_reserved_sms(int sms) { return zq::set_reserved_sms(sms); }
+
+zq_status zq_ipc_export(const void* dev_ptr, zq_ipc_handle* out) {
+    if (!dev_ptr || !out) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null argument");
+    static_assert(sizeof(cudaIpcMemHandle_t) <= sizeof(out->handle), "IPC handle size");
+    PFN_cuMemGetAddressRange_v3020 range = nullptr;
+    {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &fn, 3020, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+    }
+    if (!range) return fail(ZQ_ERR_CUDA, "zyron_b200: cuMemGetAddressRange is unavailable");
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS)
+        return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: pointer is not a device allocation");
+    cudaIpcMemHandle_t h;
+    ZQ_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+    std::memset(out, 0, sizeof *out);
+    std::memcpy(out->handle, &h, sizeof h);
+    out->offset = (uint64_t)(reinterpret_cast<uintptr_t>(dev_ptr) - (uintptr_t)base);
+    cudaPointerAttributes attr;
+    ZQ_CUDA(cudaPointerGetAttributes(&attr, dev_ptr));
+    out->device = attr.device;
+    return ZQ_OK;
+}
+
+zq_status zq_ipc_import(const zq_ipc_handle* h, void** dev_ptr) {
+    if (!h || !dev_ptr) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null argument");
+    cudaIpcMemHandle_t ih;
+    std::memcpy(&ih, h->handle, sizeof ih);
+    void* base = nullptr;
+    // opened while the accessing device is current: the lazy flag enables
+    // that device's peer access to the exporting device
+    ZQ_CUDA(cudaIpcOpenMemHandle(&base, ih, cudaIpcMemLazyEnablePeerAccess));
+    *dev_ptr = static_cast<uint8_t*>(base) + h->offset;
+    std::lock_guard<std::mutex> lk(g_err_mu);
+    g_ipc_bases.emplace_back(*dev_ptr, base);
+    return ZQ_OK;
+}
+
+zq_status zq_ipc_close(void* dev_ptr) {
+    void* base = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_err_mu);
+        for (auto it = g_ipc_bases.begin(); it != g_ipc_bases.end(); ++it)
+            if (it->first == dev_ptr) {
+                base = it->second;
+                g_ipc_bases.erase(it);
+                break;
+            }
+    }
+    if (!base) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: pointer was not imported");
+    ZQ_CUDA(cudaIpcCloseMemHandle(base));
     return ZQ_OK;
 }
 

@@ -30,6 +30,7 @@
 
 #include <cuda.h>
 
+#include <atomic>
 #include <mutex>
 #include <unordered_map>
 
@@ -43,12 +44,19 @@ constexpr int kUmmaK = 32;
 constexpr int kThreads = 192;
 constexpr int kEpilogueThreads = 128;
 
+// Epilogue staging: each epilogue warp turns its 32 rows x 32 columns of
+// accumulators around in shared memory so that global stores are 128-byte
+// row segments (coalesced in HBM, large packets over NVLink).
+constexpr int kEpiPitch = 32;  // floats per staged row; float4 slots XOR-swizzled by row
+constexpr int kEpiBytes = 4 * 32 * kEpiPitch * 4;
+
 template <int BN, int STAGES>
 struct Smem {
     static constexpr int kABytes = kBM * kBK;
     static constexpr int kBBytes = BN * kBK;
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kBarrierBytes = 8 * (2 * STAGES + 4 + 1) + 16;
+    static constexpr int kBarrierBytes = (8 * (2 * STAGES + 4 + 1) + 16 + 127) / 128 * 128;  // keeps the staging area aligned
+    // staging area last: it is only allocated when the output has peers
     static constexpr int kTotal = 1024 /*alignment slack*/ + STAGES * kStageBytes + kBarrierBytes;
 };
 
@@ -111,6 +119,83 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Rescale the 32 x 32 accumulator block a warp holds (lane = row row0+lane,
+// registers = columns n0 .. n0+31) and store it to every destination of
+// `out`.
+//   one destination: each thread writes its row's 128 contiguous bytes
+//     (eight 16-byte stores; L2 merges the lines in HBM);
+//   several destinations (other GPUs' outputs over NVLink, the all-gather
+//     fused into the matmul): the block is turned around in the warp's
+//     shared-memory stage (float4 slots XOR-swizzled by row: conflict-free
+//     16-byte writes and reads), so each store instruction writes four rows
+//     x 128 contiguous bytes -- large NVLink packets instead of 16-byte ones.
+// Ragged blocks store element by element.
+__device__ __forceinline__ void store_block(const uint32_t (&r)[32], float* __restrict__ stage, int row0, int lane,
+                                            int M, int n0, int N, float sr, const float* __restrict__ col_scale,
+                                            const float* __restrict__ bias, const OutDesc& out) {
+    const int row = row0 + lane;
+    if (out.vec && n0 + 32 <= N) {
+        const float4* cs4 = reinterpret_cast<const float4*>(col_scale + n0);
+        const float4* b4 = bias ? reinterpret_cast<const float4*>(bias + n0) : nullptr;
+        float4 o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float4 s4 = __ldg(cs4 + j);
+            if (b4) {
+                const float4 b = __ldg(b4 + j);
+                o[j].x = zq_epilogue_bias((int32_t)r[4 * j + 0], sr, s4.x, b.x);
+                o[j].y = zq_epilogue_bias((int32_t)r[4 * j + 1], sr, s4.y, b.y);
+                o[j].z = zq_epilogue_bias((int32_t)r[4 * j + 2], sr, s4.z, b.z);
+                o[j].w = zq_epilogue_bias((int32_t)r[4 * j + 3], sr, s4.w, b.w);
+            } else {
+                o[j].x = zq_epilogue((int32_t)r[4 * j + 0], sr, s4.x);
+                o[j].y = zq_epilogue((int32_t)r[4 * j + 1], sr, s4.y);
+                o[j].z = zq_epilogue((int32_t)r[4 * j + 2], sr, s4.z);
+                o[j].w = zq_epilogue((int32_t)r[4 * j + 3], sr, s4.w);
+            }
+        }
+        if (out.count == 1) {
+            if (row < M) {
+                float4* dst = reinterpret_cast<float4*>(out.base[0] + (size_t)row * (size_t)out.ldy +
+                                                        (size_t)out.col_offset + n0);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) dst[j] = o[j];
+            }
+            return;
+        }
+        float4* st4 = reinterpret_cast<float4*>(stage);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) st4[lane * 8 + (j ^ (lane & 7))] = o[j];
+        __syncwarp();
+        const int sub = lane >> 3;  // row within a group of four
+        const int q = lane & 7;     // column quad
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+            const int rl = it * 4 + sub;
+            const int grow = row0 + rl;
+            const float4 v = st4[rl * 8 + (q ^ (rl & 7))];
+            if (grow < M) {
+                const size_t off = (size_t)grow * (size_t)out.ldy + (size_t)out.col_offset + n0 + 4 * q;
+                for (int d = 0; d < out.count; ++d) *reinterpret_cast<float4*>(out.base[d] + off) = v;
+            }
+        }
+        __syncwarp();  // the staging area is reused by the next block
+        return;
+    }
+    if (row >= M) return;
+    const size_t base_off = (size_t)row * (size_t)out.ldy + (size_t)out.col_offset;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const int n = n0 + j;
+        if (n < N) {
+            const float sc = __ldg(col_scale + n);
+            const float val =
+                bias ? zq_epilogue_bias((int32_t)r[j], sr, sc, __ldg(bias + n)) : zq_epilogue((int32_t)r[j], sr, sc);
+            for (int d = 0; d < out.count; ++d) out.base[d][base_off + n] = val;
+        }
+    }
+}
+
 // Tile order: groups of `group_m` M-tiles; inside a group the M-tile index
 // runs fastest, then the N-tile.  The CTAs running at the same time then
 // share a few A panels (activation rows) and B panels (weight columns) in L2.
@@ -129,13 +214,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    int M, int N, int Kp, const float* __restrict__ row_scale,
                    const float* __restrict__ col_scale, const float* __restrict__ bias,
-                   float* __restrict__ y, uint32_t* __restrict__ err, int group_m) {
+                   const __grid_constant__ OutDesc out, uint32_t* __restrict__ err, int group_m) {
     using S = Smem<BN, STAGES>;
     constexpr uint32_t kTmemCols = 2 * BN;  // power of two >= 32 for BN in {64,128,256}
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* stage_base = smem;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStageBytes);
+    float* epi_stage = reinterpret_cast<float*>(smem + STAGES * S::kStageBytes + S::kBarrierBytes);
     uint64_t* full = bars;
     uint64_t* empty = bars + STAGES;
     uint64_t* tfull = bars + 2 * STAGES;
@@ -253,16 +339,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int quarter = warp & 3;
         int acc = 0;
         uint32_t acc_phase = 0;
-        const bool vec_ok = ((N & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15u) == 0);
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
             int mt, nt;
             tile_coords(t, m_tiles, n_tiles, group_m, mt, nt);
             if (!mbar_wait_bounded(&tfull[acc], acc_phase, err, kDevErrTimeoutEpilogue)) break;
             tmem_fence_after();
-            const int row = mt * kBM + quarter * 32 + lane;
-            const bool row_ok = row < M;
-            const float sr = row_ok ? __ldg(row_scale + row) : 0.0f;
-            float* yrow = y + (size_t)(row_ok ? row : 0) * N;
+            const int row0 = mt * kBM + quarter * 32;
+            const int row = row0 + lane;
+            const float sr = row < M ? __ldg(row_scale + row) : 0.0f;
+            float* stage = epi_stage + quarter * 32 * kEpiPitch;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
@@ -270,40 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_ld_32x32b_x32(taddr + c * 32, r);
                 tmem_ld_wait();
                 const int n0 = nt * BN + c * 32;
-                if (!row_ok || n0 >= N) continue;
-                const float4* cs4 = reinterpret_cast<const float4*>(col_scale + n0);
-                if (vec_ok && n0 + 32 <= N) {
-                    const float4* b4 = bias ? reinterpret_cast<const float4*>(bias + n0) : nullptr;
-                    float4* dst = reinterpret_cast<float4*>(yrow + n0);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const float4 s = __ldg(cs4 + j);
-                        float4 o;
-                        if (b4) {
-                            const float4 b = __ldg(b4 + j);
-                            o.x = zq_epilogue_bias((int32_t)r[4 * j + 0], sr, s.x, b.x);
-                            o.y = zq_epilogue_bias((int32_t)r[4 * j + 1], sr, s.y, b.y);
-                            o.z = zq_epilogue_bias((int32_t)r[4 * j + 2], sr, s.z, b.z);
-                            o.w = zq_epilogue_bias((int32_t)r[4 * j + 3], sr, s.w, b.w);
-                        } else {
-                            o.x = zq_epilogue((int32_t)r[4 * j + 0], sr, s.x);
-                            o.y = zq_epilogue((int32_t)r[4 * j + 1], sr, s.y);
-                            o.z = zq_epilogue((int32_t)r[4 * j + 2], sr, s.z);
-                            o.w = zq_epilogue((int32_t)r[4 * j + 3], sr, s.w);
-                        }
-                        dst[j] = o;
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int n = n0 + j;
-                        if (n < N) {
-                            const float sc = __ldg(col_scale + n);
-                            yrow[n] = bias ? zq_epilogue_bias((int32_t)r[j], sr, sc, __ldg(bias + n))
-                                           : zq_epilogue((int32_t)r[j], sr, sc);
-                        }
-                    }
-                }
+                if (row0 < M && n0 < N) store_block(r, stage, row0, lane, M, n0, N, sr, col_scale, bias, out);
             }
             tmem_fence_before();
             mbar_arrive(&tempty[acc]);
@@ -311,6 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
+    if (out.count > 1 && warp >= 2) __threadfence_system();  // peer stores performed before the grid ends
     tmem_fence_before();
     __syncthreads();
     tmem_fence_after();
@@ -324,7 +377,8 @@ template <int BN, int STAGES>
 cudaError_t launch_gemm_t(const GemmArgs& a, cudaStream_t stream, bool pdl) {
     using S = Smem<BN, STAGES>;
     auto kern = gemm_i8_kernel<BN, STAGES>;
-    cudaError_t e = ensure_smem_attr(kern, S::kTotal);
+    const int smem = S::kTotal + (a.out.count > 1 ? kEpiBytes : 0);
+    cudaError_t e = ensure_smem_attr(kern, smem);
     if (e != cudaSuccess) return e;
     const int sms = sm_count();
     const int tiles = ((a.M + kBM - 1) / kBM) * ((a.N + BN - 1) / BN);
@@ -333,7 +387,7 @@ cudaError_t launch_gemm_t(const GemmArgs& a, cudaStream_t stream, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = S::kTotal;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -344,7 +398,7 @@ cudaError_t launch_gemm_t(const GemmArgs& a, cudaStream_t stream, bool pdl) {
     int group_m = a.group_m > 0 ? a.group_m : m_tiles;
     if (group_m > m_tiles) group_m = m_tiles;
     return cudaLaunchKernelEx(&cfg, kern, *a.tmap_a, *a.tmap_b, a.M, a.N, a.Kp, a.row_scale, a.col_scale, a.bias,
-                              a.y, a.err, group_m);
+                              a.out, a.err, group_m);
 }
 
 
@@ -364,7 +418,7 @@ struct Smem2 {
     static constexpr int kABytes = 128 * kBK;  // this CTA's 128 rows of A
     static constexpr int kBBytes = 128 * kBK;  // this CTA's 128 rows (columns of W) of B
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kBarrierBytes = 8 * (2 * kStages2 + 4 + 1) + 16;
+    static constexpr int kBarrierBytes = (8 * (2 * kStages2 + 4 + 1) + 16 + 127) / 128 * 128;
     static constexpr int kTotal = 1024 + kStages2 * kStageBytes + kBarrierBytes;
 };
 
@@ -426,13 +480,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                         int M, int N, int Kp, const float* __restrict__ row_scale,
                         const float* __restrict__ col_scale, const float* __restrict__ bias,
-                        float* __restrict__ y, uint32_t* __restrict__ err, int group_m) {
+                        const __grid_constant__ OutDesc out, uint32_t* __restrict__ err, int group_m) {
     using S = Smem2;
     constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* stage_base = smem;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages2 * S::kStageBytes);
+    float* epi_stage = reinterpret_cast<float*>(smem + kStages2 * S::kStageBytes + S::kBarrierBytes);
     uint64_t* full = bars;                       // leader's copy used
     uint64_t* empty = bars + kStages2;           // both copies used
     uint64_t* tfull = bars + 2 * kStages2;       // both copies used
@@ -559,16 +614,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tempty_leader = map_to_rank(&tempty[0], 0);
         int acc = 0;
         uint32_t acc_phase = 0;
-        const bool vec_ok = ((N & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15u) == 0);
         for (int t = cluster; t < num_tiles; t += clusters) {
             int mt, nt;
             tile_coords(t, m_tiles, n_tiles, group_m, mt, nt);
             if (!mbar_wait_bounded(&tfull[acc], acc_phase, err, kDevErrTimeoutEpilogue)) break;
             tmem_fence_after();
-            const int row = mt * 256 + (int)rank * 128 + quarter * 32 + lane;
-            const bool row_ok = row < M;
-            const float sr = row_ok ? __ldg(row_scale + row) : 0.0f;
-            float* yrow = y + (size_t)(row_ok ? row : 0) * N;
+            const int row0 = mt * 256 + (int)rank * 128 + quarter * 32;
+            const int row = row0 + lane;
+            const float sr = row < M ? __ldg(row_scale + row) : 0.0f;
+            float* stage = epi_stage + quarter * 32 * kEpiPitch;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * 256);
 #pragma unroll 1
             for (int c = 0; c < 256 / 32; ++c) {
@@ -576,40 +630,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_ld_32x32b_x32(taddr + c * 32, r);
                 tmem_ld_wait();
                 const int n0 = nt * 256 + c * 32;
-                if (!row_ok || n0 >= N) continue;
-                const float4* cs4 = reinterpret_cast<const float4*>(col_scale + n0);
-                if (vec_ok && n0 + 32 <= N) {
-                    const float4* b4 = bias ? reinterpret_cast<const float4*>(bias + n0) : nullptr;
-                    float4* dst = reinterpret_cast<float4*>(yrow + n0);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const float4 s4 = __ldg(cs4 + j);
-                        float4 o;
-                        if (b4) {
-                            const float4 b = __ldg(b4 + j);
-                            o.x = zq_epilogue_bias((int32_t)r[4 * j + 0], sr, s4.x, b.x);
-                            o.y = zq_epilogue_bias((int32_t)r[4 * j + 1], sr, s4.y, b.y);
-                            o.z = zq_epilogue_bias((int32_t)r[4 * j + 2], sr, s4.z, b.z);
-                            o.w = zq_epilogue_bias((int32_t)r[4 * j + 3], sr, s4.w, b.w);
-                        } else {
-                            o.x = zq_epilogue((int32_t)r[4 * j + 0], sr, s4.x);
-                            o.y = zq_epilogue((int32_t)r[4 * j + 1], sr, s4.y);
-                            o.z = zq_epilogue((int32_t)r[4 * j + 2], sr, s4.z);
-                            o.w = zq_epilogue((int32_t)r[4 * j + 3], sr, s4.w);
-                        }
-                        dst[j] = o;
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int n = n0 + j;
-                        if (n < N) {
-                            const float sc = __ldg(col_scale + n);
-                            yrow[n] = bias ? zq_epilogue_bias((int32_t)r[j], sr, sc, __ldg(bias + n))
-                                           : zq_epilogue((int32_t)r[j], sr, sc);
-                        }
-                    }
-                }
+                if (row0 < M && n0 < N) store_block(r, stage, row0, lane, M, n0, N, sr, col_scale, bias, out);
             }
             tmem_fence_before();
             mbar_arrive_cluster(tempty_leader + (uint32_t)(acc * sizeof(uint64_t)));
@@ -617,6 +638,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
+    if (out.count > 1 && warp >= 2) __threadfence_system();  // peer stores performed before the grid ends
     tmem_fence_before();
     cluster_sync_all();  // no CTA leaves while its peer may still signal its barriers
     tmem_fence_after();
@@ -629,16 +651,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 cudaError_t launch_gemm_pair(const GemmArgs& a, cudaStream_t stream, bool pdl) {
     using S = Smem2;
     auto kern = gemm_i8_pair_kernel;
-    cudaError_t e = ensure_smem_attr(kern, S::kTotal);
+    const int smem = S::kTotal + (a.out.count > 1 ? kEpiBytes : 0);
+    cudaError_t e = ensure_smem_attr(kern, smem);
     if (e != cudaSuccess) return e;
     const int sms = sm_count();
     const int tiles = ((a.M + 255) / 256) * ((a.N + 255) / 256);
     int clusters = sms / 2;
+    if (clusters < 1) clusters = 1;
     if (clusters > tiles) clusters = tiles;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = S::kTotal;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -654,7 +678,7 @@ cudaError_t launch_gemm_pair(const GemmArgs& a, cudaStream_t stream, bool pdl) {
     if (group_m > m_tiles) group_m = m_tiles;
     if (group_m < 1) group_m = 1;
     return cudaLaunchKernelEx(&cfg, kern, *a.tmap_a, *a.tmap_b, a.M, a.N, a.Kp, a.row_scale, a.col_scale, a.bias,
-                              a.y, a.err, group_m);
+                              a.out, a.err, group_m);
 }
 
 }  // namespace
@@ -670,18 +694,26 @@ cudaError_t ensure_smem_attr_ptr(const void* kern, size_t bytes) {
     return e;
 }
 
+std::atomic<int> g_reserved_sms{0};
+
 int sm_count() {
     static int cached[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return 148;
-    if (!cached[dev]) {
-        int sms = 0;
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        cached[dev] = sms > 0 ? sms : 148;
+    int sms = 148;
+    if (dev >= 0 && dev < 64) {
+        if (!cached[dev]) {
+            int n = 0;
+            cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+            cached[dev] = n > 0 ? n : 148;
+        }
+        sms = cached[dev];
     }
-    return cached[dev];
+    const int avail = sms - g_reserved_sms.load(std::memory_order_relaxed);
+    return avail >= 2 ? avail : 2;
 }
+
+int set_reserved_sms(int sms) { return g_reserved_sms.exchange(sms < 0 ? 0 : sms); }
 
 int gemm_block_n(int M, int N) {
     // 2-SM 256 x 256 tiles when there are at least two per SM pair;

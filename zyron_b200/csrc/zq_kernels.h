@@ -32,6 +32,18 @@ struct GemvArgs {
     int M;
 };
 
+// Where the GEMM epilogue writes: element (row, col) of the matmul goes to
+// base[d][row * ldy + col_offset + col] for every d < count.  count > 1 means
+// the other bases are peer GPUs' buffers mapped into this process.
+constexpr int kMaxOutputs = 8;
+struct OutDesc {
+    float* base[kMaxOutputs];
+    int count;
+    int vec;  // ldy, col_offset and every base allow 16-byte stores
+    long long ldy;
+    long long col_offset;
+};
+
 struct GemmArgs {
     const CUtensorMap* tmap_a;
     const CUtensorMap* tmap_b;
@@ -40,7 +52,7 @@ struct GemmArgs {
     const float* row_scale;
     const float* col_scale;
     const float* bias;
-    float* y;
+    OutDesc out;
     uint32_t* err;
     int group_m;  // tile-order group size in M-tiles (0 = all M-tiles)
 };
@@ -61,8 +73,10 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl);
 
 int gemm_block_n(int M, int N);
 
-// Multiprocessor count of the current device (cached per device).
+// Multiprocessors of the current device available to the persistent kernels
+// (device count cached per device, minus the reserved count).
 int sm_count();
+int set_reserved_sms(int sms);
 
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) at most once per kernel
 // (keyed by the kernel's address) and size: host-side launch overhead matters

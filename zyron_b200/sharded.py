@@ -80,3 +80,92 @@ def sharded_matmul(x, weight_shard, n_cols: int, group=None, gather: bool = True
     dist.all_gather_into_tensor(buf, send, group=group)
     blocks = [blk[:, :w] for blk, w in zip(buf.view(world, M, wmax).unbind(0), widths)]
     return assemble_columns(blocks, ranges)
+
+
+class PeerOutputs:
+    """A full [rows, cols] fp32 output on every rank of the process group,
+    each rank holding device pointers to all the others' copies (CUDA IPC
+    through torch's tensor sharing; peer access over NVLink).
+
+    ``sharded_matmul_gathered`` lets the matmul epilogue store every output
+    tile straight into all these buffers (``zq_matmul_multi``), so the
+    all-gather of column-sharded outputs happens inside the matmul.
+    """
+
+    def __init__(self, rows, cols, device, group=None):
+        import ctypes as C
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _lib
+
+        L = _lib.lib()
+        self.rows, self.cols = rows, cols
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.local = torch.empty((rows, cols), dtype=torch.float32, device=device)
+        h = _lib.IpcHandle()
+        _lib.check(L.zq_ipc_export(C.c_void_p(self.local.data_ptr()), C.byref(h)))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(h), group=group)
+        # import the peers' buffers with this rank's device current, so the
+        # matmul running here may store into them (peer access over NVLink)
+        self._imported = []
+        with torch.cuda.device(device):
+            for r, raw in enumerate(handles):
+                if r == self.rank:
+                    continue
+                ph = _lib.IpcHandle.from_buffer_copy(raw)
+                p = C.c_void_p()
+                _lib.check(L.zq_ipc_import(C.byref(ph), C.byref(p)))
+                self._imported.append(p.value)
+        # destination order: own buffer first, then the peers
+        self.pointers = [self.local.data_ptr()] + self._imported
+        self._flag = torch.zeros(1, dtype=torch.float32, device=device)
+
+    def close(self):
+        from . import _lib
+
+        for p in self._imported:
+            _lib.lib().zq_ipc_close(p)
+        self._imported = []
+
+    def barrier(self):
+        """Stream-ordered completion barrier: returns (on the stream) once every
+        rank's matmul -- and so every peer store into this rank's output --
+        has finished."""
+        import torch.distributed as dist
+
+        dist.all_reduce(self._flag, group=self.group)
+
+
+def sharded_matmul_gathered(x, weight_shard, peer_out: PeerOutputs, bias_shard=None, workspace=None, stream=None):
+    """y = matmul(x, W) with W column-sharded over the group; every rank ends
+    with the full [M, N] output in ``peer_out.local``.  The matmul epilogue
+    writes each tile to all ranks' outputs over NVLink; no separate
+    collective moves the data."""
+    import ctypes as C
+
+    import torch
+
+    from . import _lib
+    from .quantization import workspace as get_workspace
+
+    L = _lib.lib()
+    ranges = column_ranges(peer_out.cols, peer_out.world)
+    b, e = ranges[peer_out.rank]
+    if weight_shard.cols() != e - b:
+        raise ValueError("weight shard does not match this rank's column range")
+    x = x.contiguous()
+    m = x.shape[0]
+    s = stream if stream is not None else torch.cuda.current_stream(x.device)
+    ws, ws_bytes = workspace if workspace is not None else get_workspace(weight_shard, m, x.device, s.cuda_stream)
+    ptrs = (C.c_void_p * len(peer_out.pointers))(*peer_out.pointers)
+    _lib.check(L.zq_matmul_multi(weight_shard.handle, C.c_void_p(x.data_ptr()), m,
+                                 None if bias_shard is None else C.c_void_p(bias_shard.data_ptr()),
+                                 ptrs, len(peer_out.pointers), peer_out.cols, b, C.c_void_p(ws), ws_bytes,
+                                 C.c_void_p(s.cuda_stream)))
+    peer_out.barrier()
+    return peer_out.local

@@ -502,6 +502,72 @@ def run_gemv_workload(args):
     print(json.dumps(line), flush=True)
 
 
+def run_small_workload(args):
+    """The two small matmul configurations: INT8 M=64 K=512 N=512 and INT4
+    M=128 K=2048 N=2048, x ~N(0,1), w ~N(0,0.02).  Calls are replayed from a
+    CUDA graph; the reference's CPU matmul is timed on the same inputs."""
+    import numpy as np
+    import torch
+
+    import zyron_b200 as zb
+    from zyron_b200 import _lib
+
+    L = _lib.lib()
+    dev = torch.device("cuda:0")
+    s = torch.cuda.Stream()
+    out = {}
+    for name, qt, M, K, N, seed in (("int8_M64_K512_N512", 1, 64, 512, 512, 0),
+                                    ("int4_M128_K2048_N2048", 2, 128, 2048, 2048, 1)):
+        rng = np.random.default_rng(seed)
+        x = rng.standard_normal((M, K)).astype(np.float32)
+        w = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+        W = zb.quantize(torch.from_numpy(w).to(dev), zb.Type(qt))
+        xd = torch.from_numpy(x).to(dev)
+        y = torch.empty((M, N), device=dev)
+        wsb = L.zq_matmul_workspace_bytes(W.handle, M)
+        ws = torch.empty(wsb + 256, dtype=torch.uint8, device=dev)
+        wp = (ws.data_ptr() + 255) & ~255
+        with torch.cuda.stream(s):
+            sp = C.c_void_p(s.cuda_stream)
+
+            def call():
+                _lib.check(L.zq_matmul(W.handle, C.c_void_p(xd.data_ptr()), M, None, C.c_void_p(y.data_ptr()),
+                                       C.c_void_p(wp), wsb, sp))
+
+            for _ in range(3):
+                call()
+            s.synchronize()
+            reps = 50
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                for _ in range(reps):
+                    call()
+            for _ in range(args.warmup):
+                graph.replay()
+            s.synchronize()
+            a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+            a.record(s)
+            for _ in range(args.steps):
+                graph.replay()
+            b.record(s)
+            s.synchronize()
+            us = a.elapsed_time(b) / (args.steps * reps) * 1e3
+        res = {"us_per_call": us, "TOPS": 2.0 * M * N * K / us / 1e6}
+        if not args.skip_cpu_baseline:
+            zyq = W.save_bytes()
+            call_ref, threads, kind, _keep = reference_cpu_timer(zyq, x)
+            call_ref()
+            tc = min(call_ref() for _ in range(3))
+            res["cpu_baseline"] = {"us_per_call": tc * 1e6, "TOPS": 2.0 * M * N * K / tc / 1e12, "cores": threads,
+                                   "kind": kind}
+        out[name] = res
+    line = {"metric": "small quantized matmul configurations (quantization::matmul)",
+            "value": out["int4_M128_K2048_N2048"]["TOPS"], "unit": "TOPS", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic", "config": {"workload": "small_matmuls"}, "cases": out}
+    print(json.dumps(line), flush=True)
+
+
 def run_qlm_workload(args):
     """QuantizedLanguageModel decode: d_model 768, 12 layers, 12 heads, 4 KV
     heads, GELU FFN 3072, tied vocab 16384, INT8, batch 1, 64-token prompt,
@@ -585,8 +651,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["prefill", "gemv", "qlm"], default="prefill",
-                    help="prefill (default line), gemv (decode GEMV) or qlm (LM decode)")
+    ap.add_argument("--workload", choices=["prefill", "gemv", "small", "qlm"], default="prefill",
+                    help="prefill (default line), gemv (decode GEMV), small (64x512x512 INT8 and "
+                         "128x2048x2048 INT4) or qlm (LM decode)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling runs)")
     ap.add_argument("--shape", type=lambda v: tuple(int(t) for t in v.split(",")),
                     default=(M_ROWS, K_DIM, N_COLS), help="M,K,N override for small profiling cases")
@@ -608,6 +675,9 @@ def main():
         return
     if args.workload == "qlm":
         run_qlm_workload(args)
+        return
+    if args.workload == "small":
+        run_small_workload(args)
         return
 
     import torch

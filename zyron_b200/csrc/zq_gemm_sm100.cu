@@ -119,17 +119,13 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// Rescale the 32 x 32 accumulator block a warp holds (lane = row row0+lane,
-// registers = columns n0 .. n0+31) and store it to every destination of
-// `out`.
-//   one destination: each thread writes its row's 128 contiguous bytes
-//     (eight 16-byte stores; L2 merges the lines in HBM);
-//   several destinations (other GPUs' outputs over NVLink, the all-gather
-//     fused into the matmul): the block is turned around in the warp's
-//     shared-memory stage (float4 slots XOR-swizzled by row: conflict-free
-//     16-byte writes and reads), so each store instruction writes four rows
-//     x 128 contiguous bytes -- large NVLink packets instead of 16-byte ones.
-// Ragged blocks store element by element.
+// Several destinations (other GPUs' outputs over NVLink: the all-gather
+// fused into the matmul).  The warp's 32 x 32 block (lane = row row0+lane,
+// registers = columns n0 .. n0+31) is rescaled, turned around in the warp's
+// shared-memory stage (float4 slots XOR-swizzled by row: conflict-free
+// 16-byte writes and reads) and stored so that each store instruction writes
+// four rows x 128 contiguous bytes to every destination -- large NVLink
+// packets instead of 16-byte ones.  Ragged blocks store element by element.
 __device__ __forceinline__ void store_block(const uint32_t (&r)[32], float* __restrict__ stage, int row0, int lane,
                                             int M, int n0, int N, float sr, const float* __restrict__ col_scale,
                                             const float* __restrict__ bias, const OutDesc& out) {
@@ -153,15 +149,6 @@ __device__ __forceinline__ void store_block(const uint32_t (&r)[32], float* __re
                 o[j].z = zq_epilogue((int32_t)r[4 * j + 2], sr, s4.z);
                 o[j].w = zq_epilogue((int32_t)r[4 * j + 3], sr, s4.w);
             }
-        }
-        if (out.count == 1) {
-            if (row < M) {
-                float4* dst = reinterpret_cast<float4*>(out.base[0] + (size_t)row * (size_t)out.ldy +
-                                                        (size_t)out.col_offset + n0);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) dst[j] = o[j];
-            }
-            return;
         }
         float4* st4 = reinterpret_cast<float4*>(stage);
 #pragma unroll
@@ -196,6 +183,57 @@ __device__ __forceinline__ void store_block(const uint32_t (&r)[32], float* __re
     }
 }
 
+// One destination (the plain matmul): each thread rescales its row of the
+// tile 32 columns at a time and writes them as 128 contiguous bytes
+// (eight 16-byte stores; L2 merges the lines before they reach HBM).
+template <int BN>
+__device__ __forceinline__ void store_tile_rows(uint32_t taddr, int row, bool row_ok, int nbase, int N, float sr,
+                                                const float* __restrict__ col_scale,
+                                                const float* __restrict__ bias, float* __restrict__ y, bool vec_ok) {
+    float* yrow = y + (size_t)(row_ok ? row : 0) * N;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, r);
+        tmem_ld_wait();
+        const int n0 = nbase + c * 32;
+        if (!row_ok || n0 >= N) continue;
+        const float4* cs4 = reinterpret_cast<const float4*>(col_scale + n0);
+        if (vec_ok && n0 + 32 <= N) {
+            const float4* b4 = bias ? reinterpret_cast<const float4*>(bias + n0) : nullptr;
+            float4* dst = reinterpret_cast<float4*>(yrow + n0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float4 s = __ldg(cs4 + j);
+                float4 o;
+                if (b4) {
+                    const float4 b = __ldg(b4 + j);
+                    o.x = zq_epilogue_bias((int32_t)r[4 * j + 0], sr, s.x, b.x);
+                    o.y = zq_epilogue_bias((int32_t)r[4 * j + 1], sr, s.y, b.y);
+                    o.z = zq_epilogue_bias((int32_t)r[4 * j + 2], sr, s.z, b.z);
+                    o.w = zq_epilogue_bias((int32_t)r[4 * j + 3], sr, s.w, b.w);
+                } else {
+                    o.x = zq_epilogue((int32_t)r[4 * j + 0], sr, s.x);
+                    o.y = zq_epilogue((int32_t)r[4 * j + 1], sr, s.y);
+                    o.z = zq_epilogue((int32_t)r[4 * j + 2], sr, s.z);
+                    o.w = zq_epilogue((int32_t)r[4 * j + 3], sr, s.w);
+                }
+                dst[j] = o;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int n = n0 + j;
+                if (n < N) {
+                    const float sc = __ldg(col_scale + n);
+                    yrow[n] = bias ? zq_epilogue_bias((int32_t)r[j], sr, sc, __ldg(bias + n))
+                                   : zq_epilogue((int32_t)r[j], sr, sc);
+                }
+            }
+        }
+    }
+}
+
 // Tile order: groups of `group_m` M-tiles; inside a group the M-tile index
 // runs fastest, then the N-tile.  The CTAs running at the same time then
 // share a few A panels (activation rows) and B panels (weight columns) in L2.
@@ -209,7 +247,11 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
     nt = r / gm;
 }
 
-template <int BN, int STAGES>
+// kGather: the output goes to several GPUs' buffers (the all-gather fused
+// into the matmul).  A separate instantiation keeps the single-destination
+// epilogue lean: the gather path's staging roughly doubles the epilogue
+// warps' registers and costs the plain matmul about 8 % when compiled in.
+template <int BN, int STAGES, bool kGather>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    int M, int N, int Kp, const float* __restrict__ row_scale,
@@ -339,6 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int quarter = warp & 3;
         int acc = 0;
         uint32_t acc_phase = 0;
+        const bool vec1 = out.vec != 0;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
             int mt, nt;
             tile_coords(t, m_tiles, n_tiles, group_m, mt, nt);
@@ -347,15 +390,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int row0 = mt * kBM + quarter * 32;
             const int row = row0 + lane;
             const float sr = row < M ? __ldg(row_scale + row) : 0.0f;
-            float* stage = epi_stage + quarter * 32 * kEpiPitch;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+            if constexpr (!kGather) {
+                store_tile_rows<BN>(taddr, row, row < M, nt * BN, N, sr, col_scale, bias, out.base[0], vec1);
+            } else {
+                float* stage = epi_stage + quarter * 32 * kEpiPitch;
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(taddr + c * 32, r);
-                tmem_ld_wait();
-                const int n0 = nt * BN + c * 32;
-                if (row0 < M && n0 < N) store_block(r, stage, row0, lane, M, n0, N, sr, col_scale, bias, out);
+                for (int c = 0; c < BN / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(taddr + c * 32, r);
+                    tmem_ld_wait();
+                    const int n0 = nt * BN + c * 32;
+                    if (row0 < M && n0 < N) store_block(r, stage, row0, lane, M, n0, N, sr, col_scale, bias, out);
+                }
             }
             tmem_fence_before();
             mbar_arrive(&tempty[acc]);
@@ -363,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
-    if (out.count > 1 && warp >= 2) __threadfence_system();  // peer stores performed before the grid ends
+    if (kGather && warp >= 2) __threadfence_system();  // peer stores performed before the grid ends
     tmem_fence_before();
     __syncthreads();
     tmem_fence_after();
@@ -373,11 +420,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// Anything but one dense [M, N] output (several destinations, a row pitch
+// wider than N, a column offset) takes the staged general epilogue.
+bool general_output(const GemmArgs& a) {
+    return a.out.count != 1 || a.out.ldy != (long long)a.N || a.out.col_offset != 0;
+}
+
 template <int BN, int STAGES>
 cudaError_t launch_gemm_t(const GemmArgs& a, cudaStream_t stream, bool pdl) {
     using S = Smem<BN, STAGES>;
-    auto kern = gemm_i8_kernel<BN, STAGES>;
-    const int smem = S::kTotal + (a.out.count > 1 ? kEpiBytes : 0);
+    const bool gather = general_output(a);
+    auto kern = gather ? gemm_i8_kernel<BN, STAGES, true> : gemm_i8_kernel<BN, STAGES, false>;
+    const int smem = S::kTotal + (gather ? kEpiBytes : 0);
     cudaError_t e = ensure_smem_attr(kern, smem);
     if (e != cudaSuccess) return e;
     const int sms = sm_count();
@@ -476,6 +530,7 @@ __device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
         : "memory");
 }
 
+template <bool kGather>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                         int M, int N, int Kp, const float* __restrict__ row_scale,
@@ -614,6 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tempty_leader = map_to_rank(&tempty[0], 0);
         int acc = 0;
         uint32_t acc_phase = 0;
+        const bool vec1 = out.vec != 0;
         for (int t = cluster; t < num_tiles; t += clusters) {
             int mt, nt;
             tile_coords(t, m_tiles, n_tiles, group_m, mt, nt);
@@ -622,15 +678,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int row0 = mt * 256 + (int)rank * 128 + quarter * 32;
             const int row = row0 + lane;
             const float sr = row < M ? __ldg(row_scale + row) : 0.0f;
-            float* stage = epi_stage + quarter * 32 * kEpiPitch;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * 256);
+            if constexpr (!kGather) {
+                store_tile_rows<256>(taddr, row, row < M, nt * 256, N, sr, col_scale, bias, out.base[0], vec1);
+            } else {
+                float* stage = epi_stage + quarter * 32 * kEpiPitch;
 #pragma unroll 1
-            for (int c = 0; c < 256 / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(taddr + c * 32, r);
-                tmem_ld_wait();
-                const int n0 = nt * 256 + c * 32;
-                if (row0 < M && n0 < N) store_block(r, stage, row0, lane, M, n0, N, sr, col_scale, bias, out);
+                for (int c = 0; c < 256 / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(taddr + c * 32, r);
+                    tmem_ld_wait();
+                    const int n0 = nt * 256 + c * 32;
+                    if (row0 < M && n0 < N) store_block(r, stage, row0, lane, M, n0, N, sr, col_scale, bias, out);
+                }
             }
             tmem_fence_before();
             mbar_arrive_cluster(tempty_leader + (uint32_t)(acc * sizeof(uint64_t)));
@@ -638,7 +698,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
-    if (out.count > 1 && warp >= 2) __threadfence_system();  // peer stores performed before the grid ends
+    if (kGather && warp >= 2) __threadfence_system();  // peer stores performed before the grid ends
     tmem_fence_before();
     cluster_sync_all();  // no CTA leaves while its peer may still signal its barriers
     tmem_fence_after();
@@ -650,8 +710,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 cudaError_t launch_gemm_pair(const GemmArgs& a, cudaStream_t stream, bool pdl) {
     using S = Smem2;
-    auto kern = gemm_i8_pair_kernel;
-    const int smem = S::kTotal + (a.out.count > 1 ? kEpiBytes : 0);
+    const bool gather = general_output(a);
+    auto kern = gather ? gemm_i8_pair_kernel<true> : gemm_i8_pair_kernel<false>;
+    const int smem = S::kTotal + (gather ? kEpiBytes : 0);
     cudaError_t e = ensure_smem_attr(kern, smem);
     if (e != cudaSuccess) return e;
     const int sms = sm_count();

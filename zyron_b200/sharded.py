@@ -85,7 +85,8 @@ def sharded_matmul(x, weight_shard, n_cols: int, group=None, gather: bool = True
 class PeerOutputs:
     """A full [rows, cols] fp32 output on every rank of the process group,
     each rank holding device pointers to all the others' copies (CUDA IPC
-    through torch's tensor sharing; peer access over NVLink).
+    handles from ``zq_ipc_export``, opened with ``zq_ipc_import`` while this
+    rank's device is current, so its kernels reach them over NVLink).
 
     ``sharded_matmul_gathered`` lets the matmul epilogue store every output
     tile straight into all these buffers (``zq_matmul_multi``), so the

@@ -443,28 +443,32 @@ def run_gemv_workload(args):
                     _lib.check(L.zq_matmul(Ws[i % copies].handle, C.c_void_p(x.data_ptr()), M, None,
                                            C.c_void_p(y.data_ptr()), C.c_void_p(wp), wsb, sp))
 
-                for name, fn in (("gemv_kernel", kernel_only), ("matmul_call", full_call)):
-                    for i in range(copies):
-                        fn(i)
-                    s.synchronize()
-                    reps = 10 * copies
-                    graph = torch.cuda.CUDAGraph()
-                    with torch.cuda.graph(graph, stream=s):
-                        for i in range(reps):
+                for kname, kind in (("tensor_core", 1), ("cuda_core", 2)):
+                    L.zq_set_decode_kernel(kind)
+                    res[kname] = {}
+                    for name, fn in (("kernel", kernel_only), ("matmul_call", full_call)):
+                        for i in range(copies):
                             fn(i)
-                    for _ in range(args.warmup):
-                        graph.replay()
-                    s.synchronize()
-                    a, b = torch.cuda.Event(True), torch.cuda.Event(True)
-                    a.record(s)
-                    for _ in range(args.steps):
-                        graph.replay()
-                    b.record(s)
-                    s.synchronize()
-                    us = a.elapsed_time(b) / (args.steps * reps) * 1e3
-                    byts = payload + 4 * N + M * Kp + 4 * M * N
-                    res[name] = {"us": us, "GBs": byts / us / 1e3, "frac_of_hbm": byts / us / 1e3 / peak}
-                    del graph
+                        s.synchronize()
+                        reps = 10 * copies
+                        graph = torch.cuda.CUDAGraph()
+                        with torch.cuda.graph(graph, stream=s):
+                            for i in range(reps):
+                                fn(i)
+                        for _ in range(args.warmup):
+                            graph.replay()
+                        s.synchronize()
+                        a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+                        a.record(s)
+                        for _ in range(args.steps):
+                            graph.replay()
+                        b.record(s)
+                        s.synchronize()
+                        us = a.elapsed_time(b) / (args.steps * reps) * 1e3
+                        byts = payload + 4 * N + M * Kp + 4 * M * N
+                        res[kname][name] = {"us": us, "GBs": byts / us / 1e3, "frac_of_hbm": byts / us / 1e3 / peak}
+                        del graph
+                L.zq_set_decode_kernel(0)
             cases[f"{'int8' if qt == 1 else 'int4'}_M{M}"] = res
     # end to end through the host entry point (M=1, INT8): pinned host x in, host y out
     W0 = zb.quantize(torch.randn((K, N), device=dev).mul_(0.02), zb.Type.Int8)
@@ -486,13 +490,14 @@ def run_gemv_workload(args):
         cpu = {"value": (K * N) / tc / 1e9, "unit": "GB/s", "cores": 1, "kind": kind,
                "sample": f"M=1 x K={K} x N={N} INT8, best of 3 (the reference splits work over rows, so M=1 runs on "
                          f"one thread whatever the thread count)"}
-    head = cases["int8_M1"]["gemv_kernel"]
+    head = cases["int8_M1"]["tensor_core"]["kernel"]
     line = {"metric": "decode GEMV weight-stream bandwidth (quantization::matmul, M=1 INT8)", "value": head["GBs"],
             "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["us"] / 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": "decode_gemv_K4096_N11008", "M": [1, 8], "types": ["int8", "int4"],
                        "l2": "weights rotate over enough copies to stream > 2 x L2 per pass"},
-            "roofline": {"bound": "hbm", "kernel": "gemv_kernel", "achieved": head["GBs"], "peak": peak,
+            "roofline": {"bound": "hbm", "kernel": "skinny_kernel<int8> (tcgen05 decode, stream-K over 148 SMs)",
+                         "achieved": head["GBs"], "peak": peak,
                          "unit": "GB/s", "frac": head["frac_of_hbm"], "peak_source": peak_src,
                          "bytes_per_launch": K * N + 4 * N + 16 * ((K + 15) // 16) + 4 * N},
             "cases": cases,

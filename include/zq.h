@@ -212,6 +212,19 @@ zq_status zq_ipc_close(void* dev_ptr);
  * free SMs.  Returns the previous value. */
 int zq_set_reserved_sms(int sms);
 
+/* Which kernel runs plain matmuls with few activation rows (process-wide):
+ *   ZQ_DECODE_TENSOR_CORE: the tcgen05 decode kernel for m <= 16 (weights
+ *     streamed by TMA, work split evenly over the SMs);
+ *   ZQ_DECODE_CUDA_CORE: the dp4a warp-per-column GEMV for m <= 8;
+ *   ZQ_DECODE_AUTO (default): the GEMV for m <= 4, the tcgen05 kernel for
+ *     5 <= m <= 16.
+ * Larger m always runs the tcgen05 GEMM.  Results are identical.  Returns the
+ * previous value. */
+#define ZQ_DECODE_AUTO 0
+#define ZQ_DECODE_TENSOR_CORE 1
+#define ZQ_DECODE_CUDA_CORE 2
+int zq_set_decode_kernel(int kind);
+
 /* Synchronise `stream`, then read and clear the current device's error word
  * (0 = none; otherwise which bounded wait gave up).  Returns
  * ZQ_ERR_DEVICE_TIMEOUT when the word was set. */

@@ -1,0 +1,130 @@
+"""Decode-sized matmuls (M <= 16 activation rows) bit for bit against the
+oracle, through both decode kernels: the tcgen05 kernel (weights streamed by
+TMA, work split evenly over the SMs with exact int32 partial sums) and the
+dp4a warp-per-column GEMV (M <= 8).
+
+The shapes stress the split: N not a multiple of the 128-column block, K not
+a multiple of the 128-code k-block, one column block shared by 64 CTAs,
+blocks of a single k-block, and more CTAs than column blocks.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TENSOR_CORE, CUDA_CORE = 1, 2
+
+DECODE_SHAPES = [
+    (1, 1, 1), (1, 64, 7), (1, 4096, 1000), (2, 31, 33), (3, 129, 255), (4, 8192, 64), (5, 1000, 300),
+    (7, 12288, 129), (8, 4096, 1100), (8, 33, 1), (9, 200, 130), (12, 3000, 777), (16, 4096, 2048),
+    (16, 100, 5000),
+]
+
+
+def bits(a):
+    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+
+
+def assert_bits_equal(got, want, what):
+    g, w = bits(got), bits(want)
+    if not np.array_equal(g, w):
+        bad = np.argwhere(g != w)
+        i = tuple(bad[0])
+        raise AssertionError(f"{what}: {len(bad)} mismatches, first at {i}: got {got[i]!r} want {want[i]!r}")
+
+
+@pytest.fixture(scope="module")
+def zb(cuda):
+    import zyron_b200
+
+    return zyron_b200
+
+
+@pytest.fixture
+def decode_kernel(zb):
+    L = zb._lib.lib()
+    prev = L.zq_set_decode_kernel(0)
+    L.zq_set_decode_kernel(prev)
+
+    def use(kind):
+        L.zq_set_decode_kernel(kind)
+
+    yield use
+    L.zq_set_decode_kernel(prev)
+
+
+def _case(M, K, N, qt):
+    rng = np.random.default_rng(M * 1009 + K * 13 + N * 7 + qt)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    w = (rng.standard_normal((K, N)) * 0.02).astype(np.float32)
+    if M > 1:
+        x[1] = 0.0
+    if M > 2:
+        x[2, 0] = np.nan
+    if M > 3:
+        x[3, K // 2] = np.inf
+    b = rng.standard_normal(N).astype(np.float32)
+    return x, w, b
+
+
+@pytest.mark.parametrize("kernel", [TENSOR_CORE, CUDA_CORE])
+@pytest.mark.parametrize("qt", [1, 2])
+@pytest.mark.parametrize("M,K,N", DECODE_SHAPES)
+def test_decode_matmul_bit_exact(zb, decode_kernel, kernel, qt, M, K, N):
+    import torch
+
+    if kernel == CUDA_CORE and M > 8:
+        pytest.skip("the dp4a GEMV serves M <= 8")
+    decode_kernel(kernel)
+    x, w, b = _case(M, K, N, qt)
+    pay, sc = O.quantize_weights(w, qt)
+    W = zb.QuantizedMatrix.from_parts(qt, K, N, sc, pay)
+    xd = torch.from_numpy(x).cuda()
+    y = zb.matmul(xd, W).cpu().numpy()
+    _, _, _, yo = O.matmul(x, qt, pay, sc, N)
+    assert_bits_equal(y, yo, f"matmul t{qt} {M}x{K}x{N}")
+    yb = zb.matmul(xd, W, bias=torch.from_numpy(b).cuda()).cpu().numpy()
+    _, _, _, ybo = O.matmul(x, qt, pay, sc, N, b)
+    assert_bits_equal(yb, ybo, f"linear t{qt} {M}x{K}x{N}")
+    assert zb.device_error() == 0
+
+
+@pytest.mark.parametrize("qt", [1, 2])
+def test_decode_codes_entry_reuses_workspace(zb, decode_kernel, qt):
+    """zq_matmul_codes (no quantizer before it) clears the kernel's tickets
+    itself; repeated calls on one workspace, with a different weight in
+    between, stay exact."""
+    import torch
+
+    decode_kernel(TENSOR_CORE)
+    L = zb._lib.lib()
+    M, K = 6, 5000
+    cases = []
+    for N in (700, 129):
+        x, w, b = _case(M, K, N, qt)
+        pay, sc = O.quantize_weights(w, qt)
+        W = zb.QuantizedMatrix.from_parts(qt, K, N, sc, pay)
+        _, _, _, yo = O.matmul(x, qt, pay, sc, N, b)
+        cases.append((x, b, W, yo, N))
+    need = max(L.zq_matmul_workspace_bytes(W.handle, M) for _, _, W, _, _ in cases)
+    ws = torch.empty(need + 256, dtype=torch.uint8, device="cuda")
+    ws_ptr = (ws.data_ptr() + 255) & ~255
+    for rep in range(3):
+        for x, b, W, yo, N in cases:
+            Kp = L.zq_weight_padded_k(W.handle)
+            xd = torch.from_numpy(x).cuda()
+            codes = torch.empty((M, Kp), dtype=torch.int8, device="cuda")
+            rs = torch.empty((M,), dtype=torch.float32, device="cuda")
+            zb._lib.check(L.zq_quantize_rows(C.c_void_p(xd.data_ptr()), M, K, C.c_void_p(codes.data_ptr()), Kp,
+                                             C.c_void_p(rs.data_ptr()), None))
+            y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+            bd = torch.from_numpy(b).cuda()
+            zb._lib.check(L.zq_matmul_codes(W.handle, C.c_void_p(codes.data_ptr()), C.c_void_p(rs.data_ptr()), M,
+                                            C.c_void_p(bd.data_ptr()), C.c_void_p(y.data_ptr()), C.c_void_p(ws_ptr),
+                                            need, None))
+            assert_bits_equal(y.cpu().numpy(), yo, f"codes entry t{qt} N={N} rep {rep}")
+    assert zb.device_error() == 0

@@ -103,6 +103,7 @@ SIGNATURES = {
     "zq_dequantize": (st, [vp, vp, vp]),
     "zq_device_error": (st, [vp, C.POINTER(C.c_uint32)]),
     "zq_set_reserved_sms": (C.c_int, [C.c_int]),
+    "zq_set_decode_kernel": (C.c_int, [C.c_int]),
     "zq_ipc_export": (st, [vp, vp]),
     "zq_ipc_import": (st, [vp, C.POINTER(vp)]),
     "zq_ipc_close": (st, [vp]),

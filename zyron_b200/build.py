@@ -22,8 +22,9 @@ LIB = os.path.join(HERE, "libzyron_b200.so")
 QLIB = os.path.join(HERE, "libzyron_quant.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
-CU_SOURCES = ["zq_api.cu", "zq_quant.cu", "zq_gemv.cu", "zq_gemm_sm100.cu", "zq_noalloc.cu", "zq_lm.cu"]
-CU_HEADERS = ["zq_common.cuh", "zq_dot.cuh", "zq_kernels.h", "zq_internal.h"]
+CU_SOURCES = ["zq_api.cu", "zq_quant.cu", "zq_gemv.cu", "zq_gemm_sm100.cu", "zq_skinny_sm100.cu", "zq_noalloc.cu",
+              "zq_lm.cu"]
+CU_HEADERS = ["zq_common.cuh", "zq_dot.cuh", "zq_tcgen05.cuh", "zq_kernels.h", "zq_internal.h"]
 CPP_SOURCES = ["src/quantization.cpp", "src/quantized_linear.cpp", "src/tensor.cpp"]
 
 NVCC_FLAGS = [

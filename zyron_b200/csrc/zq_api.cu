@@ -17,6 +17,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
+#include <atomic>
 #include <cstring>
 #include <limits>
 #include <mutex>
@@ -206,6 +207,27 @@ int gemm_group_m() {
         return e ? std::atoi(e) : 32;
     }();
     return g;
+}
+
+// Packed INT4 panel [N][Kp/2] bytes, box 64 bytes (128 codes) x 128 columns,
+// unswizzled: the decode kernel unpacks it in shared memory.
+zq_status encode_packed_int4(CUtensorMap* map, const void* base, size_t cols, int Kp) {
+    zq_status s = get_encoder();
+    if (s != ZQ_OK) return s;
+    cuuint64_t dims[2] = {(cuuint64_t)(Kp / 2), (cuuint64_t)cols};
+    cuuint64_t strides[1] = {(cuuint64_t)(Kp / 2)};
+    cuuint32_t box[2] = {64u, 128u};
+    cuuint32_t estr[2] = {1u, 1u};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        char buf[160];
+        std::snprintf(buf, sizeof buf, "zyron_b200: cuTensorMapEncodeTiled failed (%d) cols=%zu Kp=%d (packed)",
+                      (int)r, cols, Kp);
+        return fail(ZQ_ERR_CUDA, buf);
+    }
+    return ZQ_OK;
 }
 
 int tile_index(int block_n) {
@@ -453,8 +475,15 @@ zq_status zq_weight_destroy(zq_weight* w) {
 size_t zq_matmul_workspace_bytes(const zq_weight* w, size_t m) {
     if (!w || m == 0) return 0;
     size_t b = align256(m * (size_t)w->Kp) + align256(m * sizeof(float));
-    if (w->type == ZQ_TYPE_INT4 && m > (size_t)zq::kGemvMaxRows) b += align256(w->N * (size_t)w->Kp);
-    return b;
+    // scratch: decode counters and partial sums (m <= 16), or the INT4 panel
+    // expanded to int8 for the tensor-core GEMM (m > 8)
+    size_t scratch = 0;
+    if (m <= (size_t)zq::kSkinnyMaxRows) scratch = zq::skinny_scratch_bytes((int)w->N, (int)m);
+    if (w->type == ZQ_TYPE_INT4 && m > (size_t)zq::kGemvMaxRows) {
+        const size_t e = align256(w->N * (size_t)w->Kp);
+        if (e > scratch) scratch = e;
+    }
+    return b + scratch;
 }
 
 zq_status zq_quantize_rows(const float* x, size_t m, size_t k, int8_t* q, size_t ldq, float* row_scale,
@@ -509,6 +538,9 @@ zq::OutDesc single_output(float* y, size_t N) {
 // Dot + epilogue on activation codes q [m][Kp] (row stride Kp) and row
 // scales rs; the GEMM path writes through `out` (several destinations when
 // gathering), the GEMV path to out.base[0] with row stride N.
+// Kernel for decode-sized matmuls (zq_set_decode_kernel).
+std::atomic<int> g_decode_kernel{ZQ_DECODE_AUTO};
+
 zq_status run_codes_out(const zq_weight* w, const int8_t* codes, const float* rs, size_t m, const float* bias,
                         const zq::OutDesc& out, uint8_t* scratch, cudaStream_t st, bool pdl);
 
@@ -525,9 +557,51 @@ zq_status run_codes_out(const zq_weight* w, const int8_t* codes, const float* rs
     if (s != ZQ_OK) return s;
     const int M = (int)m, N = (int)w->N, Kp = w->Kp;
     const bool plain = out.count == 1 && out.ldy == (long long)N && out.col_offset == 0;
-    if (plain && M <= zq::kGemvMaxRows && zq::gemv_smem_bytes(M, Kp) <= 200 * 1024) {
+    const int decode = g_decode_kernel.load(std::memory_order_relaxed);
+    const bool gemv_ok = plain && M <= zq::kGemvMaxRows && zq::gemv_smem_bytes(M, Kp) <= 200 * 1024;
+    // Default: the dp4a GEMV for 1-4 rows, where the weight stream alone
+    // sets the time and it has the least fixed cost per launch; the tensor
+    // cores above that, where dp4a and shared-memory reads of the activation
+    // rows limit the GEMV.
+    const bool use_gemv = gemv_ok && (decode == ZQ_DECODE_CUDA_CORE || (decode == ZQ_DECODE_AUTO && M <= 4));
+    if (use_gemv) {
         zq::GemvArgs a{w->type, w->panel, N, Kp, w->scales, codes, rs, bias, y, M};
         ZQ_CUDA(zq::launch_gemv(a, st, pdl));
+        return ZQ_OK;
+    }
+    if (plain && M <= zq::kSkinnyMaxRows) {
+        // Tensor-core decode kernel.  Its counters must be zero when it
+        // starts: the quantizer of this call cleared them (pdl: it ran just
+        // before), otherwise a zeroing kernel does.
+        int* counters = reinterpret_cast<int*>(scratch);
+        int* partials = reinterpret_cast<int*>(scratch + align256((size_t)zq::skinny_counter_words(N) * sizeof(int)));
+        if (!pdl) ZQ_CUDA(zq::launch_zero_words(counters, zq::skinny_counter_words(N), st));
+        CUtensorMap tmap_x;
+        s = encode_kmajor(&tmap_x, codes, m, Kp, 16);
+        if (s != ZQ_OK) return s;
+        const CUtensorMap* tmap_w = nullptr;
+        {
+            zq_weight* mw = const_cast<zq_weight*>(w);
+            std::lock_guard<std::mutex> lk(mw->mu);
+            if (w->type == ZQ_TYPE_INT8) {
+                const int ti = tile_index(zq::kPairBlockN);  // 128 columns x 128 B, swizzled
+                if (!mw->tmap_ready[ti]) {
+                    s = encode_kmajor(&mw->tmap_b[ti], w->panel, w->N, Kp, box_rows_b(zq::kPairBlockN));
+                    if (s != ZQ_OK) return s;
+                    mw->tmap_ready[ti] = true;
+                }
+                tmap_w = &mw->tmap_b[ti];
+            } else {
+                if (!mw->tmap_w4_ready) {
+                    s = encode_packed_int4(&mw->tmap_w4, w->panel, w->N, Kp);
+                    if (s != ZQ_OK) return s;
+                    mw->tmap_w4_ready = true;
+                }
+                tmap_w = &mw->tmap_w4;
+            }
+        }
+        zq::SkinnyArgs a{w->type, tmap_w, &tmap_x, M, N, Kp, rs, w->scales, bias, y, counters, partials, err};
+        ZQ_CUDA(zq::launch_skinny(a, st, true));
         return ZQ_OK;
     }
     const int bn = zq::gemm_block_n(M, N);
@@ -566,7 +640,11 @@ zq_status matmul_in_workspace_out(const zq_weight* w, const float* x, size_t m, 
     int8_t* codes = reinterpret_cast<int8_t*>(ws);
     float* rs = reinterpret_cast<float*>(ws + align256(m * (size_t)w->Kp));
     uint8_t* scratch = ws + align256(m * (size_t)w->Kp) + align256(m * sizeof(float));
-    ZQ_CUDA(zq::launch_quantize_rows(x, (int)m, (int)w->K, w->Kp, codes, rs, st));
+    // m <= 16: the decode kernel's counters sit at the start of the scratch
+    // and the quantizer clears them.
+    int* counters = m <= (size_t)zq::kSkinnyMaxRows ? reinterpret_cast<int*>(scratch) : nullptr;
+    const int n_counters = counters ? zq::skinny_counter_words((int)w->N) : 0;
+    ZQ_CUDA(zq::launch_quantize_rows(x, (int)m, (int)w->K, w->Kp, codes, rs, st, counters, n_counters));
     return run_codes_out(w, codes, rs, m, bias, out, scratch, st, true);
 }
 
@@ -813,6 +891,11 @@ zq_status zq_dequantize_host(const zq_weight* w, float* out_host, void* stream) 
 }
 
 int zq_set_reserved_sms(int sms) { return zq::set_reserved_sms(sms); }
+
+int zq_set_decode_kernel(int kind) {
+    if (kind < ZQ_DECODE_AUTO || kind > ZQ_DECODE_CUDA_CORE) kind = ZQ_DECODE_AUTO;
+    return g_decode_kernel.exchange(kind);
+}
 
 zq_status zq_ipc_export(const void* dev_ptr, zq_ipc_handle* out) {
     if (!dev_ptr || !out) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null argument");

@@ -28,6 +28,7 @@ enum : uint32_t {
     kDevErrTimeoutMma = 2,
     kDevErrTimeoutEpilogue = 3,
     kDevErrTimeoutDrain = 4,
+    kDevErrTimeoutPeer = 5,  // a CTA waited for another CTA's partial sums
 };
 
 // ---------------------------------------------------------------------------
@@ -94,6 +95,24 @@ __device__ __forceinline__ void zq_unpack_int4x8(uint32_t w, uint32_t& even, uin
     // v | ((v & 8) * 0x1E) per byte sets the high nibble to 0xF for negatives.
     even = lo | ((lo & 0x08080808u) * 0x1Eu);
     odd = hi | ((hi & 0x08080808u) * 0x1Eu);
+}
+
+// 32 packed INT4 codes (16 bytes, low nibble = even k) -> 32 int8 codes in
+// k order: codes 0..15 in `lo`, 16..31 in `hi`.
+__device__ __forceinline__ void zq_expand_int4x32(const uint4& w, uint4& lo, uint4& hi) {
+    uint32_t e[4], o[4];
+    zq_unpack_int4x8(w.x, e[0], o[0]);
+    zq_unpack_int4x8(w.y, e[1], o[1]);
+    zq_unpack_int4x8(w.z, e[2], o[2]);
+    zq_unpack_int4x8(w.w, e[3], o[3]);
+    lo.x = __byte_perm(e[0], o[0], 0x5140);
+    lo.y = __byte_perm(e[0], o[0], 0x7362);
+    lo.z = __byte_perm(e[1], o[1], 0x5140);
+    lo.w = __byte_perm(e[1], o[1], 0x7362);
+    hi.x = __byte_perm(e[2], o[2], 0x5140);
+    hi.y = __byte_perm(e[2], o[2], 0x7362);
+    hi.z = __byte_perm(e[3], o[3], 0x5140);
+    hi.w = __byte_perm(e[3], o[3], 0x7362);
 }
 
 // ---------------------------------------------------------------------------

@@ -27,6 +27,7 @@
 // own in-flight copies and MMAs, frees TMEM and returns.
 #include "zq_common.cuh"
 #include "zq_kernels.h"
+#include "zq_tcgen05.cuh"
 
 #include <cuda.h>
 
@@ -60,64 +61,7 @@ struct Smem {
     static constexpr int kTotal = 1024 /*alignment slack*/ + STAGES * kStageBytes + kBarrierBytes;
 };
 
-__device__ __forceinline__ uint64_t make_sw128_desc(uint32_t saddr) {
-    // tcgen05 shared-memory matrix descriptor: K-major, 128-byte swizzle,
-    // 8-row core groups 1024 B apart (SBO), LBO unused for this layout.
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-    d |= (uint64_t)(1u) << 16;            // LBO (ignored for swizzled K-major)
-    d |= (uint64_t)(1024u >> 4) << 32;    // SBO
-    d |= (uint64_t)1 << 46;               // descriptor version (sm_100)
-    d |= (uint64_t)2 << 61;               // SWIZZLE_128B
-    return d;
-}
 
-template <int BN>
-__host__ __device__ constexpr uint32_t make_idesc_i8() {
-    return (2u << 4)                 // D format: s32
-           | (1u << 7)               // A: signed 8-bit
-           | (1u << 10)              // B: signed 8-bit
-           | (0u << 15) | (0u << 16) // both K-major
-           | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
-}
-
-__device__ __forceinline__ void tmem_fence_before() {
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_fence_after() {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                        uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-          "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
-          "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
-          "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Several destinations (other GPUs' outputs over NVLink: the all-gather
 // fused into the matmul).  The warp's 32 x 32 block (lane = row row0+lane,
@@ -342,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = make_idesc_i8<BN>();
+            constexpr uint32_t idesc = idesc_i8(kBM, BN);
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
@@ -476,9 +420,6 @@ struct Smem2 {
     static constexpr int kTotal = 1024 + kStages2 * kStageBytes + kBarrierBytes;
 };
 
-__host__ __device__ constexpr uint32_t make_idesc_i8_m256() {
-    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
-}
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;
@@ -628,7 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0 && leader) {
-            constexpr uint32_t idesc = make_idesc_i8_m256();
+            constexpr uint32_t idesc = idesc_i8(256, 256);
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;

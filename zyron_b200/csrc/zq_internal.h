@@ -25,6 +25,9 @@ struct zq_weight {
     std::mutex mu;
     CUtensorMap tmap_b[4];
     bool tmap_ready[4] = {false, false, false, false};
+    // INT4: tensor map over the packed panel for the decode kernel.
+    CUtensorMap tmap_w4;
+    bool tmap_w4_ready = false;
 };
 
 namespace zq {

@@ -57,8 +57,10 @@ struct GemmArgs {
     int group_m;  // tile-order group size in M-tiles (0 = all M-tiles)
 };
 
+// `zero` (n_zero ints, may be NULL) is cleared by the same launch: the
+// decode kernel's counters, so that zeroing them costs no launch of its own.
 cudaError_t launch_quantize_rows(const float* x, int M, int K, int Kp, int8_t* q, float* row_scale,
-                                 cudaStream_t stream);
+                                 cudaStream_t stream, int* zero = nullptr, int n_zero = 0);
 cudaError_t launch_repack_int4(const uint8_t* src, int K, int N, int Kp, uint8_t* dst, cudaStream_t stream);
 cudaError_t launch_unpack_panel_int4(const uint8_t* panel, int K, int N, int Kp, uint8_t* dst,
                                      cudaStream_t stream);
@@ -70,6 +72,30 @@ cudaError_t launch_expand_int4(const uint8_t* panel4, int N, int Kp, int8_t* pan
 
 size_t gemv_smem_bytes(int M, int Kp);
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl);
+
+// Decode-sized matmul on tensor cores (zq_skinny_sm100.cu), M <= 16.
+constexpr int kSkinnyMaxRows = 16;
+constexpr int kSkinnyMaxCtas = 256;
+struct SkinnyArgs {
+    int type;
+    const CUtensorMap* tmap_w;  // INT8: [N][Kp] box 128 B x 128 rows, 128B swizzle; INT4: [N][Kp/2] box 64 B x 128 rows
+    const CUtensorMap* tmap_x;  // codes [M][Kp], box 128 B x 16 rows, 128B swizzle
+    int M, N, Kp;
+    const float* row_scale;
+    const float* col_scale;
+    const float* bias;
+    float* y;
+    int* counters;  // skinny_counter_words(N), zero when the kernel starts
+    int* partials;  // kSkinnyMaxCtas * 2 * M * 128
+    uint32_t* err;
+};
+int skinny_blocks(int N);
+// Arrival and publication counters of the split blocks (8 per block).
+int skinny_counter_words(int N);
+// Scratch of one decode launch: counters, then partial sums (256-byte aligned).
+size_t skinny_scratch_bytes(int N, int M);
+cudaError_t launch_zero_words(int* p, int n, cudaStream_t stream);
+cudaError_t launch_skinny(const SkinnyArgs& a, cudaStream_t stream, bool pdl);
 
 int gemm_block_n(int M, int N);
 

@@ -22,11 +22,18 @@ namespace zq {
 // One warp per row: pass 1 reduces |x| with fmaxf (NaN skipped, like
 // std::max), pass 2 writes codes; the [K, Kp) tail is zero-filled.
 // ---------------------------------------------------------------------------
+// Block 0 also clears `zero[0, n_zero)` (see launch_quantize_rows).
+__device__ __forceinline__ void clear_words(int* zero, int n_zero) {
+    if (blockIdx.x == 0)
+        for (int i = threadIdx.x; i < n_zero; i += blockDim.x) zero[i] = 0;
+}
+
 template <bool kVec>
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restrict__ x, int M, int K,
                                                             int Kp, int8_t* __restrict__ q,
-                                                            float* __restrict__ row_scale) {
+                                                            float* __restrict__ row_scale, int* zero, int n_zero) {
     pdl_launch_dependents();
+    clear_words(zero, n_zero);
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= M) return;
@@ -73,8 +80,10 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restr
 template <int kWarpsPerRow, int kVec>
 __global__ void __launch_bounds__(256) quantize_rows_reg_kernel(const float* __restrict__ x, int M, int K, int Kp,
                                                                 int8_t* __restrict__ q,
-                                                                float* __restrict__ row_scale) {
+                                                                float* __restrict__ row_scale, int* zero,
+                                                                int n_zero) {
     pdl_launch_dependents();
+    clear_words(zero, n_zero);
     constexpr int kRowsPerBlock = 8 / kWarpsPerRow;
     constexpr int kT = 32 * kWarpsPerRow;
     __shared__ float part[8];
@@ -122,7 +131,7 @@ __global__ void __launch_bounds__(256) quantize_rows_reg_kernel(const float* __r
 }
 
 cudaError_t launch_quantize_rows(const float* x, int M, int K, int Kp, int8_t* q, float* row_scale,
-                                 cudaStream_t stream) {
+                                 cudaStream_t stream, int* zero, int n_zero) {
     if (M <= 0) return cudaSuccess;
     const bool aligned = (K % 4 == 0) && (Kp % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) &&
                          ((reinterpret_cast<uintptr_t>(q) & 3u) == 0);
@@ -133,10 +142,10 @@ cudaError_t launch_quantize_rows(const float* x, int M, int K, int Kp, int8_t* q
         const int rows_per_block = 8 / wpr;
         const dim3 grid((M + rows_per_block - 1) / rows_per_block);
         switch (wpr) {
-            case 1: quantize_rows_reg_kernel<1, 8><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale); break;
-            case 2: quantize_rows_reg_kernel<2, 8><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale); break;
-            case 4: quantize_rows_reg_kernel<4, 8><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale); break;
-            default: quantize_rows_reg_kernel<8, 8><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale); break;
+            case 1: quantize_rows_reg_kernel<1, 8><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale, zero, n_zero); break;
+            case 2: quantize_rows_reg_kernel<2, 8><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale, zero, n_zero); break;
+            case 4: quantize_rows_reg_kernel<4, 8><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale, zero, n_zero); break;
+            default: quantize_rows_reg_kernel<8, 8><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale, zero, n_zero); break;
         }
         return cudaGetLastError();
     }
@@ -145,9 +154,9 @@ cudaError_t launch_quantize_rows(const float* x, int M, int K, int Kp, int8_t* q
     const bool vec = (K % 4 == 0) && (Kp % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) &&
                      ((reinterpret_cast<uintptr_t>(q) & 3u) == 0);
     if (vec)
-        quantize_rows_kernel<true><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale);
+        quantize_rows_kernel<true><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale, zero, n_zero);
     else
-        quantize_rows_kernel<false><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale);
+        quantize_rows_kernel<false><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale, zero, n_zero);
     return cudaGetLastError();
 }
 
@@ -381,22 +390,8 @@ namespace zq {
 __global__ void expand_int4_kernel(const uint4* __restrict__ src, size_t chunks, uint4* __restrict__ dst) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < chunks;
          i += (size_t)gridDim.x * blockDim.x) {
-        const uint4 w = src[i];
-        uint32_t e[4], o[4];
-        zq_unpack_int4x8(w.x, e[0], o[0]);
-        zq_unpack_int4x8(w.y, e[1], o[1]);
-        zq_unpack_int4x8(w.z, e[2], o[2]);
-        zq_unpack_int4x8(w.w, e[3], o[3]);
-        // interleave even/odd codes back into linear k order
         uint4 a, b;
-        a.x = __byte_perm(e[0], o[0], 0x5140);
-        a.y = __byte_perm(e[0], o[0], 0x7362);
-        a.z = __byte_perm(e[1], o[1], 0x5140);
-        a.w = __byte_perm(e[1], o[1], 0x7362);
-        b.x = __byte_perm(e[2], o[2], 0x5140);
-        b.y = __byte_perm(e[2], o[2], 0x7362);
-        b.z = __byte_perm(e[3], o[3], 0x5140);
-        b.w = __byte_perm(e[3], o[3], 0x7362);
+        zq_expand_int4x32(src[i], a, b);
         dst[2 * i] = a;
         dst[2 * i + 1] = b;
     }

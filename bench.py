@@ -406,6 +406,24 @@ def run_gemv_workload(args):
     dev = torch.device("cuda:0")
     K, N = 4096, 11008
     peak, peak_src = hbm_peak()
+    if args.once:
+        # profiling aid: three eager zq_matmul calls per case and decode
+        # kernel, in the order int8 M=1, M=8, int4 M=1, M=8, each with the
+        # tensor-core kernel first, then the dp4a GEMV; no timing
+        g = torch.Generator(device=dev)
+        g.manual_seed(2)
+        for qt in (1, 2):
+            W = zb.quantize(torch.randn((K, N), generator=g, device=dev).mul_(0.02), zb.Type(qt))
+            for M in (1, 8):
+                x = torch.randn((M, K), generator=g, device=dev)
+                for kind in (1, 2):
+                    L.zq_set_decode_kernel(kind)
+                    for _ in range(3):
+                        y = zb.matmul(x, W)
+                L.zq_set_decode_kernel(0)
+        torch.cuda.synchronize()
+        print(json.dumps({"workload": "decode_gemv_K4096_N11008", "once": True, "checksum": float(y.abs().sum())}))
+        return
     s = torch.cuda.Stream()
     cases = {}
     for qt in (1, 2):
@@ -490,13 +508,17 @@ def run_gemv_workload(args):
         cpu = {"value": (K * N) / tc / 1e9, "unit": "GB/s", "cores": 1, "kind": kind,
                "sample": f"M=1 x K={K} x N={N} INT8, best of 3 (the reference splits work over rows, so M=1 runs on "
                          f"one thread whatever the thread count)"}
-    head = cases["int8_M1"]["tensor_core"]["kernel"]
+    # the default dispatch (ZQ_DECODE_AUTO) runs the dp4a GEMV for M <= 4 and
+    # the tensor-core kernel above; the headline is the kernel it picks
+    for key, c in cases.items():
+        c["default"] = "cuda_core" if key.endswith("_M1") else "tensor_core"
+    head = cases["int8_M1"]["cuda_core"]["kernel"]
     line = {"metric": "decode GEMV weight-stream bandwidth (quantization::matmul, M=1 INT8)", "value": head["GBs"],
             "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["us"] / 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": "decode_gemv_K4096_N11008", "M": [1, 8], "types": ["int8", "int4"],
                        "l2": "weights rotate over enough copies to stream > 2 x L2 per pass"},
-            "roofline": {"bound": "hbm", "kernel": "skinny_kernel<int8> (tcgen05 decode, stream-K over 148 SMs)",
+            "roofline": {"bound": "hbm", "kernel": "gemv_kernel<int8, M=1> (dp4a, warp per column)",
                          "achieved": head["GBs"], "peak": peak,
                          "unit": "GB/s", "frac": head["frac_of_hbm"], "peak_source": peak_src,
                          "bytes_per_launch": K * N + 4 * N + 16 * ((K + 15) // 16) + 4 * N},
@@ -660,6 +682,8 @@ def main():
                     help="prefill (default line), gemv (decode GEMV), small (64x512x512 INT8 and "
                          "128x2048x2048 INT4) or qlm (LM decode)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling runs)")
+    ap.add_argument("--once", action="store_true",
+                    help="--workload gemv: a few untimed calls of each decode kernel (for ncu captures)")
     ap.add_argument("--shape", type=lambda v: tuple(int(t) for t in v.split(",")),
                     default=(M_ROWS, K_DIM, N_COLS), help="M,K,N override for small profiling cases")
     args = ap.parse_args()

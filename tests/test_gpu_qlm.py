@@ -24,8 +24,20 @@ def qgold():
     return np.load(os.path.join(ROOT, "tests", "golden", "qlm_golden.npz"))
 
 
+@pytest.fixture(params=["kernel_chain", "persistent"])
+def decode_path(request, monkeypatch):
+    """Both device decode loops: the chain of per-phase kernels replayed from
+    CUDA graphs (default) and the persistent cooperative kernel
+    (ZQ_LM_PERSISTENT=1)."""
+    if request.param == "persistent":
+        monkeypatch.setenv("ZQ_LM_PERSISTENT", "1")
+    else:
+        monkeypatch.delenv("ZQ_LM_PERSISTENT", raising=False)
+    return request.param
+
+
 @pytest.mark.parametrize("name", ["rope_gqa_int8", "rope_gqa_int4", "pe_layernorm_mha_int8", "rope_mqa_odd_int8"])
-def test_greedy_generation_matches_reference(cuda, qgold, name):
+def test_greedy_generation_matches_reference(cuda, qgold, name, decode_path):
     from zyron_b200.qlm import GenerationConfig, QuantizedLanguageModel
 
     lm = QuantizedLanguageModel.load_bytes(qgold[f"{name}_model"].tobytes())
@@ -39,11 +51,11 @@ def test_greedy_generation_matches_reference(cuda, qgold, name):
     err = float(np.abs(logits - ref_logits).max())
     assert err <= LOGIT_RTOL * span, f"{name}: max logit error {err:.3g} (range {span:.3g})"
     assert toks == want.tolist(), f"{name}: {toks} vs {want.tolist()}"
-    # graph-replay path (no per-step logits) gives the same tokens
+    # without per-step logits (graph replay in the kernel chain) the same tokens
     assert lm.generate(prompt.tolist(), cfg) == want.tolist()
 
 
-def test_generation_stops_at_context(cuda, qgold):
+def test_generation_stops_at_context(cuda, qgold, decode_path):
     from zyron_b200.qlm import GenerationConfig, QuantizedLanguageModel
 
     lm = QuantizedLanguageModel.load_bytes(qgold["rope_gqa_int8_model"].tobytes())

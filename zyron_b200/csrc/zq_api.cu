@@ -668,6 +668,8 @@ zq_status matmul_with_scratch(const zq_weight* w, const float* x, size_t m, cons
 
 zq_status set_error(zq_status s, const char* msg) { return fail(s, msg); }
 
+zq_status device_error_word(uint32_t** out) { return device_error_ptr(out); }
+
 zq_status parse_zyq(const void* bytes, size_t len, ZyqRecord* rec) {
     const uint8_t* p = static_cast<const uint8_t*>(bytes);
     size_t off = 0;

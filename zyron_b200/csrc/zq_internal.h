@@ -53,4 +53,8 @@ zq_status concat_cols(zq_weight* const* parts, int n, void* stream, zq_weight** 
 // Records a CUDA failure as the calling thread's last error.
 zq_status cuda_error(cudaError_t e, const char* what);
 
+// The current device's error word, where bounded device waits record a
+// timeout (read and cleared by zq_device_error).
+zq_status device_error_word(uint32_t** out);
+
 }  // namespace zq

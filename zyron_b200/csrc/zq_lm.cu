@@ -42,6 +42,7 @@
 #include <cmath>
 #include <cstdio>
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <limits>
 #include <string>
@@ -143,6 +144,59 @@ __global__ void embed_kernel(const uint8_t* __restrict__ panel, int type, int Kp
 }
 
 // ---------------------------------------------------------------------------
+// The row prologue of every decode linear: xs[0, K) holds the activation row
+// (fp32, shared memory, [K, Kp) zero).  Optional RMSNorm / LayerNorm (norm
+// 284-319) in place, then the per-row activation quantizer
+// (quantization.cpp:202-212) into qs: INT8 codes in k order, or for INT4
+// weights split even/odd per group of 8 codes to match the nibble unpack.
+// Returns the row scale.  Every thread of the block calls it.
+// ---------------------------------------------------------------------------
+template <int kNT>
+__device__ float quantize_row(float* xs, int8_t* qs, int K, int Kp, int type, int pro, const float* __restrict__ nw,
+                              const float* __restrict__ nb, float eps, float* red) {
+    if (pro == kProRms) {
+        float ss = 0.0f;
+        for (int i = threadIdx.x; i < K; i += kNT) ss = __fadd_rn(ss, __fmul_rn(xs[i], xs[i]));
+        ss = block_sum<kNT>(ss, red);
+        const float var = __fdiv_rn(ss, (float)K);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+        for (int i = threadIdx.x; i < K; i += kNT) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), nw[i]);
+        __syncthreads();
+    } else if (pro == kProLayer) {
+        float sm = 0.0f;
+        for (int i = threadIdx.x; i < K; i += kNT) sm = __fadd_rn(sm, xs[i]);
+        sm = block_sum<kNT>(sm, red);
+        const float mean = __fdiv_rn(sm, (float)K);
+        float ss = 0.0f;
+        for (int i = threadIdx.x; i < K; i += kNT) {
+            const float c = __fsub_rn(xs[i], mean);
+            ss = __fadd_rn(ss, __fmul_rn(c, c));
+        }
+        ss = block_sum<kNT>(ss, red);
+        const float var = __fdiv_rn(ss, (float)K);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+        for (int i = threadIdx.x; i < K; i += kNT)
+            xs[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xs[i], mean), inv), nw[i]), nb[i]);
+        __syncthreads();
+    }
+    float m = 0.0f;
+    for (int i = threadIdx.x; i < K; i += kNT) m = fmaxf(m, fabsf(xs[i]));
+    m = block_max<kNT>(m, red);
+    const float s = zq_scale_from_absmax(m, 127.0f);
+    for (int i = threadIdx.x; i < Kp; i += kNT) {
+        const int8_t code = i < K ? (int8_t)zq_quantize_value(xs[i], s, 127) : (int8_t)0;
+        if (type == kInt8) {
+            qs[i] = code;
+        } else {
+            const int g = i & ~7, r = i & 7;
+            qs[g + ((r & 1) ? 4 + (r >> 1) : (r >> 1))] = code;
+        }
+    }
+    __syncthreads();
+    return s;
+}
+
+// ---------------------------------------------------------------------------
 // One QuantizedLinear on a single activation row, with the operations around
 // it fused:
 //   prologue  optional RMSNorm / LayerNorm of x (norm 284-319), then the
@@ -188,46 +242,7 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const float* __restric
 
     for (int i = threadIdx.x; i < Kp; i += kThreads) xs[i] = i < K ? __ldcg(x + i) : 0.0f;
     __syncthreads();
-    if (kPro == kProRms) {
-        float ss = 0.0f;
-        for (int i = threadIdx.x; i < K; i += kThreads) ss = __fadd_rn(ss, __fmul_rn(xs[i], xs[i]));
-        ss = block_sum<kThreads>(ss, red);
-        const float var = __fdiv_rn(ss, (float)K);
-        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-        for (int i = threadIdx.x; i < K; i += kThreads) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), nw[i]);
-        __syncthreads();
-    } else if (kPro == kProLayer) {
-        float sm = 0.0f;
-        for (int i = threadIdx.x; i < K; i += kThreads) sm = __fadd_rn(sm, xs[i]);
-        sm = block_sum<kThreads>(sm, red);
-        const float mean = __fdiv_rn(sm, (float)K);
-        float ss = 0.0f;
-        for (int i = threadIdx.x; i < K; i += kThreads) {
-            const float c = __fsub_rn(xs[i], mean);
-            ss = __fadd_rn(ss, __fmul_rn(c, c));
-        }
-        ss = block_sum<kThreads>(ss, red);
-        const float var = __fdiv_rn(ss, (float)K);
-        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-        for (int i = threadIdx.x; i < K; i += kThreads)
-            xs[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xs[i], mean), inv), nw[i]), nb[i]);
-        __syncthreads();
-    }
-    float m = 0.0f;
-    for (int i = threadIdx.x; i < K; i += kThreads) m = fmaxf(m, fabsf(xs[i]));
-    m = block_max<kThreads>(m, red);
-    const float s = zq_scale_from_absmax(m, 127.0f);
-    for (int i = threadIdx.x; i < Kp; i += kThreads) {
-        const int8_t code = i < K ? (int8_t)zq_quantize_value(xs[i], s, 127) : (int8_t)0;
-        if (kType == kInt8) {
-            qs[i] = code;
-        } else {
-            // even/odd split per group of 8 codes, matching the nibble unpack
-            const int g = i & ~7, r = i & 7;
-            qs[g + ((r & 1) ? 4 + (r >> 1) : (r >> 1))] = code;
-        }
-    }
-    __syncthreads();
+    const float s = quantize_row<kThreads>(xs, qs, K, Kp, kType, kPro, nw, nb, eps, red);
 
     for (int col = first_col; col < N; col += warps_total) {
         const uint8_t* wc = panel + (size_t)col * cb;
@@ -479,6 +494,825 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
     }
 }
 
+// ===========================================================================
+// Persistent decode: the whole greedy generation in one cooperative launch.
+//
+// The multi-kernel step above pays a launch and a dependency hand-over for
+// each of its ~5 kernels per layer, and every one of them is latency-bound
+// (a few MB of weights per kernel).  Here one CTA per SM runs every step; the
+// phases of a step are separated by a grid barrier, and before arriving at a
+// barrier each warp already loads everything of the next phase that does not
+// depend on it: its weight columns, their scales and biases, the residual
+// values it will add, and each thread its norm weights.  After the barrier
+// only the activation row, its norm and quantization, the dots and the
+// stores remain.  Per step and layer:
+//   A  (layer 0: embedding lookup) norm1 -> quantize -> q|k|v columns
+//   B  attention items (KV group, 64-position chunk): RoPE, KV append by the
+//      first chunk, scores, chunk softmax, partial context (m, l, c)
+//   C  merge the chunks' (m, l, c) into the context row -> out_proj columns,
+//      residual add into h
+//   D  norm2 -> ff_up columns, GELU
+//   E  ff_down columns, residual add into h
+// then, when the step's logits are needed, the final norm and lm_head
+// columns; the greedy argmax is folded into that phase (per-CTA maximum of
+// an order-preserving key, one 64-bit atomicMax per CTA) and every CTA reads
+// the chosen token after the next barrier.
+//
+// Each thread owns the row elements tid, tid + 512, ... in every phase, so a
+// row needs no barrier between its load and its reductions; a block
+// reduction costs one __syncthreads.  Every barrier wait is bounded: on
+// timeout the kernel records an error and all CTAs leave at their next
+// barrier.  Data written by other CTAs is read through L2 (ld.global.cg).
+// ===========================================================================
+constexpr int kStepThreads = 512;
+constexpr int kStepWarps = kStepThreads / 32;
+constexpr int kPreSlots = 8;          // 16-byte weight chunks per lane loaded before a barrier
+constexpr int kMaxColsPerWarp = 8;    // columns one warp reduces at once
+constexpr int kHeadBatch = 4;         // query heads of a KV group handled together
+constexpr int kAttnPosPerWarp = kAttnChunk / kStepWarps;  // 4
+constexpr int kRowRegs = 4;           // norm weights per thread held in registers (K <= 2048)
+constexpr int kMergeChunks = 12;      // attention chunks merged from registers (contexts <= 768)
+
+struct LinDesc {
+    const uint8_t* panel;
+    const float* scales;
+    const float* bias;
+    int K, Kp, N;
+};
+
+struct LayerDesc {
+    LinDesc qkv, out, up, down;
+    const float *n1w, *n1b, *n2w, *n2b;
+    int rms1, rms2;
+};
+
+struct StepParams {
+    const LayerDesc* layers;
+    int n_layers;
+    LinDesc head;
+    const float* final_w;
+    const uint8_t* emb_panel;
+    const float* emb_scales;
+    int emb_Kp;
+    const float* pe;
+    const float* rcos;
+    const float* rsin;
+    float* h;
+    float* qkv;
+    float* ff;
+    float* part;  // [heads][n_chunks_max][kMaxHeadDim + 2]
+    float* kc;
+    float* vc;
+    int32_t* tokens;
+    State* state;
+    unsigned long long* keys;  // [2] argmax keys, by step parity
+    int* nan_flags;            // [2]
+    unsigned int* bar;         // grid barrier arrivals (zero at launch)
+    float* step_logits;        // [new tokens][V] or null
+    uint32_t* err;
+    int H, F, V, heads, kvh, hd, max_seq, n_chunks_max, xmax;
+    float eps, scale;
+    int prompt_len, n_steps;
+};
+
+__device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Grid-wide barrier of a cooperative launch (all CTAs resident): the k-th
+// barrier of the launch waits for the arrival counter to reach k * gridDim.
+// Returns false when this or another CTA gave up on a wait.
+__device__ bool grid_barrier(unsigned int* ctr, unsigned int target, uint32_t* err, int* flag_sh) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int ok = *(volatile uint32_t*)err == kDevErrNone;
+        if (ok) {
+            // release: this CTA's writes (ordered before by __syncthreads)
+            // are visible to whoever observes the arrival
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+            if (ld_acquire_u32(ctr) < target) {
+                const uint64_t t0 = global_timer_ns();
+                uint32_t spins = 0;
+                while (ld_acquire_u32(ctr) < target) {
+                    if ((++spins & 255u) == 0u) {
+                        if (*(volatile uint32_t*)err != kDevErrNone) {
+                            ok = 0;
+                            break;
+                        }
+                        if (global_timer_ns() - t0 > 4000000000ull) {
+                            atomicCAS(err, kDevErrNone, kDevErrTimeoutPeer);
+                            ok = 0;
+                            break;
+                        }
+                    }
+                }
+            }
+        }
+        *flag_sh = ok;
+    }
+    __syncthreads();
+    return *flag_sh != 0;
+}
+
+// Block reductions with one __syncthreads: the r-th reduction of a row
+// prologue writes its warp partials to buffer r of three 32-float buffers
+// (a row needs at most three; the prologue ends with a barrier before the
+// next one starts), and every thread adds the partials in the same order.
+__device__ __forceinline__ float block_sum1(float v, float* red, int& rsel) {
+    v = warp_sum(v);
+    float* b = red + 32 * rsel;
+    ++rsel;
+    if ((threadIdx.x & 31) == 0) b[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kStepWarps; ++w) t = __fadd_rn(t, b[w]);
+    return t;
+}
+__device__ __forceinline__ float block_max1(float v, float* red, int& rsel) {
+    v = warp_max(v);
+    float* b = red + 32 * rsel;
+    ++rsel;
+    if ((threadIdx.x & 31) == 0) b[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = b[0];
+#pragma unroll
+    for (int w = 1; w < kStepWarps; ++w) t = fmaxf(t, b[w]);
+    return t;
+}
+
+struct NormPre {
+    float w[kRowRegs], b[kRowRegs];
+};
+
+__device__ __forceinline__ void prefetch_norm(const float* nw, const float* nb, int K, NormPre& np) {
+#pragma unroll
+    for (int k = 0; k < kRowRegs; ++k) {
+        const int i = threadIdx.x + kStepThreads * k;
+        np.w[k] = (nw && i < K) ? nw[i] : 0.0f;
+        np.b[k] = (nb && i < K) ? nb[i] : 0.0f;
+    }
+}
+
+// The row prologue of the step kernel: the same arithmetic as quantize_row
+// (norm 284-319, then quantization.cpp:202-212) on the elements this thread
+// owns, xs[tid + 512 k] for k >= 0 (already written by this thread, [K, Kp)
+// zero).  Returns the row scale; qs is complete when it returns.
+__device__ float quantize_row_step(float* xs, int8_t* qs, int K, int Kp, int type, int pro,
+                                   const float* __restrict__ nw, const float* __restrict__ nb, const NormPre& np,
+                                   float eps, float* red) {
+    const int tid = threadIdx.x;
+    int rsel = 0;
+    if (pro == kProRms) {
+        float ss = 0.0f;
+        for (int i = tid; i < K; i += kStepThreads) ss = __fadd_rn(ss, __fmul_rn(xs[i], xs[i]));
+        ss = block_sum1(ss, red, rsel);
+        const float var = __fdiv_rn(ss, (float)K);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+#pragma unroll
+        for (int k = 0; k < kRowRegs; ++k) {
+            const int i = tid + kStepThreads * k;
+            if (i < K) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), np.w[k]);
+        }
+        for (int i = tid + kStepThreads * kRowRegs; i < K; i += kStepThreads)
+            xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), nw[i]);
+    } else if (pro == kProLayer) {
+        float sm = 0.0f;
+        for (int i = tid; i < K; i += kStepThreads) sm = __fadd_rn(sm, xs[i]);
+        sm = block_sum1(sm, red, rsel);
+        const float mean = __fdiv_rn(sm, (float)K);
+        float ss = 0.0f;
+        for (int i = tid; i < K; i += kStepThreads) {
+            const float c = __fsub_rn(xs[i], mean);
+            ss = __fadd_rn(ss, __fmul_rn(c, c));
+        }
+        ss = block_sum1(ss, red, rsel);
+        const float var = __fdiv_rn(ss, (float)K);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+#pragma unroll
+        for (int k = 0; k < kRowRegs; ++k) {
+            const int i = tid + kStepThreads * k;
+            if (i < K) xs[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xs[i], mean), inv), np.w[k]), np.b[k]);
+        }
+        for (int i = tid + kStepThreads * kRowRegs; i < K; i += kStepThreads)
+            xs[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xs[i], mean), inv), nw[i]), nb[i]);
+    }
+    float m = 0.0f;
+    for (int i = tid; i < K; i += kStepThreads) m = fmaxf(m, fabsf(xs[i]));
+    m = block_max1(m, red, rsel);
+    const float s = zq_scale_from_absmax(m, 127.0f);
+    for (int i = tid; i < Kp; i += kStepThreads) {
+        const int8_t code = i < K ? (int8_t)zq_quantize_value(xs[i], s, 127) : (int8_t)0;
+        if (type == kInt8) {
+            qs[i] = code;
+        } else {
+            const int g = i & ~7, r = i & 7;
+            qs[g + ((r & 1) ? 4 + (r >> 1) : (r >> 1))] = code;
+        }
+    }
+    __syncthreads();
+    return s;
+}
+
+struct Pre {
+    uint4 w[kPreSlots];
+    float sc, bi, res;  // lane j < columns: scale, bias and residual of the warp's column j
+};
+
+// This warp's columns of L are gw, gw + W, ... (at most kMaxColsPerWarp at a
+// time); its lanes take the columns' 16-byte chunks in order, so slot u of
+// lane l holds flat chunk l + 32u.  Lane j also loads column j's scale and
+// bias and, when `res` is given, the residual value res[col].
+template <int kType>
+__device__ __forceinline__ void prefetch_cols(const LinDesc& L, int gw, int W, int lane, const float* res, Pre& pre) {
+    const int cb = kType == kInt8 ? L.Kp : (L.Kp >> 1);
+    const int chunks = cb >> 4;
+    int ncols = gw < L.N ? (L.N - gw + W - 1) / W : 0;
+    if (ncols > kMaxColsPerWarp) ncols = kMaxColsPerWarp;
+    const int total = ncols * chunks;
+    if (ncols <= 1) {
+        const uint8_t* base = L.panel + (size_t)gw * cb;
+#pragma unroll
+        for (int u = 0; u < kPreSlots; ++u) {
+            const int f = lane + 32 * u;
+            pre.w[u] = f < total ? ld_stream_u4(base + (size_t)f * 16) : make_uint4(0u, 0u, 0u, 0u);
+        }
+    } else {
+        int ci = 0, c = lane;  // flat chunk lane + 32u = column ci, chunk c
+        while (c >= chunks) c -= chunks, ++ci;
+#pragma unroll
+        for (int u = 0; u < kPreSlots; ++u) {
+            pre.w[u] = ci < ncols ? ld_stream_u4(L.panel + (size_t)(gw + ci * W) * cb + (size_t)c * 16)
+                                  : make_uint4(0u, 0u, 0u, 0u);
+            c += 32;
+            while (c >= chunks) c -= chunks, ++ci;
+        }
+    }
+    const int col = gw + lane * W;
+    const bool mine = lane < ncols;
+    pre.sc = mine ? L.scales[col] : 0.0f;
+    pre.bi = (mine && L.bias) ? L.bias[col] : 0.0f;
+    pre.res = (mine && res) ? __ldcg(res + col) : 0.0f;
+}
+
+// Dots of this warp's columns against the codes in shared memory; for every
+// column epi(col, acc, scale, bias, residual) runs on lane 0.  The first
+// round uses what prefetch_cols loaded; later rounds reload `pre` in place.
+template <int kType, class Epi>
+__device__ __forceinline__ void run_cols(const LinDesc& L, int gw, int W, int lane, Pre& pre, const float* res,
+                                         const int8_t* qs, Epi&& epi) {
+    const int cb = kType == kInt8 ? L.Kp : (L.Kp >> 1);
+    const int chunks = cb >> 4;
+    for (int first = gw, group = 0; first < L.N; first += kMaxColsPerWarp * W, ++group) {
+        int ncols = (L.N - first + W - 1) / W;
+        if (ncols > kMaxColsPerWarp) ncols = kMaxColsPerWarp;
+        const int total = ncols * chunks;
+        int acc[kMaxColsPerWarp];
+#pragma unroll
+        for (int j = 0; j < kMaxColsPerWarp; ++j) acc[j] = 0;
+        if (ncols == 1) {
+            // one column: flat chunk f is chunk f of column `first`
+            const uint8_t* base = L.panel + (size_t)first * cb;
+            for (int f0 = 0; f0 < total; f0 += 32 * kPreSlots) {
+                if (group != 0 || f0 != 0) {
+#pragma unroll
+                    for (int u = 0; u < kPreSlots; ++u) {
+                        const int f = f0 + lane + 32 * u;
+                        if (f < total) pre.w[u] = ld_stream_u4(base + (size_t)f * 16);
+                    }
+                }
+                int d[1] = {0};
+#pragma unroll
+                for (int u = 0; u < kPreSlots; ++u) {
+                    const int f = f0 + lane + 32 * u;
+                    if (f < total) {
+                        if (kType == kInt8)
+                            dot16_int8<1>(pre.w[u], qs, L.Kp, f * 16, d);
+                        else
+                            dot16_int4<1>(pre.w[u], qs, L.Kp, f * 32, d);
+                    }
+                }
+                acc[0] += d[0];
+            }
+        } else
+        for (int f0 = 0; f0 < total; f0 += 32 * kPreSlots) {
+            if (group != 0 || f0 != 0) {
+#pragma unroll
+                for (int u = 0; u < kPreSlots; ++u) {
+                    const int f = f0 + lane + 32 * u;
+                    if (f < total) {
+                        const int ci = f / chunks, c = f - ci * chunks;
+                        pre.w[u] = ld_stream_u4(L.panel + (size_t)(first + ci * W) * cb + (size_t)c * 16);
+                    }
+                }
+            }
+            int ci = 0, c = f0 + lane;  // flat chunk f0 + lane + 32u = column ci, chunk c
+            while (c >= chunks) c -= chunks, ++ci;
+#pragma unroll
+            for (int u = 0; u < kPreSlots; ++u) {
+                if (ci < ncols) {
+                    int d[1] = {0};
+                    if (kType == kInt8)
+                        dot16_int8<1>(pre.w[u], qs, L.Kp, c * 16, d);
+                    else
+                        dot16_int4<1>(pre.w[u], qs, L.Kp, c * 32, d);
+#pragma unroll
+                    for (int j = 0; j < kMaxColsPerWarp; ++j)
+                        if (j == ci) acc[j] += d[0];
+                }
+                c += 32;
+                while (c >= chunks) c -= chunks, ++ci;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kMaxColsPerWarp; ++j) {
+            if (j < ncols) {
+                int v = acc[j];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                float sc = __shfl_sync(0xffffffffu, pre.sc, j);
+                float bi = __shfl_sync(0xffffffffu, pre.bi, j);
+                float rs = __shfl_sync(0xffffffffu, pre.res, j);
+                const int col = first + j * W;
+                if (lane == 0) {
+                    if (group != 0) {
+                        sc = L.scales[col];
+                        bi = L.bias ? L.bias[col] : 0.0f;
+                        rs = res ? __ldcg(res + col) : 0.0f;
+                    }
+                    epi(col, v, sc, bi, rs);
+                }
+            }
+        }
+    }
+}
+
+// Greedy choice as one comparable 64-bit key: the logit's bits made
+// order-preserving (-0 counted as +0), then the complement of the column, so
+// the larger key is the larger logit and, on ties, the lower token id.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int col) {
+    uint32_t b = __float_as_uint(v);
+    if ((b & 0x7fffffffu) == 0u) b = 0u;
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)b << 32) | (unsigned long long)(0xffffffffu - (uint32_t)col);
+}
+__device__ __forceinline__ int token_from_key(unsigned long long key, int nan, int V) {
+    if (nan || key == 0ull) return 0;
+    const uint32_t hi = (uint32_t)(key >> 32);
+    const float best = __uint_as_float((hi & 0x80000000u) ? (hi ^ 0x80000000u) : ~hi);
+    const int idx = (int)(0xffffffffu - (uint32_t)key);
+    return (isinf(best) || idx >= V) ? 0 : idx;
+}
+
+// Query rows of heads h0 .. h0+nh-1 into q_s (row stride kMaxHeadDim), with
+// RoPE at `pos` (apply_rope 347-384) when the model uses it.
+__device__ __forceinline__ void load_queries(const StepParams& p, float* q_s, int h0, int nh, int pos, int tid) {
+    const int hd = p.hd, half = hd >> 1;
+    if (p.rcos) {
+        for (int e = tid; e < nh * half; e += kStepThreads) {
+            const int i = e / half, t = e - i * half;
+            const float* qsrc = p.qkv + (size_t)(h0 + i) * hd;
+            const float qe = __ldcg(qsrc + 2 * t), qo = __ldcg(qsrc + 2 * t + 1);
+            const float c = p.rcos[(size_t)pos * half + t], sn = p.rsin[(size_t)pos * half + t];
+            q_s[i * kMaxHeadDim + 2 * t] = __fsub_rn(__fmul_rn(qe, c), __fmul_rn(qo, sn));
+            q_s[i * kMaxHeadDim + 2 * t + 1] = __fadd_rn(__fmul_rn(qe, sn), __fmul_rn(qo, c));
+        }
+    } else {
+        for (int e = tid; e < nh * hd; e += kStepThreads) {
+            const int i = e / hd, d = e - i * hd;
+            q_s[i * kMaxHeadDim + d] = __ldcg(p.qkv + (size_t)(h0 + i) * hd + d);
+        }
+    }
+}
+
+// One attention item: query heads of KV group `grp` against positions
+// [chunk*64, chunk*64 + 64) <= pos; writes each head's (m, l, c) partial.
+__device__ __noinline__ void attention_item(const StepParams& p, int grp, int chunk, int pos, int li, float* q_s, float* kn,
+                               float* vn, float* sc, float* mh, float* wpart) {
+    constexpr int kPerLane = kMaxHeadDim / 32;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int hd = p.hd, half = hd >> 1;
+    const int rep = p.heads / p.kvh;
+    const size_t cache_layer = (size_t)p.kvh * p.max_seq * hd;
+    float* kc_l = p.kc + (size_t)li * cache_layer;
+    float* vc_l = p.vc + (size_t)li * cache_layer;
+    const float* ksrc = p.qkv + (size_t)p.heads * hd + (size_t)grp * hd;
+    const float* vsrc = p.qkv + (size_t)(p.heads + p.kvh) * hd + (size_t)grp * hd;
+    // Every load is issued before the first wait: the cached keys and values
+    // of this warp's positions, the new key and value, the first queries.
+    float kr[kAttnPosPerWarp][kPerLane], vr[kAttnPosPerWarp][kPerLane];
+#pragma unroll
+    for (int i = 0; i < kAttnPosPerWarp; ++i) {
+        const int j = chunk * kAttnChunk + warp * kAttnPosPerWarp + i;
+        const float* kj = kc_l + ((size_t)grp * p.max_seq + j) * hd;
+        const float* vj = vc_l + ((size_t)grp * p.max_seq + j) * hd;
+#pragma unroll
+        for (int r = 0; r < kPerLane; ++r) {
+            const int d = lane + 32 * r;
+            const bool cached = d < hd && j < pos;
+            kr[i][r] = cached ? __ldcg(kj + d) : 0.0f;
+            vr[i][r] = cached ? __ldcg(vj + d) : 0.0f;
+        }
+    }
+    if (p.rcos) {
+        if (tid < half) {
+            const float c = p.rcos[(size_t)pos * half + tid], sn = p.rsin[(size_t)pos * half + tid];
+            const float ke = __ldcg(ksrc + 2 * tid), ko = __ldcg(ksrc + 2 * tid + 1);
+            kn[2 * tid] = __fsub_rn(__fmul_rn(ke, c), __fmul_rn(ko, sn));
+            kn[2 * tid + 1] = __fadd_rn(__fmul_rn(ke, sn), __fmul_rn(ko, c));
+        }
+    } else if (tid < hd) {
+        kn[tid] = __ldcg(ksrc + tid);
+    }
+    if (tid < hd) vn[tid] = __ldcg(vsrc + tid);
+    load_queries(p, q_s, grp * rep, rep < kHeadBatch ? rep : kHeadBatch, pos, tid);
+    __syncthreads();
+    if (chunk == 0 && tid < hd) {
+        kc_l[((size_t)grp * p.max_seq + pos) * hd + tid] = kn[tid];
+        vc_l[((size_t)grp * p.max_seq + pos) * hd + tid] = vn[tid];
+    }
+#pragma unroll
+    for (int i = 0; i < kAttnPosPerWarp; ++i) {
+        if (chunk * kAttnChunk + warp * kAttnPosPerWarp + i == pos) {
+#pragma unroll
+            for (int r = 0; r < kPerLane; ++r) {
+                const int d = lane + 32 * r;
+                if (d < hd) kr[i][r] = kn[d], vr[i][r] = vn[d];
+            }
+        }
+    }
+    for (int hb = 0; hb < rep; hb += kHeadBatch) {
+        const int nh = rep - hb < kHeadBatch ? rep - hb : kHeadBatch;
+        if (hb > 0) {  // the previous batch ended with a barrier: q_s is free
+            load_queries(p, q_s, grp * rep + hb, nh, pos, tid);
+            __syncthreads();
+        }
+        // scores (forward_block 424-451 for the newest row)
+        for (int i2 = 0; i2 < nh; ++i2) {
+#pragma unroll
+            for (int i = 0; i < kAttnPosPerWarp; ++i) {
+                float part = 0.0f;
+#pragma unroll
+                for (int r = 0; r < kPerLane; ++r) {
+                    const int d = lane + 32 * r;
+                    if (d < hd) part = __fadd_rn(part, __fmul_rn(q_s[i2 * kMaxHeadDim + d], kr[i][r]));
+                }
+                part = warp_sum(part);
+                const int t = warp * kAttnPosPerWarp + i;
+                const int j = chunk * kAttnChunk + t;
+                if (lane == 0) sc[i2 * kAttnChunk + t] = j <= pos ? __fmul_rn(part, p.scale) : -INFINITY;
+            }
+        }
+        __syncthreads();
+        // chunk softmax: warp i2 takes head i2
+        if (warp < nh) {
+            const float a0 = sc[warp * kAttnChunk + lane], a1 = sc[warp * kAttnChunk + lane + 32];
+            const float m = warp_max(fmaxf(a0, a1));
+            const float e0 = a0 == -INFINITY ? 0.0f : expf(__fsub_rn(a0, m));
+            const float e1 = a1 == -INFINITY ? 0.0f : expf(__fsub_rn(a1, m));
+            const float l = warp_sum(__fadd_rn(e0, e1));
+            sc[warp * kAttnChunk + lane] = e0;
+            sc[warp * kAttnChunk + lane + 32] = e1;
+            if (lane == 0) mh[warp] = m, mh[kHeadBatch + warp] = l;
+        }
+        __syncthreads();
+        // partial context of this warp's positions
+        for (int i2 = 0; i2 < nh; ++i2) {
+#pragma unroll
+            for (int r = 0; r < kPerLane; ++r) {
+                float a = 0.0f;
+#pragma unroll
+                for (int i = 0; i < kAttnPosPerWarp; ++i)
+                    a = __fadd_rn(a, __fmul_rn(sc[i2 * kAttnChunk + warp * kAttnPosPerWarp + i], vr[i][r]));
+                const int d = lane + 32 * r;
+                if (d < hd) wpart[(warp * kHeadBatch + i2) * kMaxHeadDim + d] = a;
+            }
+        }
+        __syncthreads();
+        for (int e = tid; e < nh * hd; e += kStepThreads) {
+            const int i2 = e / hd, d = e - i2 * hd;
+            float c = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kStepWarps; ++w) c = __fadd_rn(c, wpart[(w * kHeadBatch + i2) * kMaxHeadDim + d]);
+            float* dst = p.part + ((size_t)(grp * rep + hb + i2) * p.n_chunks_max + chunk) * (kMaxHeadDim + 2);
+            dst[2 + d] = c;
+            if (d == 0) dst[0] = mh[i2], dst[1] = mh[kHeadBatch + i2];
+        }
+        __syncthreads();
+    }
+}
+
+// Context row of the attention: merges the chunks' (m, l, c) partials into
+// xs[o], o = heads * hd, for the elements this thread owns:
+// M = max m, L = sum l e^(m - M), ctx = (sum c e^(m - M)) / L.
+__device__ __noinline__ void merge_context(const StepParams& p, int nchunk, float* xs, float* mls, float* invl) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int H = p.H, hd = p.hd;
+    const size_t stride = kMaxHeadDim + 2;
+    const bool fast = nchunk <= kMergeChunks && H <= 2 * kStepThreads;
+    float cv[2][kMergeChunks];
+    if (fast) {  // this thread's partial contexts, loaded with the (m, l) pairs
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int o = tid + kStepThreads * k;
+            const int hq = o / hd, d = o - hq * hd;
+            const float* ph = p.part + (size_t)hq * p.n_chunks_max * stride + 2 + d;
+#pragma unroll
+            for (int c = 0; c < kMergeChunks; ++c)
+                cv[k][c] = (o < H && c < nchunk) ? __ldcg(ph + (size_t)c * stride) : 0.0f;
+        }
+    }
+    for (int e = tid; e < p.heads * nchunk; e += kStepThreads) {
+        const int hq = e / nchunk, c = e - hq * nchunk;
+        const float* pc = p.part + ((size_t)hq * p.n_chunks_max + c) * stride;
+        mls[2 * e] = __ldcg(pc);
+        mls[2 * e + 1] = __ldcg(pc + 1);
+    }
+    __syncthreads();
+    for (int hq = warp; hq < p.heads; hq += kStepWarps) {
+        float M = -INFINITY;
+        for (int c = lane; c < nchunk; c += 32) M = fmaxf(M, mls[2 * (hq * nchunk + c)]);
+        M = warp_max(M);
+        float L = 0.0f;
+        for (int c = lane; c < nchunk; c += 32) {
+            const int e = hq * nchunk + c;
+            const float f = expf(__fsub_rn(mls[2 * e], M));
+            L = __fadd_rn(L, __fmul_rn(mls[2 * e + 1], f));
+            mls[2 * e] = f;
+        }
+        L = warp_sum(L);
+        if (lane == 0) invl[hq] = L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f;
+    }
+    __syncthreads();
+    if (fast) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int o = tid + kStepThreads * k;
+            if (o < H) {
+                const int hq = o / hd;
+                float acc = 0.0f;
+#pragma unroll
+                for (int c = 0; c < kMergeChunks; ++c)
+                    if (c < nchunk) acc = __fadd_rn(acc, __fmul_rn(cv[k][c], mls[2 * (hq * nchunk + c)]));
+                xs[o] = __fmul_rn(acc, invl[hq]);
+            }
+        }
+    } else {
+        for (int o = tid; o < H; o += kStepThreads) {
+            const int hq = o / hd, d = o - hq * hd;
+            const float* ph = p.part + (size_t)hq * p.n_chunks_max * stride + 2 + d;
+            float acc = 0.0f;
+            for (int c = 0; c < nchunk; ++c)
+                acc = __fadd_rn(acc, __fmul_rn(__ldcg(ph + (size_t)c * stride), mls[2 * (hq * nchunk + c)]));
+            xs[o] = __fmul_rn(acc, invl[hq]);
+        }
+    }
+}
+
+// Per-CTA control block at the start of the step kernel's shared memory.
+struct StepCtl {
+    float red[96];
+    unsigned long long cta_key;
+    int cta_nan;
+    int flag;
+};
+constexpr int kStepCtlFloats = (int)((sizeof(StepCtl) + 15) / 16 * 4);
+
+struct StepSmem {
+    StepCtl* ctl;
+    float* xs;
+    int8_t* qs;
+    float *q_s, *kn, *vn, *sc, *mh, *wpart, *mls, *invl;
+    LayerDesc* lds;
+};
+
+__device__ __forceinline__ StepSmem step_smem(const StepParams& p) {
+    extern __shared__ __align__(16) float ssm[];
+    StepSmem m;
+    m.ctl = reinterpret_cast<StepCtl*>(ssm);
+    m.xs = ssm + kStepCtlFloats;                                       // [xmax]
+    m.qs = reinterpret_cast<int8_t*>(m.xs + p.xmax);                   // [xmax]
+    m.q_s = m.xs + p.xmax + p.xmax / 4;                                // [kHeadBatch][kMaxHeadDim]
+    m.kn = m.q_s + kHeadBatch * kMaxHeadDim;                           // [kMaxHeadDim]
+    m.vn = m.kn + kMaxHeadDim;                                         // [kMaxHeadDim]
+    m.sc = m.vn + kMaxHeadDim;                                         // [kHeadBatch][kAttnChunk]
+    m.mh = m.sc + kHeadBatch * kAttnChunk;                             // [2][kHeadBatch]
+    m.wpart = m.mh + 2 * kHeadBatch;                                   // [kStepWarps][kHeadBatch][kMaxHeadDim]
+    m.mls = m.wpart + kStepWarps * kHeadBatch * kMaxHeadDim;           // [heads][n_chunks_max][2]
+    m.invl = m.mls + 2 * p.heads * p.n_chunks_max;                     // [heads]
+    m.lds = reinterpret_cast<LayerDesc*>(m.invl + p.heads + (p.heads & 1));  // [n_layers]
+    return m;
+}
+
+enum RowSrc { kRowEmbed = 0, kRowGlobal = 1, kRowMerge = 2 };
+enum EpiKind { kEpStore = 0, kEpGelu = 1, kEpResidual = 2, kEpLogits = 3 };
+
+struct PhaseArgs {
+    LinDesc L;
+    const float* nw;
+    const float* nb;
+    int pro;
+    int row_src;      // RowSrc
+    const float* row; // kRowGlobal: the activation row in global memory
+    int K;            // row length
+    int epi;          // EpiKind
+    float* out;       // destination of the columns (kEpLogits: per-step logits or null)
+    const float* res; // kEpResidual: residual source (out itself)
+};
+
+// One decode linear as a phase of the step kernel: load this warp's weight
+// columns (and scales, biases, residuals) and this thread's norm weights,
+// wait at the grid barrier (when `barrier_target` is not 0), build and
+// quantize the activation row, then the dots and the epilogue.  Kept out of
+// line so that every phase runs the same, warm, instructions.
+template <int kType>
+__device__ __noinline__ bool linear_phase(const StepParams& p, const PhaseArgs& a, unsigned int barrier_target, int tok,
+                                          int pos, int nchunk) {
+    const StepSmem m = step_smem(p);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int W = gridDim.x * kStepWarps;
+    const int gw = blockIdx.x * kStepWarps + warp;
+    Pre pre;
+    NormPre np;
+    prefetch_cols<kType>(a.L, gw, W, lane, a.epi == kEpResidual ? a.res : nullptr, pre);
+    if (a.pro != kProNone) prefetch_norm(a.nw, a.nb, a.K, np);
+    if (barrier_target && !grid_barrier(p.bar, barrier_target, p.err, &m.ctl->flag)) return false;
+    float* xs = m.xs;
+    if (a.row_src == kRowEmbed) {
+        // token_lookup (271-282) [+ sinusoidal PE]
+        for (int j = tid; j < a.K; j += kStepThreads) {
+            int code;
+            if (kType == kInt8) {
+                code = (int8_t)p.emb_panel[(size_t)j * p.emb_Kp + tok];
+            } else {
+                const uint8_t b = p.emb_panel[(size_t)j * (p.emb_Kp >> 1) + (tok >> 1)];
+                const int nib = (tok & 1) ? (b >> 4) : (b & 0x0F);
+                code = nib < 8 ? nib : nib - 16;
+            }
+            float v = x86_mul((float)code, p.emb_scales[j]);
+            if (p.pe) v = x86_add(v, p.pe[(size_t)pos * a.K + j]);
+            xs[j] = v;
+            if (blockIdx.x == 0) p.h[j] = v;  // residual stream, read after the next barriers
+        }
+    } else if (a.row_src == kRowGlobal) {
+        for (int j = tid; j < a.K; j += kStepThreads) xs[j] = __ldcg(a.row + j);
+    } else {
+        merge_context(p, nchunk, xs, m.mls, m.invl);
+    }
+    for (int j = a.K + tid; j < a.L.Kp; j += kStepThreads) xs[j] = 0.0f;
+    if (a.epi == kEpLogits && tid == 0) m.ctl->cta_key = 0ull, m.ctl->cta_nan = 0;
+    const float srow = quantize_row_step(xs, m.qs, a.K, a.L.Kp, kType, a.pro, a.nw, a.nb, np, p.eps, m.ctl->red);
+    unsigned long long best = 0ull;
+    int nan = 0;
+    run_cols<kType>(a.L, gw, W, lane, pre, a.epi == kEpResidual ? a.res : nullptr, m.qs,
+                    [&](int col, int acc, float s_col, float b, float r) {
+                        float v = zq_epilogue(acc, srow, s_col);
+                        if (a.L.bias) v = x86_add(v, b);
+                        switch (a.epi) {
+                            case kEpStore: a.out[col] = v; break;
+                            case kEpGelu: a.out[col] = gelu_ref(v); break;
+                            case kEpResidual: a.out[col] = x86_add(r, v); break;
+                            default:
+                                if (a.out) a.out[col] = v;
+                                if (isnan(v)) {
+                                    nan = 1;
+                                } else {
+                                    const unsigned long long k = argmax_key(v, col);
+                                    if (k > best) best = k;
+                                }
+                        }
+                    });
+    if (a.epi == kEpLogits) {
+        if (lane == 0) {
+            if (best) atomicMax(&m.ctl->cta_key, best);
+            if (nan) m.ctl->cta_nan = 1;
+        }
+        __syncthreads();
+    }
+    return true;
+}
+
+template <int kType>
+__global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_constant__ StepParams p) {
+    const StepSmem m = step_smem(p);
+    const int tid = threadIdx.x;
+    const unsigned int G = gridDim.x;
+    const int H = p.H;
+
+    // layer descriptors into shared memory (read by every phase)
+    {
+        const int words = p.n_layers * (int)(sizeof(LayerDesc) / sizeof(int));
+        const int* src = reinterpret_cast<const int*>(p.layers);
+        int* dst = reinterpret_cast<int*>(m.lds);
+        for (int i = tid; i < words; i += kStepThreads) dst[i] = src[i];
+    }
+    __syncthreads();
+
+    int pos = __ldcg(&p.state->pos);
+    int tok = __ldcg(p.tokens + pos);
+    bool ok = true;
+    bool need_barrier = false;  // h was written since the last barrier
+    unsigned int nbar = 0;      // barriers passed in this launch
+    for (int step = 0; step < p.n_steps && ok; ++step, ++pos) {
+        const bool want_logits = pos + 1 >= p.prompt_len;
+        const int nchunk = (pos + kAttnChunk) / kAttnChunk;
+        for (int li = 0; li < p.n_layers && ok; ++li) {
+            const LayerDesc& Ld = m.lds[li];
+            PhaseArgs a;
+            // ---- A: (layer 0: embedding) norm1 -> q|k|v ----------------
+            a.L = Ld.qkv;
+            a.nw = Ld.n1w;
+            a.nb = Ld.n1b;
+            a.pro = Ld.rms1 ? kProRms : kProLayer;
+            a.row_src = li == 0 ? kRowEmbed : kRowGlobal;
+            a.row = p.h;
+            a.K = H;
+            a.epi = kEpStore;
+            a.out = p.qkv;
+            a.res = nullptr;
+            const bool bar_a = li > 0 || need_barrier;
+            if (bar_a) ++nbar;
+            ok = linear_phase<kType>(p, a, bar_a ? nbar * G : 0u, tok, pos, nchunk);
+            if (!ok) break;
+            // ---- B: attention items ------------------------------------
+            ++nbar;
+            ok = grid_barrier(p.bar, nbar * G, p.err, &m.ctl->flag);
+            if (!ok) break;
+            if (li == 0 && blockIdx.x == 0 && tid == 0) {
+                // every CTA has read the previous step's argmax key by now
+                p.keys[(step + 1) & 1] = 0ull;
+                p.nan_flags[(step + 1) & 1] = 0;
+            }
+            for (int item = blockIdx.x; item < p.kvh * nchunk; item += G)
+                attention_item(p, item / nchunk, item % nchunk, pos, li, m.q_s, m.kn, m.vn, m.sc, m.mh, m.wpart);
+            // ---- C: context merge -> out_proj, residual -----------------
+            a.L = Ld.out;
+            a.nw = a.nb = nullptr;
+            a.pro = kProNone;
+            a.row_src = kRowMerge;
+            a.epi = kEpResidual;
+            a.out = p.h;
+            a.res = p.h;
+            ok = linear_phase<kType>(p, a, ++nbar * G, tok, pos, nchunk);
+            if (!ok) break;
+            // ---- D: norm2 -> ff_up, GELU --------------------------------
+            a.L = Ld.up;
+            a.nw = Ld.n2w;
+            a.nb = Ld.n2b;
+            a.pro = Ld.rms2 ? kProRms : kProLayer;
+            a.row_src = kRowGlobal;
+            a.row = p.h;
+            a.epi = kEpGelu;
+            a.out = p.ff;
+            a.res = nullptr;
+            ok = linear_phase<kType>(p, a, ++nbar * G, tok, pos, nchunk);
+            if (!ok) break;
+            // ---- E: ff_down, residual -----------------------------------
+            a.L = Ld.down;
+            a.nw = a.nb = nullptr;
+            a.pro = kProNone;
+            a.row = p.ff;
+            a.K = p.F;
+            a.epi = kEpResidual;
+            a.out = p.h;
+            a.res = p.h;
+            ok = linear_phase<kType>(p, a, ++nbar * G, tok, pos, nchunk);
+        }
+        if (!ok) break;
+        need_barrier = true;
+        if (want_logits) {
+            // ---- final RMS norm (forward 492) -> lm_head -> argmax key --
+            PhaseArgs a;
+            a.L = p.head;
+            a.nw = p.final_w;
+            a.nb = nullptr;
+            a.pro = kProRms;
+            a.row_src = kRowGlobal;
+            a.row = p.h;
+            a.K = H;
+            a.epi = kEpLogits;
+            a.out = p.step_logits ? p.step_logits + (size_t)(pos + 1 - p.prompt_len) * p.V : nullptr;
+            a.res = nullptr;
+            ok = linear_phase<kType>(p, a, ++nbar * G, tok, pos, nchunk);
+            if (!ok) break;
+            if (tid == 0) {
+                if (m.ctl->cta_key) atomicMax(p.keys + (step & 1), m.ctl->cta_key);
+                if (m.ctl->cta_nan) atomicExch(p.nan_flags + (step & 1), 1);
+            }
+            ok = grid_barrier(p.bar, ++nbar * G, p.err, &m.ctl->flag);
+            if (!ok) break;
+            tok = token_from_key(__ldcg(p.keys + (step & 1)), __ldcg(p.nan_flags + (step & 1)), p.V);
+            if (blockIdx.x == 0 && tid == 0) p.tokens[pos + 1] = tok;
+            need_barrier = false;  // the argmax barrier ordered every read of h
+        } else {
+            tok = __ldcg(p.tokens + pos + 1);  // the prompt's next token
+        }
+    }
+    if (blockIdx.x == 0 && tid == 0 && ok) p.state->pos = pos;
+}
+
 }  // namespace lm
 }  // namespace zq
 
@@ -647,6 +1481,14 @@ struct zq_lm {
     std::vector<void*> allocations;
     cudaGraphExec_t graph_one = nullptr;
     cudaGraphExec_t graph_chunk = nullptr;
+    // persistent decode (step_kernel): layer descriptors, barrier, argmax keys
+    zq::lm::LayerDesc* layer_desc = nullptr;
+    unsigned int* bar = nullptr;
+    unsigned long long* keys = nullptr;
+    int* nan_flags = nullptr;
+    int step_grid = 0;  // 0: cooperative launch unavailable, use the kernel chain
+    size_t step_smem = 0;
+    int xmax = 0;
     int chunk = 16;
     // Used when the caller passes no stream: graph capture needs a stream
     // that is not a default stream.
@@ -830,6 +1672,120 @@ cudaError_t enqueue_step(zq_lm* lm, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     return launch_pdl(zq::lm::argmax_kernel, dim3(1), dim3(1024), 0, s, (const float*)lm->logits, (int)c.vocab_size,
                       lm->tokens, lm->state);
+}
+
+zq::lm::LinDesc lin_desc(const zq_weight* w, const float* bias) {
+    return zq::lm::LinDesc{w->panel, w->scales, bias, (int)w->K, w->Kp, (int)w->N};
+}
+
+// Descriptors, barrier and grid of the persistent decode kernel.  A model
+// that cannot run it (no cooperative launch, or no room for one CTA per SM)
+// keeps step_grid = 0 and decodes with the kernel chain.
+cudaError_t prepare_persistent(zq_lm* lm, cudaStream_t st) {
+    const zq_lm_info& c = lm->info;
+    std::vector<zq::lm::LayerDesc> h(lm->layers.size());
+    int kmax = lm->head->Kp;
+    for (size_t i = 0; i < lm->layers.size(); ++i) {
+        const DevLayer& L = lm->layers[i];
+        h[i].qkv = lin_desc(L.qkv, L.b_qkv);
+        h[i].out = lin_desc(L.out, L.b_out);
+        h[i].up = lin_desc(L.up, L.b_up);
+        h[i].down = lin_desc(L.down, L.b_down);
+        h[i].n1w = L.n1w;
+        h[i].n1b = L.n1b;
+        h[i].n2w = L.n2w;
+        h[i].n2b = L.n2b;
+        h[i].rms1 = L.rms1;
+        h[i].rms2 = L.rms2;
+        kmax = std::max({kmax, L.qkv->Kp, L.out->Kp, L.up->Kp, L.down->Kp});
+    }
+    cudaError_t e = dev_alloc(lm, &lm->layer_desc, h.size());
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(lm->layer_desc, h.data(), h.size() * sizeof(h[0]), cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = dev_alloc(lm, &lm->bar, 1);
+    if (e == cudaSuccess) e = dev_alloc(lm, &lm->keys, 2);
+    if (e == cudaSuccess) e = dev_alloc(lm, &lm->nan_flags, 2);
+    if (e != cudaSuccess) return e;
+    lm->xmax = (kmax + 31) / 32 * 32;
+    using namespace zq::lm;
+    const size_t att = (size_t)kHeadBatch * kMaxHeadDim + 2 * kMaxHeadDim + (size_t)kHeadBatch * kAttnChunk +
+                       2 * kHeadBatch + (size_t)kStepWarps * kHeadBatch * kMaxHeadDim +
+                       2 * c.num_heads * (size_t)lm->attn_splits + c.num_heads + (c.num_heads & 1);
+    lm->step_smem = ((size_t)kStepCtlFloats + lm->xmax + lm->xmax / 4 + att) * sizeof(float) +
+                    h.size() * sizeof(zq::lm::LayerDesc);
+    int coop = 0, sms = 0, per_sm = 0;
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, lm->device);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, lm->device);
+    const void* kern = c.type == ZQ_TYPE_INT8 ? (const void*)step_kernel<zq::kInt8> : (const void*)step_kernel<zq::kInt4>;
+    lm->step_grid = 0;
+    if (!coop || lm->step_smem > kMaxLinearSmem) return cudaSuccess;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lm->step_smem);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kStepThreads, lm->step_smem);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return cudaSuccess;
+    }
+    if (per_sm >= 1) lm->step_grid = sms;
+    return cudaSuccess;
+}
+
+// All `steps` decode steps as one cooperative launch of step_kernel.
+cudaError_t launch_persistent(zq_lm* lm, int steps, int prompt_len, float* step_logits_dev, uint32_t* err,
+                              cudaStream_t st) {
+    const zq_lm_info& c = lm->info;
+    zq::lm::StepParams p{};
+    p.layers = lm->layer_desc;
+    p.n_layers = (int)lm->layers.size();
+    p.head = lin_desc(lm->head, lm->b_head);
+    p.final_w = lm->final_w;
+    p.emb_panel = lm->emb->panel;
+    p.emb_scales = lm->emb->scales;
+    p.emb_Kp = lm->emb->Kp;
+    p.pe = lm->pe;
+    p.rcos = c.use_rope ? lm->rcos : nullptr;
+    p.rsin = c.use_rope ? lm->rsin : nullptr;
+    p.h = lm->h;
+    p.qkv = lm->qkv;
+    p.ff = lm->ff;
+    p.part = lm->attn_part;
+    p.kc = lm->kc;
+    p.vc = lm->vc;
+    p.tokens = lm->tokens;
+    p.state = lm->state;
+    p.keys = lm->keys;
+    p.nan_flags = lm->nan_flags;
+    p.bar = lm->bar;
+    p.step_logits = step_logits_dev;
+    p.err = err;
+    p.H = (int)c.hidden_size;
+    p.F = (int)c.intermediate_size;
+    p.V = (int)c.vocab_size;
+    p.heads = (int)c.num_heads;
+    p.kvh = (int)(c.num_kv_heads == 0 ? c.num_heads : c.num_kv_heads);
+    p.hd = (int)(c.hidden_size / c.num_heads);
+    p.max_seq = (int)c.max_sequence_length;
+    p.n_chunks_max = lm->attn_splits;
+    p.xmax = lm->xmax;
+    p.eps = c.norm_eps;
+    p.scale = 1.0f / std::sqrt(static_cast<float>(p.hd));
+    p.prompt_len = prompt_len;
+    p.n_steps = steps;
+    cudaError_t e = cudaMemsetAsync(lm->bar, 0, sizeof(unsigned int), st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(lm->keys, 0, 2 * sizeof(unsigned long long), st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(lm->nan_flags, 0, 2 * sizeof(int), st);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)lm->step_grid);
+    cfg.blockDim = dim3(zq::lm::kStepThreads);
+    cfg.dynamicSmemBytes = lm->step_smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return c.type == ZQ_TYPE_INT8 ? cudaLaunchKernelEx(&cfg, zq::lm::step_kernel<zq::kInt8>, p)
+                                  : cudaLaunchKernelEx(&cfg, zq::lm::step_kernel<zq::kInt4>, p);
 }
 
 cudaError_t build_graph(zq_lm* lm, int steps, cudaGraphExec_t* out, cudaStream_t s) {
@@ -1048,6 +2004,7 @@ zq_status zq_lm_load(const void* bytes, size_t len, void* stream, zq_lm** out) {
         if (e == cudaSuccess) e = cudaMemcpyAsync(lm->rsin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice, st);
         if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     }
+    if (e == cudaSuccess) e = prepare_persistent(lm, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&lm->own_stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) return cleanup(zq::cuda_error(e, "language model upload"));
@@ -1097,7 +2054,24 @@ zq_status zq_lm_generate_greedy(zq_lm* lm, const int64_t* prompt, size_t prompt_
     LM_CUDA(cudaMemcpyAsync(lm->state, &s0, sizeof s0, cudaMemcpyHostToDevice, st));
 
     const size_t steps = prompt_len - 1 + n_new;  // last step produces the last new token
-    if (step_logits) {
+    // ZQ_LM_PERSISTENT=1: every step in one cooperative launch of
+    // step_kernel (when the device allows it); otherwise the kernel chain
+    // replayed from CUDA graphs, which measured marginally faster on B200
+    // (0.479 vs 0.487 ms per token, 768-wide 12-layer model).
+    const char* persistent = std::getenv("ZQ_LM_PERSISTENT");
+    if (lm->step_grid > 0 && persistent && persistent[0] == '1') {
+        // persistent decode: every step in one cooperative launch
+        uint32_t* err = nullptr;
+        zq_status es = zq::device_error_word(&err);
+        if (es != ZQ_OK) return es;
+        float* dlog = nullptr;
+        if (step_logits) LM_CUDA(cudaMallocAsync(&dlog, n_new * c.vocab_size * sizeof(float), st));
+        cudaError_t le = launch_persistent(lm, (int)steps, (int)prompt_len, dlog, err, st);
+        if (le == cudaSuccess && dlog)
+            le = cudaMemcpyAsync(step_logits, dlog, n_new * c.vocab_size * sizeof(float), cudaMemcpyDeviceToHost, st);
+        if (dlog) cudaFreeAsync(dlog, st);
+        LM_CUDA(le);
+    } else if (step_logits) {
         // parity mode: per step, copy the logits that chose each new token
         for (size_t i = 0; i < steps; ++i) {
             LM_CUDA(enqueue_step(lm, st));

@@ -52,7 +52,6 @@ namespace zq {
 namespace lm {
 
 constexpr int kThreads = 256;
-constexpr int kAttnThreads = 256;
 constexpr int kMaxHeadDim = 128;
 constexpr int kAttnChunk = 64;  // positions per attention block
 
@@ -64,7 +63,7 @@ struct State {
     int pad[2];
 };
 
-enum Prologue { kProNone = 0, kProRms = 1, kProLayer = 2 };
+enum Prologue { kProNone = 0, kProRms = 1, kProLayer = 2, kProMerge = 3 };
 enum Epilogue { kEpiStore = 0, kEpiGelu = 1, kEpiResidual = 2 };
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -196,6 +195,61 @@ __device__ float quantize_row(float* xs, int8_t* qs, int K, int Kp, int type, in
     return s;
 }
 
+// Attention chunk partials for the merge prologue: part[head][chunk][130]
+// holds each 64-position chunk's softmax maximum m, sum l and context c.
+struct MergeArgs {
+    const float* part;
+    int heads, hd, n_chunks_max;
+};
+
+// The context row of the newest position from its chunks' partials:
+// ctx = (sum_c c_c e^(m_c - M)) / (sum_c l_c e^(m_c - M)), M = max_c m_c, per
+// head, into xs[0, heads * hd).  `mls` holds 2 * heads * nchunk floats and
+// `invl` heads floats of shared memory.  Ends with a barrier.
+template <int kNT>
+__device__ void merge_rows(const MergeArgs& a, int nchunk, float* xs, float* mls, float* invl) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t stride = kMaxHeadDim + 2;
+    for (int e = tid; e < a.heads * nchunk; e += kNT) {
+        const int hq = e / nchunk, c = e - hq * nchunk;
+        const float* pc = a.part + ((size_t)hq * a.n_chunks_max + c) * stride;
+        mls[2 * e] = __ldcg(pc);
+        mls[2 * e + 1] = __ldcg(pc + 1);
+    }
+    __syncthreads();
+    for (int hq = warp; hq < a.heads; hq += kNT / 32) {
+        float M = -INFINITY;
+        for (int c = lane; c < nchunk; c += 32) M = fmaxf(M, mls[2 * (hq * nchunk + c)]);
+        M = warp_max(M);
+        float L = 0.0f;
+        for (int c = lane; c < nchunk; c += 32) {
+            const int e = hq * nchunk + c;
+            const float f = expf(__fsub_rn(mls[2 * e], M));
+            L = __fadd_rn(L, __fmul_rn(mls[2 * e + 1], f));
+            mls[2 * e] = f;
+        }
+        L = warp_sum(L);
+        if (lane == 0) invl[hq] = L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f;
+    }
+    __syncthreads();
+    const int H = a.heads * a.hd;
+    for (int o = tid; o < H; o += kNT) {
+        const int hq = o / a.hd, d = o - hq * a.hd;
+        const float* ph = a.part + (size_t)hq * a.n_chunks_max * stride + 2 + d;
+        float acc = 0.0f;
+        for (int c0 = 0; c0 < nchunk; c0 += 8) {
+            float cv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) cv[u] = c0 + u < nchunk ? __ldcg(ph + (size_t)(c0 + u) * stride) : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (c0 + u < nchunk) acc = __fadd_rn(acc, __fmul_rn(cv[u], mls[2 * (hq * nchunk + c0 + u)]));
+        }
+        xs[o] = __fmul_rn(acc, invl[hq]);
+    }
+    __syncthreads();
+}
+
 // ---------------------------------------------------------------------------
 // One QuantizedLinear on a single activation row, with the operations around
 // it fused:
@@ -214,7 +268,8 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const float* __restric
                                                           float eps, const uint8_t* __restrict__ panel,
                                                           const float* __restrict__ scales, int N,
                                                           const float* __restrict__ bias, float* y,
-                                                          const State* __restrict__ st, int skip_prefill) {
+                                                          const State* __restrict__ st, int skip_prefill,
+                                                          const MergeArgs merge) {
     extern __shared__ __align__(16) float lsm[];
     float* xs = lsm;                                          // [Kp] fp32 (normalised) activations
     int8_t* qs = reinterpret_cast<int8_t*>(lsm + Kp);         // [Kp] codes
@@ -240,7 +295,15 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const float* __restric
     pdl_wait_primary();
     if (skip_prefill && __ldcg(&st->pos) + 1 < __ldcg(&st->prompt_len)) return;
 
-    for (int i = threadIdx.x; i < Kp; i += kThreads) xs[i] = i < K ? __ldcg(x + i) : 0.0f;
+    if (kPro == kProMerge) {
+        // context row from the attention chunks (shared memory after xs, qs)
+        float* mls = lsm + Kp + Kp / 4;
+        const int nchunk = (__ldcg(&st->pos) + kAttnChunk) / kAttnChunk;
+        merge_rows<kThreads>(merge, nchunk, xs, mls, mls + 2 * merge.heads * merge.n_chunks_max);
+        for (int i = K + threadIdx.x; i < Kp; i += kThreads) xs[i] = 0.0f;
+    } else {
+        for (int i = threadIdx.x; i < Kp; i += kThreads) xs[i] = i < K ? __ldcg(x + i) : 0.0f;
+    }
     __syncthreads();
     const float s = quantize_row<kThreads>(xs, qs, K, Kp, kType, kPro, nw, nb, eps, red);
 
@@ -276,165 +339,6 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const float* __restric
             else y[col] = x86_add(__ldcg(y + col), v);
         }
     }
-}
-
-// ---------------------------------------------------------------------------
-// Attention for the newest row (forward_block 424-451 restricted to the last
-// query, which is all the next token needs): RoPE on q and on the new key
-// with the reference's cos/sin factors (apply_rope 347-384, precomputed on the
-// host with the same float formula), append k/v to the cache, scores =
-// (q . k_j) * 1/sqrt(head_dim) for j <= pos, softmax (44-64), context =
-// sum_j p_j v_j.  GQA: query head h reads KV head h / (heads / kv_heads)
-// (repeat_kv_heads 386-410).
-//
-// Split over positions: block (h, s) takes a contiguous chunk of at most
-// kAttnChunk positions (one thread per position, 128-bit key loads), keeps a
-// local max m_s, sum l_s and context c_s, and writes them to `part`.  The
-// block that finishes last for head h (threadfence + atomic ticket; nothing
-// waits) merges the chunks: M = max m_s, L = sum l_s e^(m_s - M),
-// context = (sum c_s e^(m_s - M)) / L, and resets the ticket.
-// ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const float* __restrict__ qkv, int heads,
-                                                                 int kv_heads, int hd, float* kc, float* vc,
-                                                                 int max_seq, const float* __restrict__ rcos,
-                                                                 const float* __restrict__ rsin,
-                                                                 const State* __restrict__ st, float scale,
-                                                                 float* part, unsigned int* tickets,
-                                                                 float* __restrict__ ctx) {
-    constexpr int kWarps = kAttnThreads / 32;
-    constexpr int kPerLane = kMaxHeadDim / 32;
-    __shared__ __align__(16) float q[kMaxHeadDim];
-    __shared__ __align__(16) float kn[kMaxHeadDim];
-    __shared__ __align__(16) float vn[kMaxHeadDim];
-    __shared__ float p_sh[kAttnChunk];
-    __shared__ float wpart[kWarps][kMaxHeadDim];
-    __shared__ float red[32];
-    __shared__ int is_last;
-    pdl_launch_dependents();
-    pdl_wait_primary();
-    const int h = blockIdx.x;
-    const int split = blockIdx.y;
-    const int nsplit = gridDim.y;
-    const int rep = heads / kv_heads;
-    const int kvh = h / rep;
-    const int pos = __ldcg(&st->pos);
-    const int tid = threadIdx.x;
-    const int warp = tid >> 5, lane = tid & 31;
-    const float* qsrc = qkv + (size_t)h * hd;
-    const float* ksrc = qkv + (size_t)heads * hd + (size_t)kvh * hd;
-    const float* vsrc = qkv + (size_t)(heads + kv_heads) * hd + (size_t)kvh * hd;
-    const int half = hd >> 1;
-    if (rcos) {
-        if (tid < half) {
-            const float c = rcos[(size_t)pos * half + tid];
-            const float sn = rsin[(size_t)pos * half + tid];
-            const float qe = __ldcg(qsrc + 2 * tid), qo = __ldcg(qsrc + 2 * tid + 1);
-            q[2 * tid] = __fsub_rn(__fmul_rn(qe, c), __fmul_rn(qo, sn));
-            q[2 * tid + 1] = __fadd_rn(__fmul_rn(qe, sn), __fmul_rn(qo, c));
-            const float ke = __ldcg(ksrc + 2 * tid), ko = __ldcg(ksrc + 2 * tid + 1);
-            kn[2 * tid] = __fsub_rn(__fmul_rn(ke, c), __fmul_rn(ko, sn));
-            kn[2 * tid + 1] = __fadd_rn(__fmul_rn(ke, sn), __fmul_rn(ko, c));
-        }
-    } else if (tid < hd) {
-        q[tid] = __ldcg(qsrc + tid);
-        kn[tid] = __ldcg(ksrc + tid);
-    }
-    if (tid < hd) vn[tid] = __ldcg(vsrc + tid);
-    __syncthreads();
-    float* kc_head = kc + (size_t)kvh * max_seq * hd;
-    float* vc_head = vc + (size_t)kvh * max_seq * hd;
-    if (h % rep == 0 && split == 0 && tid < hd) {
-        kc_head[(size_t)pos * hd + tid] = kn[tid];
-        vc_head[(size_t)pos * hd + tid] = vn[tid];
-    }
-
-    const int total = pos + 1;
-    const int chunk = (total + nsplit - 1) / nsplit;  // <= kAttnChunk by the launch's choice of nsplit
-    const int begin = split * chunk;
-    const int end = min(begin + chunk, total);
-    const int n = end > begin ? end - begin : 0;
-
-    // scores, one thread per position
-    float v = -INFINITY;
-    if (tid < n) {
-        const int j = begin + tid;
-        float d = 0.0f;
-        if (j == pos) {  // the new key, in shared memory
-            for (int i = 0; i < hd; ++i) d = __fadd_rn(d, __fmul_rn(q[i], kn[i]));
-        } else {
-            const float* kj = kc_head + (size_t)j * hd;  // global (KV cache)
-            if ((hd & 3) == 0) {  // rows start on 16-byte boundaries
-                for (int i = 0; i < hd; i += 4) {
-                    const float4 k4 = __ldcg(reinterpret_cast<const float4*>(kj + i));
-                    d = __fadd_rn(d, __fmul_rn(q[i], k4.x));
-                    d = __fadd_rn(d, __fmul_rn(q[i + 1], k4.y));
-                    d = __fadd_rn(d, __fmul_rn(q[i + 2], k4.z));
-                    d = __fadd_rn(d, __fmul_rn(q[i + 3], k4.w));
-                }
-            } else {
-                for (int i = 0; i < hd; ++i) d = __fadd_rn(d, __fmul_rn(q[i], __ldcg(kj + i)));
-            }
-        }
-        v = __fmul_rn(d, scale);
-    }
-    const float m_s = block_max<kAttnThreads>(v, red);
-    const float e = tid < n ? expf(__fsub_rn(v, m_s)) : 0.0f;
-    if (tid < kAttnChunk) p_sh[tid] = e;
-    const float l_s = block_sum<kAttnThreads>(e, red);  // also orders the p_sh writes
-
-    // chunk context: warps over positions, lanes over the head dimension
-    float acc[kPerLane];
-#pragma unroll
-    for (int r = 0; r < kPerLane; ++r) acc[r] = 0.0f;
-    for (int t = warp; t < n; t += kWarps) {
-        const int j = begin + t;
-        const float p = p_sh[t];
-        const float* vj = vc_head + (size_t)j * hd;  // global unless j == pos
-#pragma unroll
-        for (int r = 0; r < kPerLane; ++r) {
-            const int i = lane + 32 * r;
-            if (i < hd) acc[r] = __fadd_rn(acc[r], __fmul_rn(p, j == pos ? vn[i] : __ldcg(vj + i)));
-        }
-    }
-#pragma unroll
-    for (int r = 0; r < kPerLane; ++r) {
-        const int i = lane + 32 * r;
-        if (i < hd) wpart[warp][i] = acc[r];
-    }
-    __syncthreads();
-    float* mine = part + ((size_t)h * nsplit + split) * (kMaxHeadDim + 2);
-    if (tid < hd) {
-        float c = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) c = __fadd_rn(c, wpart[w][tid]);
-        mine[2 + tid] = c;
-    }
-    if (tid == 0) {
-        mine[0] = m_s;
-        mine[1] = l_s;
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) is_last = atomicAdd(tickets + h, 1u) == (unsigned)(nsplit - 1);
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    const float* hp = part + (size_t)h * nsplit * (kMaxHeadDim + 2);
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < nsplit; ++s2) M = fmaxf(M, __ldcg(hp + (size_t)s2 * (kMaxHeadDim + 2)));
-    float L = 0.0f;
-    float c = 0.0f;
-    for (int s2 = 0; s2 < nsplit; ++s2) {
-        const float* ps = hp + (size_t)s2 * (kMaxHeadDim + 2);
-        const float ls = __ldcg(ps + 1);
-        if (ls == 0.0f) continue;  // empty chunk
-        const float f = expf(__fsub_rn(__ldcg(ps), M));
-        L = __fadd_rn(L, __fmul_rn(ls, f));
-        if (tid < hd) c = __fadd_rn(c, __fmul_rn(__ldcg(ps + 2 + tid), f));
-    }
-    const float inv = L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f;
-    if (tid < hd) ctx[(size_t)h * hd + tid] = __fmul_rn(c, inv);
-    if (tid == 0) tickets[h] = 0u;
 }
 
 // ---------------------------------------------------------------------------
@@ -1004,6 +908,28 @@ __device__ __noinline__ void attention_item(const StepParams& p, int grp, int ch
     }
 }
 
+// Attention of the kernel chain: one block of 512 threads per (KV group,
+// 64-position chunk) runs attention_item; blocks of chunks past the current
+// position return at once, so one launch shape serves every position.  The
+// out_proj kernel that follows merges the chunks (kProMerge).
+constexpr int kAttnSmemFloats = kHeadBatch * kMaxHeadDim + 2 * kMaxHeadDim + kHeadBatch * kAttnChunk +
+                                2 * kHeadBatch + kStepWarps * kHeadBatch * kMaxHeadDim;
+__global__ void __launch_bounds__(kStepThreads) attn_chunk_kernel(const __grid_constant__ StepParams p, int li) {
+    extern __shared__ __align__(16) float asm_[];
+    float* q_s = asm_;
+    float* kn = q_s + kHeadBatch * kMaxHeadDim;
+    float* vn = kn + kMaxHeadDim;
+    float* sc = vn + kMaxHeadDim;
+    float* mh = sc + kHeadBatch * kAttnChunk;
+    float* wpart = mh + 2 * kHeadBatch;
+    pdl_launch_dependents();
+    pdl_wait_primary();
+    const int pos = __ldcg(&p.state->pos);
+    const int grp = blockIdx.x / p.n_chunks_max, chunk = blockIdx.x - grp * p.n_chunks_max;
+    if (chunk * kAttnChunk > pos) return;
+    attention_item(p, grp, chunk, pos, li, q_s, kn, vn, sc, mh, wpart);
+}
+
 // Context row of the attention: merges the chunks' (m, l, c) partials into
 // xs[o], o = heads * hd, for the elements this thread owns:
 // M = max m, L = sum l e^(m - M), ctx = (sum c e^(m - M)) / L.
@@ -1470,11 +1396,10 @@ struct zq_lm {
     zq_weight* head = nullptr;
     float* b_head = nullptr;
     // runtime buffers
-    float *h = nullptr, *qkv = nullptr, *ctx = nullptr, *ff = nullptr, *logits = nullptr;
+    float *h = nullptr, *qkv = nullptr, *ff = nullptr, *logits = nullptr;
     float *kc = nullptr, *vc = nullptr;
     float *rcos = nullptr, *rsin = nullptr;
     float* attn_part = nullptr;          // [heads][splits][128 + 2] chunk partials
-    unsigned int* attn_tickets = nullptr;  // [heads], zero between launches
     int attn_splits = 1;
     int32_t* tokens = nullptr;
     State* state = nullptr;
@@ -1595,6 +1520,7 @@ cudaError_t prepare_type() {
     if (e == cudaSuccess) e = prepare_linear_t<kType, kProLayer, kEpiStore>();
     if (e == cudaSuccess) e = prepare_linear_t<kType, kProLayer, kEpiGelu>();
     if (e == cudaSuccess) e = prepare_linear_t<kType, kProLayer, kEpiResidual>();
+    if (e == cudaSuccess) e = prepare_linear_t<kType, kProMerge, kEpiResidual>();
     return e;
 }
 
@@ -1607,24 +1533,27 @@ cudaError_t prepare_kernels() {
 
 template <int kType, int kPro, int kEpi>
 cudaError_t launch_linear_t(const float* x, const float* nw, const float* nb, float eps, const zq_weight* w,
-                            const float* bias, float* y, const State* st, int skip_prefill, cudaStream_t s) {
+                            const float* bias, float* y, const State* st, int skip_prefill, cudaStream_t s,
+                            zq::lm::MergeArgs merge) {
     auto kern = zq::lm::linear_kernel<kType, kPro, kEpi>;
-    const size_t smem = linear_smem(w->Kp);
+    size_t smem = linear_smem(w->Kp);
+    if (kPro == zq::lm::kProMerge) smem += (2 * (size_t)merge.heads * merge.n_chunks_max + merge.heads) * sizeof(float);
     int dev = 0, sms = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     int blocks = (int)((w->N + 7) / 8);
     if (blocks > 2 * sms) blocks = 2 * sms;
     return launch_pdl(kern, dim3(blocks), dim3(zq::lm::kThreads), smem, s, x, (int)w->K, w->Kp, nw, nb, eps,
-                      (const uint8_t*)w->panel, (const float*)w->scales, (int)w->N, bias, y, st, skip_prefill);
+                      (const uint8_t*)w->panel, (const float*)w->scales, (int)w->N, bias, y, st, skip_prefill, merge);
 }
 
 template <int kPro, int kEpi>
 cudaError_t launch_linear(const float* x, const float* nw, const float* nb, float eps, const zq_weight* w,
-                          const float* bias, float* y, const State* st, int skip_prefill, cudaStream_t s) {
+                          const float* bias, float* y, const State* st, int skip_prefill, cudaStream_t s,
+                          zq::lm::MergeArgs merge = {}) {
     return w->type == ZQ_TYPE_INT8
-               ? launch_linear_t<ZQ_TYPE_INT8, kPro, kEpi>(x, nw, nb, eps, w, bias, y, st, skip_prefill, s)
-               : launch_linear_t<ZQ_TYPE_INT4, kPro, kEpi>(x, nw, nb, eps, w, bias, y, st, skip_prefill, s);
+               ? launch_linear_t<ZQ_TYPE_INT8, kPro, kEpi>(x, nw, nb, eps, w, bias, y, st, skip_prefill, s, merge)
+               : launch_linear_t<ZQ_TYPE_INT4, kPro, kEpi>(x, nw, nb, eps, w, bias, y, st, skip_prefill, s, merge);
 }
 
 template <int kEpi>
@@ -1645,20 +1574,32 @@ cudaError_t enqueue_step(zq_lm* lm, cudaStream_t s) {
                                (const uint8_t*)lm->emb->panel, lm->emb->type, lm->emb->Kp,
                                (const float*)lm->emb->scales, hidden, (const int32_t*)lm->tokens,
                                (const State*)lm->state, (const float*)lm->pe, lm->h);
-    const size_t cache_layer = (size_t)kvh * c.max_sequence_length * hd;
-    const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
+    // attention chunks (attn_chunk_kernel) and their merge (kProMerge)
+    zq::lm::StepParams ap{};
+    ap.qkv = lm->qkv;
+    ap.part = lm->attn_part;
+    ap.kc = lm->kc;
+    ap.vc = lm->vc;
+    ap.state = lm->state;
+    ap.rcos = c.use_rope ? lm->rcos : nullptr;
+    ap.rsin = c.use_rope ? lm->rsin : nullptr;
+    ap.H = hidden;
+    ap.heads = (int)c.num_heads;
+    ap.kvh = kvh;
+    ap.hd = hd;
+    ap.max_seq = (int)c.max_sequence_length;
+    ap.n_chunks_max = lm->attn_splits;
+    ap.scale = 1.0f / std::sqrt(static_cast<float>(hd));
+    const zq::lm::MergeArgs merge{lm->attn_part, (int)c.num_heads, hd, lm->attn_splits};
     for (size_t li = 0; li < lm->layers.size() && e == cudaSuccess; ++li) {
         const DevLayer& L = lm->layers[li];
         e = launch_normed<zq::lm::kEpiStore>(L.rms1, lm->h, L.n1w, L.n1b, eps, L.qkv, L.b_qkv, lm->qkv, lm->state, 0, s);
         if (e != cudaSuccess) break;
-        e = launch_pdl(zq::lm::attention_kernel, dim3((unsigned)c.num_heads, (unsigned)lm->attn_splits),
-                       dim3(zq::lm::kAttnThreads), 0, s, (const float*)lm->qkv, (int)c.num_heads, kvh, hd,
-                       lm->kc + li * cache_layer, lm->vc + li * cache_layer, (int)c.max_sequence_length,
-                       (const float*)(c.use_rope ? lm->rcos : nullptr), (const float*)(c.use_rope ? lm->rsin : nullptr),
-                       (const State*)lm->state, scale, lm->attn_part, lm->attn_tickets, lm->ctx);
+        e = launch_pdl(zq::lm::attn_chunk_kernel, dim3((unsigned)(kvh * lm->attn_splits)), dim3(zq::lm::kStepThreads),
+                       zq::lm::kAttnSmemFloats * sizeof(float), s, ap, (int)li);
         if (e != cudaSuccess) break;
-        e = launch_linear<zq::lm::kProNone, zq::lm::kEpiResidual>(lm->ctx, nullptr, nullptr, eps, L.out, L.b_out, lm->h,
-                                                                  lm->state, 0, s);
+        e = launch_linear<zq::lm::kProMerge, zq::lm::kEpiResidual>(nullptr, nullptr, nullptr, eps, L.out, L.b_out, lm->h,
+                                                                   lm->state, 0, s, merge);
         if (e != cudaSuccess) break;
         e = launch_normed<zq::lm::kEpiGelu>(L.rms2, lm->h, L.n2w, L.n2b, eps, L.up, L.b_up, lm->ff, lm->state, 0, s);
         if (e != cudaSuccess) break;
@@ -1972,7 +1913,6 @@ zq_status zq_lm_load(const void* bytes, size_t len, void* stream, zq_lm** out) {
     const size_t T = c.max_sequence_length;
     if (e == cudaSuccess) e = dev_alloc(lm, &lm->h, H);
     if (e == cudaSuccess) e = dev_alloc(lm, &lm->qkv, H + 2 * kvh * hd);
-    if (e == cudaSuccess) e = dev_alloc(lm, &lm->ctx, H);
     if (e == cudaSuccess) e = dev_alloc(lm, &lm->ff, F);
     if (e == cudaSuccess) e = dev_alloc(lm, &lm->logits, V);
     if (e == cudaSuccess) e = dev_alloc(lm, &lm->kc, c.num_layers * kvh * T * hd);
@@ -1980,8 +1920,6 @@ zq_status zq_lm_load(const void* bytes, size_t len, void* stream, zq_lm** out) {
     lm->attn_splits = (int)((T + zq::lm::kAttnChunk - 1) / zq::lm::kAttnChunk);
     if (e == cudaSuccess)
         e = dev_alloc(lm, &lm->attn_part, c.num_heads * (size_t)lm->attn_splits * (zq::lm::kMaxHeadDim + 2));
-    if (e == cudaSuccess) e = dev_alloc(lm, &lm->attn_tickets, c.num_heads);
-    if (e == cudaSuccess) e = cudaMemsetAsync(lm->attn_tickets, 0, c.num_heads * sizeof(unsigned int), st);
     if (e == cudaSuccess) e = dev_alloc(lm, &lm->tokens, T + 2);
     if (e == cudaSuccess) e = dev_alloc(lm, &lm->state, 1);
     if (e == cudaSuccess && c.use_rope) {

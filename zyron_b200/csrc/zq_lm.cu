@@ -150,13 +150,38 @@ __global__ void embed_kernel(const uint8_t* __restrict__ panel, int type, int Kp
 // weights split even/odd per group of 8 codes to match the nibble unpack.
 // Returns the row scale.  Every thread of the block calls it.
 // ---------------------------------------------------------------------------
+// One-barrier block reductions for the row prologue: the r-th reduction of a
+// row writes its warp partials to red[32 r ..] (at most three per row, and
+// the row ends with a barrier), and every thread adds them in one order.
+template <int kNT>
+__device__ __forceinline__ float row_sum(float v, float* red, int r) {
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) red[32 * r + (threadIdx.x >> 5)] = v;
+    __syncthreads();
+    float t = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kNT / 32; ++w) t = __fadd_rn(t, red[32 * r + w]);
+    return t;
+}
+template <int kNT>
+__device__ __forceinline__ float row_max(float v, float* red, int r) {
+    v = warp_max(v);
+    if ((threadIdx.x & 31) == 0) red[32 * r + (threadIdx.x >> 5)] = v;
+    __syncthreads();
+    float t = red[32 * r];
+#pragma unroll
+    for (int w = 1; w < kNT / 32; ++w) t = fmaxf(t, red[32 * r + w]);
+    return t;
+}
+
+// `red` holds 96 floats.
 template <int kNT>
 __device__ float quantize_row(float* xs, int8_t* qs, int K, int Kp, int type, int pro, const float* __restrict__ nw,
                               const float* __restrict__ nb, float eps, float* red) {
     if (pro == kProRms) {
         float ss = 0.0f;
         for (int i = threadIdx.x; i < K; i += kNT) ss = __fadd_rn(ss, __fmul_rn(xs[i], xs[i]));
-        ss = block_sum<kNT>(ss, red);
+        ss = row_sum<kNT>(ss, red, 0);
         const float var = __fdiv_rn(ss, (float)K);
         const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
         for (int i = threadIdx.x; i < K; i += kNT) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), nw[i]);
@@ -164,14 +189,14 @@ __device__ float quantize_row(float* xs, int8_t* qs, int K, int Kp, int type, in
     } else if (pro == kProLayer) {
         float sm = 0.0f;
         for (int i = threadIdx.x; i < K; i += kNT) sm = __fadd_rn(sm, xs[i]);
-        sm = block_sum<kNT>(sm, red);
+        sm = row_sum<kNT>(sm, red, 0);
         const float mean = __fdiv_rn(sm, (float)K);
         float ss = 0.0f;
         for (int i = threadIdx.x; i < K; i += kNT) {
             const float c = __fsub_rn(xs[i], mean);
             ss = __fadd_rn(ss, __fmul_rn(c, c));
         }
-        ss = block_sum<kNT>(ss, red);
+        ss = row_sum<kNT>(ss, red, 1);
         const float var = __fdiv_rn(ss, (float)K);
         const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
         for (int i = threadIdx.x; i < K; i += kNT)
@@ -180,7 +205,7 @@ __device__ float quantize_row(float* xs, int8_t* qs, int K, int Kp, int type, in
     }
     float m = 0.0f;
     for (int i = threadIdx.x; i < K; i += kNT) m = fmaxf(m, fabsf(xs[i]));
-    m = block_max<kNT>(m, red);
+    m = row_max<kNT>(m, red, 2);
     const float s = zq_scale_from_absmax(m, 127.0f);
     for (int i = threadIdx.x; i < Kp; i += kNT) {
         const int8_t code = i < K ? (int8_t)zq_quantize_value(xs[i], s, 127) : (int8_t)0;
@@ -273,7 +298,7 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const float* __restric
     extern __shared__ __align__(16) float lsm[];
     float* xs = lsm;                                          // [Kp] fp32 (normalised) activations
     int8_t* qs = reinterpret_cast<int8_t*>(lsm + Kp);         // [Kp] codes
-    __shared__ float red[32];
+    __shared__ float red[96];
     constexpr int kPre = 4;  // 16-byte weight chunks per lane fetched before the dependency wait
     const int lane = threadIdx.x & 31;
     const int warps_total = gridDim.x * (kThreads / 32);
@@ -291,9 +316,15 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const float* __restric
         pre[u] = (first_col < N && c < chunks) ? ld_stream_u4(panel + (size_t)first_col * cb + (size_t)c * 16)
                                                : make_uint4(0, 0, 0, 0);
     }
+    const bool lead = lane == 0 && first_col < N;  // lane 0 finishes the warp's columns
+    const float pre_scale = lead ? scales[first_col] : 0.0f;
+    const float pre_bias = (lead && bias) ? bias[first_col] : 0.0f;
     pdl_launch_dependents();
     pdl_wait_primary();
     if (skip_prefill && __ldcg(&st->pos) + 1 < __ldcg(&st->prompt_len)) return;
+    // The residual is final once the kernel before this one completed (its
+    // own wait covered every kernel before it): load it with the row.
+    const float pre_res = (kEpi == kEpiResidual && lead) ? __ldcg(y + first_col) : 0.0f;
 
     if (kPro == kProMerge) {
         // context row from the attention chunks (shared memory after xs, qs)
@@ -332,11 +363,11 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const float* __restric
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], o);
         if (lane == 0) {
-            float v = zq_epilogue(acc[0], s, scales[col]);
-            if (bias) v = x86_add(v, bias[col]);
+            float v = zq_epilogue(acc[0], s, have_pre ? pre_scale : scales[col]);
+            if (bias) v = x86_add(v, have_pre ? pre_bias : bias[col]);
             if (kEpi == kEpiStore) y[col] = v;
             else if (kEpi == kEpiGelu) y[col] = gelu_ref(v);
-            else y[col] = x86_add(__ldcg(y + col), v);
+            else y[col] = x86_add(have_pre ? pre_res : __ldcg(y + col), v);
         }
     }
 }
@@ -1538,11 +1569,9 @@ cudaError_t launch_linear_t(const float* x, const float* nw, const float* nb, fl
     auto kern = zq::lm::linear_kernel<kType, kPro, kEpi>;
     size_t smem = linear_smem(w->Kp);
     if (kPro == zq::lm::kProMerge) smem += (2 * (size_t)merge.heads * merge.n_chunks_max + merge.heads) * sizeof(float);
-    int dev = 0, sms = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    int blocks = (int)((w->N + 7) / 8);
-    if (blocks > 2 * sms) blocks = 2 * sms;
+    // one column per warp: every column's weights are loaded before the
+    // dependency wait (blocks beyond the resident ones run as a second wave)
+    const int blocks = (int)((w->N + 7) / 8);
     return launch_pdl(kern, dim3(blocks), dim3(zq::lm::kThreads), smem, s, x, (int)w->K, w->Kp, nw, nb, eps,
                       (const uint8_t*)w->panel, (const float*)w->scales, (int)w->N, bias, y, st, skip_prefill, merge);
 }

@@ -64,7 +64,7 @@ struct State {
 };
 
 enum Prologue { kProNone = 0, kProRms = 1, kProLayer = 2, kProMerge = 3 };
-enum Epilogue { kEpiStore = 0, kEpiGelu = 1, kEpiResidual = 2 };
+enum Epilogue { kEpiStore = 0, kEpiGelu = 1, kEpiResidual = 2, kEpiLogits = 3 };
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -113,6 +113,23 @@ __device__ __forceinline__ float gelu_ref(float x) {
     const float x3 = __fmul_rn(__fmul_rn(x, x), x);
     const float inner = __fmul_rn(kInvSqrt2Pi, __fadd_rn(x, __fmul_rn(kC, x3)));
     return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+// Greedy choice as one comparable 64-bit key: the logit's bits made
+// order-preserving (-0 counted as +0), then the complement of the column, so
+// the larger key is the larger logit and, on ties, the lower token id.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int col) {
+    uint32_t b = __float_as_uint(v);
+    if ((b & 0x7fffffffu) == 0u) b = 0u;
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)b << 32) | (unsigned long long)(0xffffffffu - (uint32_t)col);
+}
+__device__ __forceinline__ int token_from_key(unsigned long long key, int nan, int V) {
+    if (nan || key == 0ull) return 0;
+    const uint32_t hi = (uint32_t)(key >> 32);
+    const float best = __uint_as_float((hi & 0x80000000u) ? (hi ^ 0x80000000u) : ~hi);
+    const int idx = (int)(0xffffffffu - (uint32_t)key);
+    return (isinf(best) || idx >= V) ? 0 : idx;
 }
 
 // ---------------------------------------------------------------------------
@@ -227,6 +244,14 @@ struct MergeArgs {
     int heads, hd, n_chunks_max;
 };
 
+// The lm_head's greedy choice: every block folds its columns into one
+// order-preserving key (argmax_key) and a NaN flag, published with one
+// atomicMax; next_token_kernel reads and clears them.
+struct ArgmaxArgs {
+    unsigned long long* key;
+    int* nan;
+};
+
 // The context row of the newest position from its chunks' partials:
 // ctx = (sum_c c_c e^(m_c - M)) / (sum_c l_c e^(m_c - M)), M = max_c m_c, per
 // head, into xs[0, heads * hd).  `mls` holds 2 * heads * nchunk floats and
@@ -294,11 +319,13 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const float* __restric
                                                           const float* __restrict__ scales, int N,
                                                           const float* __restrict__ bias, float* y,
                                                           const State* __restrict__ st, int skip_prefill,
-                                                          const MergeArgs merge) {
+                                                          const MergeArgs merge, const ArgmaxArgs am) {
     extern __shared__ __align__(16) float lsm[];
     float* xs = lsm;                                          // [Kp] fp32 (normalised) activations
     int8_t* qs = reinterpret_cast<int8_t*>(lsm + Kp);         // [Kp] codes
     __shared__ float red[96];
+    __shared__ unsigned long long blk_key;
+    __shared__ int blk_nan;
     constexpr int kPre = 4;  // 16-byte weight chunks per lane fetched before the dependency wait
     const int lane = threadIdx.x & 31;
     const int warps_total = gridDim.x * (kThreads / 32);
@@ -336,7 +363,10 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const float* __restric
         for (int i = threadIdx.x; i < Kp; i += kThreads) xs[i] = i < K ? __ldcg(x + i) : 0.0f;
     }
     __syncthreads();
+    if (kEpi == kEpiLogits && threadIdx.x == 0) blk_key = 0ull, blk_nan = 0;
     const float s = quantize_row<kThreads>(xs, qs, K, Kp, kType, kPro, nw, nb, eps, red);
+    unsigned long long best = 0ull;
+    int nan = 0;
 
     for (int col = first_col; col < N; col += warps_total) {
         const uint8_t* wc = panel + (size_t)col * cb;
@@ -365,68 +395,50 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const float* __restric
         if (lane == 0) {
             float v = zq_epilogue(acc[0], s, have_pre ? pre_scale : scales[col]);
             if (bias) v = x86_add(v, have_pre ? pre_bias : bias[col]);
-            if (kEpi == kEpiStore) y[col] = v;
+            if (kEpi == kEpiStore || kEpi == kEpiLogits) y[col] = v;
             else if (kEpi == kEpiGelu) y[col] = gelu_ref(v);
             else y[col] = x86_add(have_pre ? pre_res : __ldcg(y + col), v);
+            if (kEpi == kEpiLogits) {
+                if (isnan(v)) {
+                    nan = 1;
+                } else {
+                    const unsigned long long k = argmax_key(v, col);
+                    if (k > best) best = k;
+                }
+            }
+        }
+    }
+    if (kEpi == kEpiLogits) {
+        if (lane == 0) {
+            if (best) atomicMax(&blk_key, best);
+            if (nan) blk_nan = 1;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            if (blk_key) atomicMax(am.key, blk_key);
+            if (blk_nan) atomicExch(am.nan, 1);
         }
     }
 }
 
 // ---------------------------------------------------------------------------
 // Greedy choice (sample_next with top_k = 1, 82-174): the highest logit,
-// lowest id on ties.  The reference returns token 0 when its softmax
-// denominator is not finite (any NaN logit, or a maximum of +-inf).  During
-// prefill the step only advances the position.
+// lowest id on ties, folded into one key by the lm_head kernel.  The
+// reference returns token 0 when its softmax denominator is not finite (any
+// NaN logit, or a maximum of +-inf).  During prefill the step only advances
+// the position.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int V, int32_t* tokens,
-                                                      State* st) {
-    __shared__ float bv[32];
-    __shared__ int bi[32];
-    __shared__ int bnan[32];
+__global__ void next_token_kernel(ArgmaxArgs am, int V, int32_t* tokens, State* st) {
     pdl_launch_dependents();
     pdl_wait_primary();
+    if (threadIdx.x != 0) return;
     const int pos = __ldcg(&st->pos);
-    if (pos + 1 < __ldcg(&st->prompt_len)) {
-        __syncthreads();
-        if (threadIdx.x == 0) st->pos = pos + 1;
-        return;
+    if (pos + 1 >= __ldcg(&st->prompt_len)) {
+        tokens[pos + 1] = token_from_key(__ldcg(am.key), __ldcg(am.nan), V);
+        *am.key = 0ull;  // ready for the next step's lm_head
+        *am.nan = 0;
     }
-    float best = -INFINITY;
-    int idx = V;
-    int nan = 0;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        const float v = __ldcg(logits + i);
-        if (isnan(v)) nan = 1;
-        else if (v > best || (v == best && i < idx)) best = v, idx = i;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-        nan |= __shfl_xor_sync(0xffffffffu, nan, o);
-        if (ov > best || (ov == best && oi < idx)) best = ov, idx = oi;
-    }
-    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-    if (l == 0) bv[w] = best, bi[w] = idx, bnan[w] = nan;
-    __syncthreads();
-    if (w == 0) {
-        const int nw = blockDim.x >> 5;
-        best = l < nw ? bv[l] : -INFINITY;
-        idx = l < nw ? bi[l] : V;
-        nan = l < nw ? bnan[l] : 0;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-            nan |= __shfl_xor_sync(0xffffffffu, nan, o);
-            if (ov > best || (ov == best && oi < idx)) best = ov, idx = oi;
-        }
-        if (l == 0) {
-            const int next = (nan || isinf(best) || idx >= V) ? 0 : idx;
-            tokens[pos + 1] = next;
-            st->pos = pos + 1;
-        }
-    }
+    st->pos = pos + 1;
 }
 
 // ===========================================================================
@@ -782,23 +794,6 @@ __device__ __forceinline__ void run_cols(const LinDesc& L, int gw, int W, int la
             }
         }
     }
-}
-
-// Greedy choice as one comparable 64-bit key: the logit's bits made
-// order-preserving (-0 counted as +0), then the complement of the column, so
-// the larger key is the larger logit and, on ties, the lower token id.
-__device__ __forceinline__ unsigned long long argmax_key(float v, int col) {
-    uint32_t b = __float_as_uint(v);
-    if ((b & 0x7fffffffu) == 0u) b = 0u;
-    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-    return ((unsigned long long)b << 32) | (unsigned long long)(0xffffffffu - (uint32_t)col);
-}
-__device__ __forceinline__ int token_from_key(unsigned long long key, int nan, int V) {
-    if (nan || key == 0ull) return 0;
-    const uint32_t hi = (uint32_t)(key >> 32);
-    const float best = __uint_as_float((hi & 0x80000000u) ? (hi ^ 0x80000000u) : ~hi);
-    const int idx = (int)(0xffffffffu - (uint32_t)key);
-    return (isinf(best) || idx >= V) ? 0 : idx;
 }
 
 // Query rows of heads h0 .. h0+nh-1 into q_s (row stride kMaxHeadDim), with
@@ -1552,6 +1547,7 @@ cudaError_t prepare_type() {
     if (e == cudaSuccess) e = prepare_linear_t<kType, kProLayer, kEpiGelu>();
     if (e == cudaSuccess) e = prepare_linear_t<kType, kProLayer, kEpiResidual>();
     if (e == cudaSuccess) e = prepare_linear_t<kType, kProMerge, kEpiResidual>();
+    if (e == cudaSuccess) e = prepare_linear_t<kType, kProRms, kEpiLogits>();
     return e;
 }
 
@@ -1565,7 +1561,7 @@ cudaError_t prepare_kernels() {
 template <int kType, int kPro, int kEpi>
 cudaError_t launch_linear_t(const float* x, const float* nw, const float* nb, float eps, const zq_weight* w,
                             const float* bias, float* y, const State* st, int skip_prefill, cudaStream_t s,
-                            zq::lm::MergeArgs merge) {
+                            zq::lm::MergeArgs merge, zq::lm::ArgmaxArgs am) {
     auto kern = zq::lm::linear_kernel<kType, kPro, kEpi>;
     size_t smem = linear_smem(w->Kp);
     if (kPro == zq::lm::kProMerge) smem += (2 * (size_t)merge.heads * merge.n_chunks_max + merge.heads) * sizeof(float);
@@ -1573,16 +1569,17 @@ cudaError_t launch_linear_t(const float* x, const float* nw, const float* nb, fl
     // dependency wait (blocks beyond the resident ones run as a second wave)
     const int blocks = (int)((w->N + 7) / 8);
     return launch_pdl(kern, dim3(blocks), dim3(zq::lm::kThreads), smem, s, x, (int)w->K, w->Kp, nw, nb, eps,
-                      (const uint8_t*)w->panel, (const float*)w->scales, (int)w->N, bias, y, st, skip_prefill, merge);
+                      (const uint8_t*)w->panel, (const float*)w->scales, (int)w->N, bias, y, st, skip_prefill, merge,
+                      am);
 }
 
 template <int kPro, int kEpi>
 cudaError_t launch_linear(const float* x, const float* nw, const float* nb, float eps, const zq_weight* w,
                           const float* bias, float* y, const State* st, int skip_prefill, cudaStream_t s,
-                          zq::lm::MergeArgs merge = {}) {
+                          zq::lm::MergeArgs merge = {}, zq::lm::ArgmaxArgs am = {}) {
     return w->type == ZQ_TYPE_INT8
-               ? launch_linear_t<ZQ_TYPE_INT8, kPro, kEpi>(x, nw, nb, eps, w, bias, y, st, skip_prefill, s, merge)
-               : launch_linear_t<ZQ_TYPE_INT4, kPro, kEpi>(x, nw, nb, eps, w, bias, y, st, skip_prefill, s, merge);
+               ? launch_linear_t<ZQ_TYPE_INT8, kPro, kEpi>(x, nw, nb, eps, w, bias, y, st, skip_prefill, s, merge, am)
+               : launch_linear_t<ZQ_TYPE_INT4, kPro, kEpi>(x, nw, nb, eps, w, bias, y, st, skip_prefill, s, merge, am);
 }
 
 template <int kEpi>
@@ -1636,12 +1633,14 @@ cudaError_t enqueue_step(zq_lm* lm, cudaStream_t s) {
                                                                   lm->h, lm->state, 0, s);
     }
     if (e != cudaSuccess) return e;
-    // final norm is always RMS without bias (forward 492)
-    e = launch_linear<zq::lm::kProRms, zq::lm::kEpiStore>(lm->h, lm->final_w, nullptr, eps, lm->head, lm->b_head,
-                                                          lm->logits, lm->state, 1, s);
+    // final norm is always RMS without bias (forward 492); the lm_head folds
+    // the greedy choice into lm->keys[0] / lm->nan_flags[0]
+    const zq::lm::ArgmaxArgs am{lm->keys, lm->nan_flags};
+    e = launch_linear<zq::lm::kProRms, zq::lm::kEpiLogits>(lm->h, lm->final_w, nullptr, eps, lm->head, lm->b_head,
+                                                           lm->logits, lm->state, 1, s, {}, am);
     if (e != cudaSuccess) return e;
-    return launch_pdl(zq::lm::argmax_kernel, dim3(1), dim3(1024), 0, s, (const float*)lm->logits, (int)c.vocab_size,
-                      lm->tokens, lm->state);
+    return launch_pdl(zq::lm::next_token_kernel, dim3(1), dim3(32), 0, s, am, (int)c.vocab_size, lm->tokens,
+                      lm->state);
 }
 
 zq::lm::LinDesc lin_desc(const zq_weight* w, const float* bias) {
@@ -2038,27 +2037,33 @@ zq_status zq_lm_generate_greedy(zq_lm* lm, const int64_t* prompt, size_t prompt_
             le = cudaMemcpyAsync(step_logits, dlog, n_new * c.vocab_size * sizeof(float), cudaMemcpyDeviceToHost, st);
         if (dlog) cudaFreeAsync(dlog, st);
         LM_CUDA(le);
-    } else if (step_logits) {
-        // parity mode: per step, copy the logits that chose each new token
-        for (size_t i = 0; i < steps; ++i) {
-            LM_CUDA(enqueue_step(lm, st));
-            if (i + 1 >= prompt_len) {
-                const size_t g = i + 1 - prompt_len;
-                LM_CUDA(cudaMemcpyAsync(step_logits + g * c.vocab_size, lm->logits, c.vocab_size * sizeof(float),
-                                        cudaMemcpyDeviceToHost, st));
-            }
-        }
     } else {
-        if (!lm->graph_one) LM_CUDA(build_graph(lm, 1, &lm->graph_one, st));
-        if (!lm->graph_chunk && steps >= (size_t)lm->chunk) LM_CUDA(build_graph(lm, lm->chunk, &lm->graph_chunk, st));
-        size_t done = 0;
-        while (steps - done >= (size_t)lm->chunk && lm->graph_chunk) {
-            LM_CUDA(cudaGraphLaunch(lm->graph_chunk, st));
-            done += lm->chunk;
-        }
-        while (done < steps) {
-            LM_CUDA(cudaGraphLaunch(lm->graph_one, st));
-            ++done;
+        // the kernel chain; the lm_head's argmax key starts cleared
+        LM_CUDA(cudaMemsetAsync(lm->keys, 0, 2 * sizeof(unsigned long long), st));
+        LM_CUDA(cudaMemsetAsync(lm->nan_flags, 0, 2 * sizeof(int), st));
+        if (step_logits) {
+            // parity mode: per step, copy the logits that chose each new token
+            for (size_t i = 0; i < steps; ++i) {
+                LM_CUDA(enqueue_step(lm, st));
+                if (i + 1 >= prompt_len) {
+                    const size_t g = i + 1 - prompt_len;
+                    LM_CUDA(cudaMemcpyAsync(step_logits + g * c.vocab_size, lm->logits, c.vocab_size * sizeof(float),
+                                            cudaMemcpyDeviceToHost, st));
+                }
+            }
+        } else {
+            if (!lm->graph_one) LM_CUDA(build_graph(lm, 1, &lm->graph_one, st));
+            if (!lm->graph_chunk && steps >= (size_t)lm->chunk)
+                LM_CUDA(build_graph(lm, lm->chunk, &lm->graph_chunk, st));
+            size_t done = 0;
+            while (steps - done >= (size_t)lm->chunk && lm->graph_chunk) {
+                LM_CUDA(cudaGraphLaunch(lm->graph_chunk, st));
+                done += lm->chunk;
+            }
+            while (done < steps) {
+                LM_CUDA(cudaGraphLaunch(lm->graph_one, st));
+                ++done;
+            }
         }
     }
     LM_CUDA(cudaMemcpyAsync(tok.data(), lm->tokens, total * sizeof(int32_t), cudaMemcpyDeviceToHost, st));

@@ -24,12 +24,12 @@ namespace zq {
 namespace {
 
 constexpr int kGemvThreads = 256;
-constexpr int kUnroll = 4;  // 16-byte weight chunks in flight per lane per column
 
 // One group of kCols columns for one warp: dp4a over all chunks (kUnroll
 // 16-byte loads per lane per column in flight), warp-shuffle reduction, exact
 // epilogue.
-template <int kType, int kM, int kCols>
+// kUnroll: 16-byte weight chunks in flight per lane per column.
+template <int kType, int kM, int kCols, int kUnroll>
 __device__ __forceinline__ void gemv_group(int g, const uint8_t* __restrict__ panel,
                                            int N, int Kp, size_t col_bytes, int chunks, const int8_t* __restrict__ sq,
                                            const float* __restrict__ col_scale, const float (&srow)[kM],
@@ -91,7 +91,7 @@ __device__ __forceinline__ void gemv_group(int g, const uint8_t* __restrict__ pa
 
 // kCols columns per warp iteration: each shared-memory activation read feeds
 // kCols columns' dp4a (M >= 4 is dp4a/LDS-heavy; M <= 2 is purely HBM-bound).
-template <int kType, int kM, int kCols>
+template <int kType, int kM, int kCols, int kUnroll>
 __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const uint8_t* __restrict__ panel, int N, int Kp,
                                                             const float* __restrict__ col_scale,
                                                             const int8_t* __restrict__ q,
@@ -149,13 +149,15 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const uint8_t* __res
     for (int m = 0; m < kM; ++m) srow[m] = m < M ? row_scale[m] : 0.0f;
 
     for (int g = warp_global; g < groups; g += warps_total)
-        gemv_group<kType, kM, kCols>(g, panel, N, Kp, col_bytes, chunks, sq, col_scale, srow, bias, y, M, lane);
+        gemv_group<kType, kM, kCols, kUnroll>(g, panel, N, Kp, col_bytes, chunks, sq, col_scale, srow, bias, y, M, lane);
 }
 
-template <int kType, int kM, int kCols>
+// Four chunks per lane: with at most 64 resident warps per SM, eight per
+// lane (one round for a 4096-code column) measured slower (fewer warps).
+template <int kType, int kM, int kCols, int kUnroll = 4>
 cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
     const size_t smem = (size_t)kM * a.Kp;
-    auto kern = gemv_kernel<kType, kM, kCols>;
+    auto kern = gemv_kernel<kType, kM, kCols, kUnroll>;
     cudaError_t e = ensure_smem_attr(kern, smem);
     if (e != cudaSuccess) return e;
     const int sms = sm_count();

@@ -529,6 +529,86 @@ def run_gemv_workload(args):
     print(json.dumps(line), flush=True)
 
 
+def run_kernels_workload(args):
+    """The HBM-bound helper kernels of the path at sizes larger than L2, each
+    timed with CUDA events: the activation quantizer (x 8192 x 8192 fp32),
+    the device weight quantizer (W 8192 x 16384 fp32 -> INT8 / INT4 panel),
+    dequantize() of the INT8 panel, and the INT4 -> int8 panel expansion the
+    prefill GEMM runs first (timed as an INT4 matmul minus the same INT8
+    matmul).  GB/s are algorithmic bytes (every input read once, every output
+    written once)."""
+    import torch
+
+    import zyron_b200 as zb
+    from zyron_b200 import _lib
+
+    L = _lib.lib()
+    dev = torch.device("cuda:0")
+    peak, peak_src = hbm_peak()
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    M, K, N = 8192, 8192, 16384
+
+    def timed(fn, reps=None):
+        reps = reps or max(args.steps, 1)
+        for _ in range(max(args.warmup, 1)):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps * 1e3  # us
+
+    cases = {}
+
+    def add(name, us, nbytes):
+        cases[name] = {"us": us, "GBs": nbytes / us / 1e3, "frac_of_hbm": nbytes / us / 1e3 / peak}
+
+    x = torch.randn((M, K), generator=g, device=dev)
+    q = torch.empty((M, K), dtype=torch.int8, device=dev)
+    rs = torch.empty((M,), device=dev)
+    add("quantize_rows (activations 8192 x 8192)",
+        timed(lambda: _lib.check(L.zq_quantize_rows(C.c_void_p(x.data_ptr()), M, K, C.c_void_p(q.data_ptr()), K,
+                                                    C.c_void_p(rs.data_ptr()), None))),
+        4 * M * K + M * K + 4 * M)
+    w = torch.randn((K, N), generator=g, device=dev).mul_(0.02)
+    holder = {}
+
+    def quant8():
+        holder["w8"] = zb.quantize(w, zb.Type.Int8)
+
+    add("zq_weight_quantize INT8 call (8192 x 16384; allocates the panel)", timed(quant8, 3),
+        2 * 4 * K * N + K * N + 4 * N)
+
+    def quant4():
+        holder["w4"] = zb.quantize(w, zb.Type.Int4)
+
+    add("zq_weight_quantize INT4 call (8192 x 16384; allocates the panel)", timed(quant4, 3), 2 * 4 * K * N + K * N // 2 + 4 * N)
+    W8, W4 = holder["w8"], holder["w4"]
+    out = torch.empty((K, N), device=dev)
+
+    def deq():
+        _lib.check(L.zq_dequantize(W8.handle, C.c_void_p(out.data_ptr()), None))
+
+    add("dequantize INT8 (8192 x 16384 -> fp32)", timed(deq), K * N + 4 * N + 4 * K * N)
+    del out
+    torch.cuda.empty_cache()
+    m = 256
+    xm = torch.randn((m, K), generator=g, device=dev)
+    t4 = timed(lambda: zb.matmul(xm, W4), 5)
+    t8 = timed(lambda: zb.matmul(xm, W8), 5)
+    add("expand INT4 panel to int8 (inside an INT4 matmul, M=256)", max(t4 - t8, 1e-3), K * N // 2 + K * N)
+    line = {"metric": "helper kernels of the path (HBM-bound)", "value": cases["quantize_rows (activations 8192 x 8192)"]["GBs"],
+            "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp32->int8", "data": "synthetic",
+            "config": {"workload": "helper_kernels", "x": [M, K], "W": [K, N]},
+            "roofline": {"bound": "hbm", "peak": peak, "unit": "GB/s", "peak_source": peak_src}, "cases": cases}
+    print(json.dumps(line), flush=True)
+
+
 def run_small_workload(args):
     """The two small matmul configurations: INT8 M=64 K=512 N=512 and INT4
     M=128 K=2048 N=2048, x ~N(0,1), w ~N(0,0.02).  Calls are replayed from a
@@ -678,7 +758,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["prefill", "gemv", "small", "qlm"], default="prefill",
+    ap.add_argument("--workload", choices=["prefill", "gemv", "small", "qlm", "kernels"], default="prefill",
                     help="prefill (default line), gemv (decode GEMV), small (64x512x512 INT8 and "
                          "128x2048x2048 INT4) or qlm (LM decode)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling runs)")
@@ -704,6 +784,9 @@ def main():
         return
     if args.workload == "qlm":
         run_qlm_workload(args)
+        return
+    if args.workload == "kernels":
+        run_kernels_workload(args)
         return
     if args.workload == "small":
         run_small_workload(args)

@@ -261,47 +261,38 @@ template <int kType>
 __global__ void __launch_bounds__(256) quantize_panel_kernel(const float* __restrict__ w, int K, int N,
                                                              int Kp, const float* __restrict__ scales,
                                                              uint8_t* __restrict__ panel) {
-    // tile: 32 columns (n) x 64 rows (k); threads (32, 8)
-    __shared__ int8_t tile[32][64 + 4];
+    // tile: 32 columns (n) x 128 rows (k); threads (32, 8).  Reads are rows
+    // of 32 consecutive floats; each column's 128 codes go out as one
+    // 128-byte (INT8) or 64-byte (INT4) segment.
+    __shared__ int8_t tile[32][128 + 4];
     const int n0 = blockIdx.x * 32;
-    const int k0 = blockIdx.y * 64;
+    const int k0 = blockIdx.y * 128;
     const int tx = threadIdx.x, ty = threadIdx.y;
     const int limit = kType == kInt8 ? 127 : 7;
     const int n = n0 + tx;
     const float s = n < N ? scales[n] : 1.0f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < 16; ++j) {
         const int k = k0 + ty + 8 * j;
         int8_t v = 0;
         if (n < N && k < K) v = (int8_t)zq_quantize_value(__ldg(w + (size_t)k * N + n), s, limit);
         tile[tx][ty + 8 * j] = v;
     }
     __syncthreads();
-    if (kType == kInt8) {
-        // each warp row writes 64 consecutive k codes of one column as 32 x 2 bytes
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int c = ty + 8 * j;
-            const int nn = n0 + c;
-            const int k = k0 + 2 * tx;
-            if (nn < N && k < Kp) {
-                const uint16_t pair = (uint16_t)(uint8_t)tile[c][2 * tx] |
-                                      ((uint16_t)(uint8_t)tile[c][2 * tx + 1] << 8);
-                *reinterpret_cast<uint16_t*>(panel + (size_t)nn * Kp + k) = pair;
-            }
-        }
-    } else {
-        const int bpc = Kp >> 1;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int c = ty + 8 * j;
-            const int nn = n0 + c;
-            const int k = k0 + 2 * tx;  // byte k/2 holds codes k (low) and k+1 (high)
-            if (nn < N && k < Kp) {
-                const uint8_t b = (uint8_t)(((uint8_t)tile[c][2 * tx] & 0x0Fu) |
-                                            (((uint8_t)tile[c][2 * tx + 1] & 0x0Fu) << 4));
-                panel[(size_t)nn * bpc + (k >> 1)] = b;
-            }
+    for (int j = 0; j < 4; ++j) {
+        const int c = ty + 8 * j;
+        const int nn = n0 + c;
+        const int k = k0 + 4 * tx;  // codes k .. k+3 of column nn
+        if (nn >= N || k >= Kp) continue;
+        const uint32_t c0 = (uint8_t)tile[c][4 * tx], c1 = (uint8_t)tile[c][4 * tx + 1];
+        const uint32_t c2 = (uint8_t)tile[c][4 * tx + 2], c3 = (uint8_t)tile[c][4 * tx + 3];
+        if (kType == kInt8) {
+            *reinterpret_cast<uint32_t*>(panel + (size_t)nn * Kp + k) = c0 | (c1 << 8) | (c2 << 16) | (c3 << 24);
+        } else {
+            // byte k/2 holds codes k (low nibble) and k+1 (high nibble)
+            const uint32_t b0 = (c0 & 0x0Fu) | ((c1 & 0x0Fu) << 4), b1 = (c2 & 0x0Fu) | ((c3 & 0x0Fu) << 4);
+            *reinterpret_cast<uint16_t*>(panel + (size_t)nn * (Kp >> 1) + (k >> 1)) = (uint16_t)(b0 | (b1 << 8));
         }
     }
 }
@@ -315,7 +306,7 @@ cudaError_t launch_quantize_weights(const float* w, int K, int N, int Kp, int ty
     column_absmax_kernel<<<g1, 128, 0, stream>>>(w, K, N, rows_per_block, absmax_tmp);
     column_scale_kernel<<<(N + 255) / 256, 256, 0, stream>>>(absmax_tmp, N, type == kInt8 ? 127.0f : 7.0f,
                                                             scales);
-    dim3 g2((N + 31) / 32, (Kp + 63) / 64);
+    dim3 g2((N + 31) / 32, (Kp + 127) / 128);
     if (type == kInt8)
         quantize_panel_kernel<kInt8><<<g2, dim3(32, 8), 0, stream>>>(w, K, N, Kp, scales, panel);
     else

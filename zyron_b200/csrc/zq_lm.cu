@@ -245,10 +245,11 @@ struct MergeArgs {
 };
 
 // The lm_head's greedy choice: every block folds its columns into one
-// order-preserving key (argmax_key) and a NaN flag, published with one
-// atomicMax; next_token_kernel reads and clears them.
+// order-preserving key (argmax_key), stored in its own slot (no contended
+// atomics across thousands of blocks), and raises a shared flag on a NaN;
+// next_token_kernel reduces the slots and clears the flag.
 struct ArgmaxArgs {
-    unsigned long long* key;
+    unsigned long long* slots;  // [lm_head blocks]
     int* nan;
 };
 
@@ -415,7 +416,7 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const float* __restric
         }
         __syncthreads();
         if (threadIdx.x == 0) {
-            if (blk_key) atomicMax(am.key, blk_key);
+            am.slots[blockIdx.x] = blk_key;
             if (blk_nan) atomicExch(am.nan, 1);
         }
     }
@@ -428,15 +429,34 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const float* __restric
 // NaN logit, or a maximum of +-inf).  During prefill the step only advances
 // the position.
 // ---------------------------------------------------------------------------
-__global__ void next_token_kernel(ArgmaxArgs am, int V, int32_t* tokens, State* st) {
+__global__ void __launch_bounds__(256) next_token_kernel(ArgmaxArgs am, int nslots, int V, int32_t* tokens,
+                                                         State* st) {
+    __shared__ unsigned long long wbest[8];
     pdl_launch_dependents();
     pdl_wait_primary();
-    if (threadIdx.x != 0) return;
     const int pos = __ldcg(&st->pos);
-    if (pos + 1 >= __ldcg(&st->prompt_len)) {
-        tokens[pos + 1] = token_from_key(__ldcg(am.key), __ldcg(am.nan), V);
-        *am.key = 0ull;  // ready for the next step's lm_head
-        *am.nan = 0;
+    const bool choose = pos + 1 >= __ldcg(&st->prompt_len);
+    if (choose) {
+        unsigned long long best = 0ull;
+        for (int i = threadIdx.x; i < nslots; i += 256) {
+            const unsigned long long k = __ldcg(am.slots + i);
+            if (k > best) best = k;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+            if (other > best) best = other;
+        }
+        if ((threadIdx.x & 31) == 0) wbest[threadIdx.x >> 5] = best;
+    }
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    if (choose) {
+        unsigned long long best = wbest[0];
+        for (int w = 1; w < 8; ++w)
+            if (wbest[w] > best) best = wbest[w];
+        tokens[pos + 1] = token_from_key(best, __ldcg(am.nan), V);
+        *am.nan = 0;  // ready for the next step's lm_head
     }
     st->pos = pos + 1;
 }
@@ -1437,6 +1457,7 @@ struct zq_lm {
     unsigned int* bar = nullptr;
     unsigned long long* keys = nullptr;
     int* nan_flags = nullptr;
+    unsigned long long* head_slots = nullptr;  // the lm_head blocks' argmax keys (kernel chain)
     int step_grid = 0;  // 0: cooperative launch unavailable, use the kernel chain
     size_t step_smem = 0;
     int xmax = 0;
@@ -1505,6 +1526,11 @@ zq_status make_weight(const zq::ZyqRecord& r, void* stream, zq_weight** out) {
 
 size_t linear_smem(int Kp) { return (size_t)Kp * sizeof(float) + (size_t)Kp; }
 
+// One column per warp (8 per block): every column's weights are loaded
+// before the dependency wait; blocks beyond the resident ones run as a
+// second wave.
+int linear_blocks(const zq_weight* w) { return (int)((w->N + 7) / 8); }
+
 // Every decode-step kernel is launched with programmatic dependent launch:
 // it may start (and prefetch constant weights) while its predecessor runs,
 // and waits in griddepcontrol.wait before reading anything the predecessor
@@ -1565,9 +1591,7 @@ cudaError_t launch_linear_t(const float* x, const float* nw, const float* nb, fl
     auto kern = zq::lm::linear_kernel<kType, kPro, kEpi>;
     size_t smem = linear_smem(w->Kp);
     if (kPro == zq::lm::kProMerge) smem += (2 * (size_t)merge.heads * merge.n_chunks_max + merge.heads) * sizeof(float);
-    // one column per warp: every column's weights are loaded before the
-    // dependency wait (blocks beyond the resident ones run as a second wave)
-    const int blocks = (int)((w->N + 7) / 8);
+    const int blocks = linear_blocks(w);
     return launch_pdl(kern, dim3(blocks), dim3(zq::lm::kThreads), smem, s, x, (int)w->K, w->Kp, nw, nb, eps,
                       (const uint8_t*)w->panel, (const float*)w->scales, (int)w->N, bias, y, st, skip_prefill, merge,
                       am);
@@ -1635,12 +1659,12 @@ cudaError_t enqueue_step(zq_lm* lm, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     // final norm is always RMS without bias (forward 492); the lm_head folds
     // the greedy choice into lm->keys[0] / lm->nan_flags[0]
-    const zq::lm::ArgmaxArgs am{lm->keys, lm->nan_flags};
+    const zq::lm::ArgmaxArgs am{lm->head_slots, lm->nan_flags};
     e = launch_linear<zq::lm::kProRms, zq::lm::kEpiLogits>(lm->h, lm->final_w, nullptr, eps, lm->head, lm->b_head,
                                                            lm->logits, lm->state, 1, s, {}, am);
     if (e != cudaSuccess) return e;
-    return launch_pdl(zq::lm::next_token_kernel, dim3(1), dim3(32), 0, s, am, (int)c.vocab_size, lm->tokens,
-                      lm->state);
+    return launch_pdl(zq::lm::next_token_kernel, dim3(1), dim3(256), 0, s, am, linear_blocks(lm->head),
+                      (int)c.vocab_size, lm->tokens, lm->state);
 }
 
 zq::lm::LinDesc lin_desc(const zq_weight* w, const float* bias) {
@@ -1674,6 +1698,7 @@ cudaError_t prepare_persistent(zq_lm* lm, cudaStream_t st) {
     if (e == cudaSuccess) e = dev_alloc(lm, &lm->bar, 1);
     if (e == cudaSuccess) e = dev_alloc(lm, &lm->keys, 2);
     if (e == cudaSuccess) e = dev_alloc(lm, &lm->nan_flags, 2);
+    if (e == cudaSuccess) e = dev_alloc(lm, &lm->head_slots, (size_t)linear_blocks(lm->head));
     if (e != cudaSuccess) return e;
     lm->xmax = (kmax + 31) / 32 * 32;
     using namespace zq::lm;

@@ -541,6 +541,16 @@ zq::OutDesc single_output(float* y, size_t N) {
 // Kernel for decode-sized matmuls (zq_set_decode_kernel).
 std::atomic<int> g_decode_kernel{ZQ_DECODE_AUTO};
 
+// Whether a plain-output matmul with M rows runs the dp4a GEMV.  Default:
+// the GEMV for 1-4 rows, where the weight stream alone sets the time and it
+// has the least fixed cost per launch; the tensor cores above that, where
+// dp4a and shared-memory reads of the activation rows limit the GEMV.
+bool use_gemv(const zq_weight* w, int M) {
+    const int decode = g_decode_kernel.load(std::memory_order_relaxed);
+    const bool fits = M <= zq::kGemvMaxRows && zq::gemv_smem_bytes(M, w->Kp) <= 200 * 1024;
+    return fits && (decode == ZQ_DECODE_CUDA_CORE || (decode == ZQ_DECODE_AUTO && M <= 4));
+}
+
 zq_status run_codes_out(const zq_weight* w, const int8_t* codes, const float* rs, size_t m, const float* bias,
                         const zq::OutDesc& out, uint8_t* scratch, cudaStream_t st, bool pdl);
 
@@ -557,14 +567,7 @@ zq_status run_codes_out(const zq_weight* w, const int8_t* codes, const float* rs
     if (s != ZQ_OK) return s;
     const int M = (int)m, N = (int)w->N, Kp = w->Kp;
     const bool plain = out.count == 1 && out.ldy == (long long)N && out.col_offset == 0;
-    const int decode = g_decode_kernel.load(std::memory_order_relaxed);
-    const bool gemv_ok = plain && M <= zq::kGemvMaxRows && zq::gemv_smem_bytes(M, Kp) <= 200 * 1024;
-    // Default: the dp4a GEMV for 1-4 rows, where the weight stream alone
-    // sets the time and it has the least fixed cost per launch; the tensor
-    // cores above that, where dp4a and shared-memory reads of the activation
-    // rows limit the GEMV.
-    const bool use_gemv = gemv_ok && (decode == ZQ_DECODE_CUDA_CORE || (decode == ZQ_DECODE_AUTO && M <= 4));
-    if (use_gemv) {
+    if (plain && use_gemv(w, M)) {
         zq::GemvArgs a{w->type, w->panel, N, Kp, w->scales, codes, rs, bias, y, M};
         ZQ_CUDA(zq::launch_gemv(a, st, pdl));
         return ZQ_OK;
@@ -637,6 +640,16 @@ zq_status run_codes_out(const zq_weight* w, const int8_t* codes, const float* rs
 // 256-byte aligned, zq_matmul_workspace_bytes(w, m) bytes).
 zq_status matmul_in_workspace_out(const zq_weight* w, const float* x, size_t m, const float* bias,
                                   const zq::OutDesc& out, uint8_t* ws, cudaStream_t st) {
+    const bool plain = out.count == 1 && out.ldy == (long long)w->N && out.col_offset == 0;
+    if (plain && m <= 4 && use_gemv(w, (int)m)) {
+        // one launch: the GEMV quantizes the rows itself (same codes and
+        // scales as the standalone quantizer)
+        zq::GemvArgs a{w->type, w->panel, (int)w->N, w->Kp, w->scales, nullptr, nullptr, bias, out.base[0], (int)m};
+        a.x = x;
+        a.K = (int)w->K;
+        ZQ_CUDA(zq::launch_gemv(a, st, false));
+        return ZQ_OK;
+    }
     int8_t* codes = reinterpret_cast<int8_t*>(ws);
     float* rs = reinterpret_cast<float*>(ws + align256(m * (size_t)w->Kp));
     uint8_t* scratch = ws + align256(m * (size_t)w->Kp) + align256(m * sizeof(float));

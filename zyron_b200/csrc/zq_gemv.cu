@@ -91,17 +91,21 @@ __device__ __forceinline__ void gemv_group(int g, const uint8_t* __restrict__ pa
 
 // kCols columns per warp iteration: each shared-memory activation read feeds
 // kCols columns' dp4a (M >= 4 is dp4a/LDS-heavy; M <= 2 is purely HBM-bound).
-template <int kType, int kM, int kCols, int kUnroll>
-__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const uint8_t* __restrict__ panel, int N, int Kp,
+// kFused: the activation rows arrive as fp32 `x` [M][K] and every block
+// quantizes them itself with the standalone quantizer's arithmetic
+// (quantization.cpp:202-212: fmaxf absmax, absmax / 127 correctly rounded,
+// round half away from zero), so a decode matmul is a single launch.
+template <int kType, int kM, int kCols, int kUnroll, bool kFused, int kThreads>
+__global__ void __launch_bounds__(kThreads) gemv_kernel(const uint8_t* __restrict__ panel, int N, int Kp,
                                                             const float* __restrict__ col_scale,
                                                             const int8_t* __restrict__ q,
                                                             const float* __restrict__ row_scale,
                                                             const float* __restrict__ bias, float* __restrict__ y,
-                                                            int M) {
+                                                            int M, const float* __restrict__ x, int K) {
     extern __shared__ __align__(16) int8_t sq[];  // [kM][Kp]
     const int lane = threadIdx.x & 31;
-    const int warp_global = (blockIdx.x * kGemvThreads + threadIdx.x) >> 5;
-    const int warps_total = (gridDim.x * kGemvThreads) >> 5;
+    const int warp_global = (blockIdx.x * kThreads + threadIdx.x) >> 5;
+    const int warps_total = (gridDim.x * kThreads) >> 5;
     const size_t col_bytes = kType == kInt8 ? (size_t)Kp : (size_t)(Kp >> 1);
     const int groups = (N + kCols - 1) / kCols;
 
@@ -118,12 +122,91 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const uint8_t* __res
     }
     pdl_wait_primary();
 
+    float srow[kM];
+    if constexpr (kFused) {
+        // Per-row absmax (NaN skipped by fmaxf, as std::max does).  When the
+        // rows start on 16-byte boundaries they are read as float4, two
+        // loads in flight per thread.
+        __shared__ float redm[kThreads / 32][kM];
+        const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (K & 3) == 0;
+        float mx[kM];
+#pragma unroll
+        for (int m = 0; m < kM; ++m) {
+            mx[m] = 0.0f;
+            if (m < M) {
+                const float* xr = x + (size_t)m * K;
+                if (vec) {
+                    const float4* x4 = reinterpret_cast<const float4*>(xr);
+                    const int K4 = K >> 2;
+                    for (int b = threadIdx.x; b < K4; b += 2 * kThreads) {
+                        float4 v[2];
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            const int i = b + u * kThreads;
+                            v[u] = i < K4 ? __ldg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+#pragma unroll
+                        for (int u = 0; u < 2; ++u)
+                            mx[m] = fmaxf(mx[m], fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)),
+                                                       fmaxf(fabsf(v[u].z), fabsf(v[u].w))));
+                    }
+                } else {
+                    for (int i = threadIdx.x; i < K; i += kThreads) mx[m] = fmaxf(mx[m], fabsf(__ldg(xr + i)));
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], o));
+            if (lane == 0) redm[threadIdx.x >> 5][m] = mx[m];
+        }
+        __syncthreads();
+#pragma unroll
+        for (int m = 0; m < kM; ++m) {
+            float t = redm[0][m];
+#pragma unroll
+            for (int w = 1; w < kThreads / 32; ++w) t = fmaxf(t, redm[w][m]);
+            srow[m] = m < M ? zq_scale_from_absmax(t, 127.0f) : 0.0f;
+        }
+        // codes into shared memory, 8 per step: k order for INT8 weights,
+        // split even/odd per group of 8 to pair with INT4 nibbles
+        uint32_t* s4 = reinterpret_cast<uint32_t*>(sq);
+        const int kgroups = Kp >> 3;
+        for (int gi = threadIdx.x; gi < kM * kgroups; gi += kThreads) {
+            const int m = gi / kgroups, k0 = (gi - m * kgroups) * 8;
+            float sm = 0.0f;
+#pragma unroll
+            for (int mm = 0; mm < kM; ++mm)
+                if (mm == m) sm = srow[mm];
+            float v[8];
+            const float* xk = x + (size_t)m * K + k0;
+            if (m < M && vec && k0 + 8 <= K) {
+                const float4 lo = __ldg(reinterpret_cast<const float4*>(xk));
+                const float4 hi = __ldg(reinterpret_cast<const float4*>(xk) + 1);
+                v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w;
+                v[4] = hi.x; v[5] = hi.y; v[6] = hi.z; v[7] = hi.w;
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = (m < M && k0 + j < K) ? __ldg(xk + j) : 0.0f;
+            }
+            uint32_t c[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) c[j] = (uint32_t)(uint8_t)(int8_t)zq_quantize_value(v[j], sm, 127);
+            const uint32_t a = c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24);
+            const uint32_t b = c[4] | (c[5] << 8) | (c[6] << 16) | (c[7] << 24);
+            if (kType == kInt8) {
+                s4[2 * gi] = a;
+                s4[2 * gi + 1] = b;
+            } else {
+                s4[2 * gi] = __byte_perm(a, b, 0x6420);
+                s4[2 * gi + 1] = __byte_perm(a, b, 0x7531);
+            }
+        }
+    } else {
     // Stage the activation codes (rows >= M are zero).
     {
         const uint32_t* q4 = reinterpret_cast<const uint32_t*>(q);
         uint32_t* s4 = reinterpret_cast<uint32_t*>(sq);
         const int words = Kp >> 2;
-        for (int i = threadIdx.x; i < kM * words; i += kGemvThreads) {
+        for (int i = threadIdx.x; i < kM * words; i += kThreads) {
             const int m = i / words;
             const int wi = i - m * words;
             if (kType == kInt8) {
@@ -142,11 +225,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const uint8_t* __res
             }
         }
     }
-    __syncthreads();
-
-    float srow[kM];
 #pragma unroll
     for (int m = 0; m < kM; ++m) srow[m] = m < M ? row_scale[m] : 0.0f;
+    }
+    __syncthreads();
 
     for (int g = warp_global; g < groups; g += warps_total)
         gemv_group<kType, kM, kCols, kUnroll>(g, panel, N, Kp, col_bytes, chunks, sq, col_scale, srow, bias, y, M, lane);
@@ -154,26 +236,30 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const uint8_t* __res
 
 // Four chunks per lane: with at most 64 resident warps per SM, eight per
 // lane (one round for a 4096-code column) measured slower (fewer warps).
-template <int kType, int kM, int kCols, int kUnroll = 4>
+template <int kType, int kM, int kCols, int kUnroll = 4, bool kFused = false>
 cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+    // The fused variant runs 512-thread blocks, so each SM reads and
+    // quantizes the activation rows half as often as with 256 (512 keeps the
+    // register budget of the 256-thread variants: no spills, same occupancy).
+    constexpr int kThreads = kFused ? 512 : kGemvThreads;
     const size_t smem = (size_t)kM * a.Kp;
-    auto kern = gemv_kernel<kType, kM, kCols, kUnroll>;
+    auto kern = gemv_kernel<kType, kM, kCols, kUnroll, kFused, kThreads>;
     cudaError_t e = ensure_smem_attr(kern, smem);
     if (e != cudaSuccess) return e;
     const int sms = sm_count();
     int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGemvThreads, smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
     // As many resident warps as occupancy allows: under load the HBM needs
     // many loads in flight per SM, and warps are what carry them.
     const int groups = (a.N + kCols - 1) / kCols;
-    const int needed = (groups + kGemvThreads / 32 - 1) / (kGemvThreads / 32);
+    const int needed = (groups + kThreads / 32 - 1) / (kThreads / 32);
     const int blocks = sms * per_sm < needed ? sms * per_sm : needed;
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(blocks);
-    cfg.blockDim = dim3(kGemvThreads);
+    cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -182,11 +268,18 @@ cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kern, a.panel, a.N, a.Kp, a.col_scale, a.q, a.row_scale, a.bias, a.y,
-                              a.M);
+                              a.M, a.x, a.K);
 }
 
 template <int kType>
 cudaError_t dispatch_m(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+    if (a.x) {  // quantizer fused, up to 4 rows
+        switch (a.M) {
+            case 1: return launch_gemv_t<kType, 1, 1, 4, true>(a, stream, pdl);
+            case 2: return launch_gemv_t<kType, 2, 1, 4, true>(a, stream, pdl);
+            default: return launch_gemv_t<kType, 4, 2, 4, true>(a, stream, pdl);
+        }
+    }
     switch (a.M) {
         case 1: return launch_gemv_t<kType, 1, 1>(a, stream, pdl);
         case 2: return launch_gemv_t<kType, 2, 1>(a, stream, pdl);
@@ -204,7 +297,7 @@ size_t gemv_smem_bytes(int M, int Kp) {
 }
 
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl) {
-    if (a.M < 1 || a.M > kGemvMaxRows) return cudaErrorInvalidValue;
+    if (a.M < 1 || a.M > kGemvMaxRows || (a.x && a.M > 4)) return cudaErrorInvalidValue;
     return a.type == kInt8 ? dispatch_m<kInt8>(a, stream, pdl) : dispatch_m<kInt4>(a, stream, pdl);
 }
 

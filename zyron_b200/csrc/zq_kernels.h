@@ -25,11 +25,13 @@ struct GemvArgs {
     int N;
     int Kp;
     const float* col_scale;
-    const int8_t* q;
-    const float* row_scale;
+    const int8_t* q;          // activation codes [M][Kp] and
+    const float* row_scale;   // row scales [M], or null when x is given
     const float* bias;
     float* y;
     int M;
+    const float* x = nullptr; // fp32 activations [M][K], quantized inside the kernel (M <= 4)
+    int K = 0;
 };
 
 // Where the GEMM epilogue writes: element (row, col) of the matmul goes to

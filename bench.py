@@ -631,6 +631,13 @@ def run_small_workload(args):
         W = zb.quantize(torch.from_numpy(w).to(dev), zb.Type(qt))
         xd = torch.from_numpy(x).to(dev)
         y = torch.empty((M, N), device=dev)
+        if args.once:
+            # profiling aid: three eager zq_matmul calls, no timing
+            for _ in range(3):
+                y = zb.matmul(xd, W)
+            torch.cuda.synchronize()
+            out[name] = {"checksum": float(y.abs().sum())}
+            continue
         wsb = L.zq_matmul_workspace_bytes(W.handle, M)
         ws = torch.empty(wsb + 256, dtype=torch.uint8, device=dev)
         wp = (ws.data_ptr() + 255) & ~255
@@ -668,6 +675,9 @@ def run_small_workload(args):
             res["cpu_baseline"] = {"us_per_call": tc * 1e6, "TOPS": 2.0 * M * N * K / tc / 1e12, "cores": threads,
                                    "kind": kind}
         out[name] = res
+    if args.once:
+        print(json.dumps({"workload": "small_matmuls", "once": True, "cases": out}), flush=True)
+        return
     line = {"metric": "small quantized matmul configurations (quantization::matmul)",
             "value": out["int4_M128_K2048_N2048"]["TOPS"], "unit": "TOPS", "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -692,6 +702,11 @@ def run_qlm_workload(args):
     img = random_zyqmodel(cfg, seed=0)
     lm = QuantizedLanguageModel.load_bytes(img)
     prompt = np.random.default_rng(0).integers(0, 16384, 64).tolist()
+    if args.once:
+        # profiling aid: one 4-token generation after the 64-token prompt
+        toks = lm.generate(prompt, GenerationConfig(max_new_tokens=4, top_k=1))
+        print(json.dumps({"workload": "qlm_decode_d768_L12", "once": True, "tokens": list(map(int, toks))}))
+        return
     lm.generate(prompt, GenerationConfig(max_new_tokens=512, top_k=1))  # builds the graphs
     s = torch.cuda.Stream()
 
@@ -763,7 +778,7 @@ def main():
                          "128x2048x2048 INT4) or qlm (LM decode)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling runs)")
     ap.add_argument("--once", action="store_true",
-                    help="--workload gemv: a few untimed calls of each decode kernel (for ncu captures)")
+                    help="gemv / small / qlm workloads: a few untimed calls of the kernels (for ncu captures)")
     ap.add_argument("--shape", type=lambda v: tuple(int(t) for t in v.split(",")),
                     default=(M_ROWS, K_DIM, N_COLS), help="M,K,N override for small profiling cases")
     args = ap.parse_args()

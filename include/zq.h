@@ -184,6 +184,42 @@ zq_status zq_dequantize(const zq_weight* w, float* out, void* stream);
  * Synchronous. */
 zq_status zq_dequantize_host(const zq_weight* w, float* out_host, void* stream);
 
+/* ---- column-sharded matmul over NCCL ------------------------------------ */
+
+/* Columns [*begin, *end) of rank `rank` when n_cols columns are split over
+ * `world` ranks: contiguous, the first n_cols % world ranks one column wider.
+ * zq_matmul_sharded expects each rank's shard to be exactly this range (e.g.
+ * zq_weight_slice_cols(w, begin, end, ...)). */
+zq_status zq_shard_range(size_t n_cols, int world, int rank, size_t* begin, size_t* end);
+
+/* NCCL communicator helpers for hosts without their own NCCL binding.  NCCL
+ * is loaded at run time (libnccl.so.2; a process that already loaded it, e.g.
+ * through PyTorch, shares that copy).  The unique id is ZQ_NCCL_UNIQUE_ID_BYTES
+ * opaque bytes that rank 0 creates and every rank passes to
+ * zq_nccl_comm_init, with its own device current.  *comm is an ncclComm_t. */
+#define ZQ_NCCL_UNIQUE_ID_BYTES 128
+zq_status zq_nccl_get_unique_id(void* id_out);
+zq_status zq_nccl_comm_init(int nranks, const void* id, int rank, void** comm);
+zq_status zq_nccl_comm_destroy(void* comm);
+
+/* Workspace zq_matmul_sharded needs for m rows of an n_cols-column weight
+ * split over `world` ranks (0 for invalid arguments). */
+size_t zq_matmul_sharded_workspace_bytes(const zq_weight* shard, size_t m, size_t n_cols, int world);
+
+/* The sharded path of quantization::matmul (the reference runs it on one
+ * host; the column split follows from quantization.cpp:141-159, one scale
+ * per column).  y [m][n_cols] (full output, on every rank) = matmul(x, W)
+ * with W's columns sharded over the ranks of `nccl_comm` (an ncclComm_t on
+ * the current device): this rank holds `shard`, its zq_shard_range columns,
+ * and bias_shard (or NULL) for them.  Every rank computes its block with
+ * zq_matmul (same activation codes everywhere, no exchange), then one
+ * ncclAllGather on `stream` joins the blocks.  Bit-identical to zq_matmul on
+ * the whole weight.  Every rank must make the same call (same m and n_cols)
+ * in the same order; a rank that fails validation issues no collective, so
+ * the others' gather waits until the communicator is aborted or times out. */
+zq_status zq_matmul_sharded(const zq_weight* shard, const float* x, size_t m, const float* bias_shard, float* y,
+                            size_t n_cols, void* nccl_comm, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- peer buffers (for zq_matmul_multi across processes) ---------------- */
 
 /* A device allocation exported from one process for another (CUDA IPC). */

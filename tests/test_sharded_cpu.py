@@ -21,6 +21,33 @@ def test_column_ranges():
         column_ranges(3, 4)
 
 
+def test_c_shard_range_matches_column_ranges():
+    """zq_shard_range (the C entry point the NCCL sharded matmul checks
+    shards against) splits exactly as column_ranges does; pure host code."""
+    import ctypes as C
+
+    from zyron_b200 import _lib
+
+    L = _lib.lib()
+    for n in (1, 2, 3, 7, 8, 100, 2047, 11008, 65536, 65537):
+        for world in (1, 2, 3, 4, 5, 7, 8):
+            if n < world:
+                b, e = C.c_size_t(), C.c_size_t()
+                assert L.zq_shard_range(n, world, 0, C.byref(b), C.byref(e)) == 1
+                assert b"fewer columns than ranks" in L.zq_last_error()
+                continue
+            got = []
+            for r in range(world):
+                b, e = C.c_size_t(), C.c_size_t()
+                assert L.zq_shard_range(n, world, r, C.byref(b), C.byref(e)) == 0
+                got.append((b.value, e.value))
+            assert got == column_ranges(n, world)
+    b, e = C.c_size_t(), C.c_size_t()
+    assert L.zq_shard_range(8, 2, 2, C.byref(b), C.byref(e)) == 1
+    assert L.zq_shard_range(8, 0, 0, C.byref(b), C.byref(e)) == 1
+    assert L.zq_matmul_sharded_workspace_bytes(None, 4, 8, 2) == 0
+
+
 def test_assemble_columns():
     r = column_ranges(5, 2)
     blocks = [torch.arange(6.).reshape(2, 3), torch.arange(4.).reshape(2, 2) + 100]

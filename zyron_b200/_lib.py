@@ -99,6 +99,12 @@ SIGNATURES = {
     "zq_matmul": (st, [vp, vp, sz, vp, vp, vp, sz, vp]),
     "zq_matmul_noalloc": (st, [vp, vp, sz, vp, vp, vp]),
     "zq_matmul_multi": (st, [vp, vp, sz, vp, vp, C.c_int, sz, sz, vp, sz, vp]),
+    "zq_shard_range": (st, [sz, C.c_int, C.c_int, C.POINTER(sz), C.POINTER(sz)]),
+    "zq_nccl_get_unique_id": (st, [vp]),
+    "zq_nccl_comm_init": (st, [C.c_int, vp, C.c_int, C.POINTER(vp)]),
+    "zq_nccl_comm_destroy": (st, [vp]),
+    "zq_matmul_sharded_workspace_bytes": (sz, [vp, sz, sz, C.c_int]),
+    "zq_matmul_sharded": (st, [vp, vp, sz, vp, vp, sz, vp, vp, sz, vp]),
     "zq_matmul_host": (st, [vp, vp, sz, vp, vp, vp]),
     "zq_dequantize": (st, [vp, vp, vp]),
     "zq_device_error": (st, [vp, C.POINTER(C.c_uint32)]),

@@ -23,7 +23,7 @@ QLIB = os.path.join(HERE, "libzyron_quant.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 CU_SOURCES = ["zq_api.cu", "zq_quant.cu", "zq_gemv.cu", "zq_gemm_sm100.cu", "zq_skinny_sm100.cu", "zq_noalloc.cu",
-              "zq_lm.cu"]
+              "zq_lm.cu", "zq_sharded.cu"]
 CU_HEADERS = ["zq_common.cuh", "zq_dot.cuh", "zq_tcgen05.cuh", "zq_kernels.h", "zq_internal.h"]
 CPP_SOURCES = ["src/quantization.cpp", "src/quantized_linear.cpp", "src/tensor.cpp"]
 
@@ -61,7 +61,8 @@ def build_cuda(force=False):
         o = os.path.join(objdir, os.path.basename(s) + ".o")
         _run([NVCC, *NVCC_FLAGS, "-I", os.path.join(ROOT, "include"), "-I", CSRC, "-dc" if False else "-c", s, "-o", o])
         objs.append(o)
-    _run([NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", LIB, *objs, "-cudart", "static"])
+    _run([NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", LIB, *objs, "-cudart", "static",
+          "-ldl"])
     return LIB
 
 

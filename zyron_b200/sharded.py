@@ -170,3 +170,73 @@ def sharded_matmul_gathered(x, weight_shard, peer_out: PeerOutputs, bias_shard=N
                                  C.c_void_p(s.cuda_stream)))
     peer_out.barrier()
     return peer_out.local
+
+
+_NCCL_ID_BYTES = 128  # ZQ_NCCL_UNIQUE_ID_BYTES
+
+
+class NcclComm:
+    """An NCCL communicator made by the library (``zq_nccl_comm_init``) over
+    the ranks of a torch.distributed group, for :func:`nccl_sharded_matmul`.
+    Rank 0 creates the unique id and the group (any backend) broadcasts it.
+    Without an initialised process group it is a single-rank communicator."""
+
+    def __init__(self, device, group=None):
+        import ctypes as C
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _lib
+
+        self._L = _lib.lib()
+        if dist.is_initialized():
+            self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        else:
+            self.world, self.rank = 1, 0
+        uid = (C.c_ubyte * _NCCL_ID_BYTES)()
+        if self.rank == 0:
+            _lib.check(self._L.zq_nccl_get_unique_id(uid))
+        if self.world > 1:
+            obj = [bytes(uid)]
+            src = 0 if group is None else dist.get_global_rank(group, 0)
+            dist.broadcast_object_list(obj, src=src, group=group)
+            uid = (C.c_ubyte * _NCCL_ID_BYTES).from_buffer_copy(obj[0])
+        self.handle = C.c_void_p()
+        with torch.cuda.device(device):
+            _lib.check(self._L.zq_nccl_comm_init(self.world, uid, self.rank, C.byref(self.handle)))
+
+    def close(self):
+        if self.handle:
+            from . import _lib
+
+            _lib.check(self._L.zq_nccl_comm_destroy(self.handle))
+            self.handle = None
+
+
+def nccl_sharded_matmul(x, weight_shard, n_cols: int, comm: NcclComm, bias_shard=None, out=None, stream=None):
+    """y = matmul(x, W) with W column-sharded over ``comm``'s ranks, through
+    the C entry point ``zq_matmul_sharded``: each rank computes its block of
+    :func:`column_ranges` columns, one NCCL all-gather joins the blocks, and
+    every rank returns the full [M, n_cols] output (bit-identical to the
+    single-GPU matmul)."""
+    import ctypes as C
+
+    import torch
+
+    from . import _lib
+
+    L = _lib.lib()
+    x = x.contiguous()
+    m = x.shape[0]
+    s = stream if stream is not None else torch.cuda.current_stream(x.device)
+    need = L.zq_matmul_sharded_workspace_bytes(weight_shard.handle, m, n_cols, comm.world)
+    with torch.cuda.stream(s):
+        ws = torch.empty(need + 256, dtype=torch.uint8, device=x.device)
+        y = out if out is not None else torch.empty((m, n_cols), dtype=torch.float32, device=x.device)
+    ws_ptr = (ws.data_ptr() + 255) & ~255
+    _lib.check(L.zq_matmul_sharded(weight_shard.handle, C.c_void_p(x.data_ptr()), m,
+                                   None if bias_shard is None else C.c_void_p(bias_shard.data_ptr()),
+                                   C.c_void_p(y.data_ptr()), n_cols, comm.handle, C.c_void_p(ws_ptr), need,
+                                   C.c_void_p(s.cuda_stream)))
+    return y

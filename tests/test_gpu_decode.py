@@ -128,3 +128,32 @@ def test_decode_codes_entry_reuses_workspace(zb, decode_kernel, qt):
                                             need, None))
             assert_bits_equal(y.cpu().numpy(), yo, f"codes entry t{qt} N={N} rep {rep}")
     assert zb.device_error() == 0
+
+
+@pytest.mark.parametrize("qt", [1, 2])
+@pytest.mark.parametrize("M,K,N", [(1, 4096, 1000), (3, 1024, 300), (4, 512, 64)])
+def test_fused_gemv_unaligned_rows(zb, decode_kernel, qt, M, K, N):
+    """The fused quantizer+GEMV reads activation rows as float4 when they
+    start on 16-byte boundaries and element by element otherwise: x handed to
+    zq_matmul one float past an aligned base takes the second path, with the
+    same bits as the oracle."""
+    import torch
+
+    decode_kernel(CUDA_CORE)
+    L = zb._lib.lib()
+    x, w, b = _case(M, K, N, qt)
+    pay, sc = O.quantize_weights(w, qt)
+    W = zb.QuantizedMatrix.from_parts(qt, K, N, sc, pay)
+    buf = torch.zeros(M * K + 4, dtype=torch.float32, device="cuda")
+    assert buf.data_ptr() % 16 == 0
+    buf[1:1 + M * K] = torch.from_numpy(x.ravel()).cuda()
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    bd = torch.from_numpy(b).cuda()
+    need = L.zq_matmul_workspace_bytes(W.handle, M)
+    ws = torch.empty(need + 256, dtype=torch.uint8, device="cuda")
+    ws_ptr = (ws.data_ptr() + 255) & ~255
+    zb._lib.check(L.zq_matmul(W.handle, C.c_void_p(buf.data_ptr() + 4), M, C.c_void_p(bd.data_ptr()),
+                              C.c_void_p(y.data_ptr()), C.c_void_p(ws_ptr), need, None))
+    _, _, _, yo = O.matmul(x, qt, pay, sc, N, b)
+    assert_bits_equal(y.cpu().numpy(), yo, f"unaligned x t{qt} {M}x{K}x{N}")
+    assert zb.device_error() == 0

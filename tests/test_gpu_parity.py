@@ -122,6 +122,25 @@ def test_matmul_bit_exact(zb, qt, M, K, N):
 
 
 @pytest.mark.parametrize("qt", [1, 2])
+def test_zero_rows(zb, qt):
+    """An input with no rows gives an empty [0, N] output, as the
+    reference's matmul does (its row loop runs zero times); device and host
+    inputs both."""
+    import torch
+
+    K, N = 64, 48
+    _, w = make(np.random.default_rng(5), 1, K, N)
+    pay, sc = O.quantize_weights(w, qt)
+    W = zb.QuantizedMatrix.from_parts(qt, K, N, sc, pay)
+    yo = O.matmul(np.zeros((0, K), np.float32), qt, pay, sc, N)[3]
+    assert yo.shape == (0, N)
+    y = zb.matmul(torch.empty((0, K), device="cuda"), W)
+    assert tuple(y.shape) == (0, N)
+    assert zb.matmul(np.zeros((0, K), np.float32), W).shape == (0, N)
+    assert zb.device_error() == 0
+
+
+@pytest.mark.parametrize("qt", [1, 2])
 def test_host_entry_point(zb, qt):
     rng = np.random.default_rng(11 + qt)
     for M, K, N in [(1, 300, 70), (40, 96, 130)]:

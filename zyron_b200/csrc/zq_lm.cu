@@ -1458,6 +1458,7 @@ struct zq_lm {
     unsigned long long* keys = nullptr;
     int* nan_flags = nullptr;
     unsigned long long* head_slots = nullptr;  // the lm_head blocks' argmax keys (kernel chain)
+    int head_blocks = 0;                       // lm_head grid: one resident wave
     int step_grid = 0;  // 0: cooperative launch unavailable, use the kernel chain
     size_t step_smem = 0;
     int xmax = 0;
@@ -1587,11 +1588,11 @@ cudaError_t prepare_kernels() {
 template <int kType, int kPro, int kEpi>
 cudaError_t launch_linear_t(const float* x, const float* nw, const float* nb, float eps, const zq_weight* w,
                             const float* bias, float* y, const State* st, int skip_prefill, cudaStream_t s,
-                            zq::lm::MergeArgs merge, zq::lm::ArgmaxArgs am) {
+                            zq::lm::MergeArgs merge, zq::lm::ArgmaxArgs am, int max_blocks) {
     auto kern = zq::lm::linear_kernel<kType, kPro, kEpi>;
     size_t smem = linear_smem(w->Kp);
     if (kPro == zq::lm::kProMerge) smem += (2 * (size_t)merge.heads * merge.n_chunks_max + merge.heads) * sizeof(float);
-    const int blocks = linear_blocks(w);
+    const int blocks = max_blocks > 0 ? std::min(max_blocks, linear_blocks(w)) : linear_blocks(w);
     return launch_pdl(kern, dim3(blocks), dim3(zq::lm::kThreads), smem, s, x, (int)w->K, w->Kp, nw, nb, eps,
                       (const uint8_t*)w->panel, (const float*)w->scales, (int)w->N, bias, y, st, skip_prefill, merge,
                       am);
@@ -1600,10 +1601,33 @@ cudaError_t launch_linear_t(const float* x, const float* nw, const float* nb, fl
 template <int kPro, int kEpi>
 cudaError_t launch_linear(const float* x, const float* nw, const float* nb, float eps, const zq_weight* w,
                           const float* bias, float* y, const State* st, int skip_prefill, cudaStream_t s,
-                          zq::lm::MergeArgs merge = {}, zq::lm::ArgmaxArgs am = {}) {
-    return w->type == ZQ_TYPE_INT8
-               ? launch_linear_t<ZQ_TYPE_INT8, kPro, kEpi>(x, nw, nb, eps, w, bias, y, st, skip_prefill, s, merge, am)
-               : launch_linear_t<ZQ_TYPE_INT4, kPro, kEpi>(x, nw, nb, eps, w, bias, y, st, skip_prefill, s, merge, am);
+                          zq::lm::MergeArgs merge = {}, zq::lm::ArgmaxArgs am = {}, int max_blocks = 0) {
+    return w->type == ZQ_TYPE_INT8 ? launch_linear_t<ZQ_TYPE_INT8, kPro, kEpi>(x, nw, nb, eps, w, bias, y, st,
+                                                                             skip_prefill, s, merge, am, max_blocks)
+                                   : launch_linear_t<ZQ_TYPE_INT4, kPro, kEpi>(x, nw, nb, eps, w, bias, y, st,
+                                                                             skip_prefill, s, merge, am, max_blocks);
+}
+
+// The lm_head's grid: at most one resident wave.  Its warps stride over the
+// columns, so the wave covers them all; (N + 7) / 8 blocks of one column per
+// warp would run in several waves that each repeat the row's norm and
+// quantization (vocab 16384: 2048 blocks, 4 resident per SM).
+int head_blocks_for(const zq_weight* head) {
+    using namespace zq::lm;
+    const int full = linear_blocks(head);
+    int dev = 0, sms = 0, per_sm = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return full;
+    const size_t smem = linear_smem(head->Kp);
+    const cudaError_t e =
+        head->type == ZQ_TYPE_INT8
+            ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, linear_kernel<ZQ_TYPE_INT8, kProRms, kEpiLogits>,
+                                                            kThreads, smem)
+            : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, linear_kernel<ZQ_TYPE_INT4, kProRms, kEpiLogits>,
+                                                            kThreads, smem);
+    if (e != cudaSuccess || per_sm < 1 || sms < 1) return full;
+    return std::min(full, sms * per_sm);
 }
 
 template <int kEpi>
@@ -1661,10 +1685,10 @@ cudaError_t enqueue_step(zq_lm* lm, cudaStream_t s) {
     // the greedy choice into lm->keys[0] / lm->nan_flags[0]
     const zq::lm::ArgmaxArgs am{lm->head_slots, lm->nan_flags};
     e = launch_linear<zq::lm::kProRms, zq::lm::kEpiLogits>(lm->h, lm->final_w, nullptr, eps, lm->head, lm->b_head,
-                                                           lm->logits, lm->state, 1, s, {}, am);
+                                                           lm->logits, lm->state, 1, s, {}, am, lm->head_blocks);
     if (e != cudaSuccess) return e;
-    return launch_pdl(zq::lm::next_token_kernel, dim3(1), dim3(256), 0, s, am, linear_blocks(lm->head),
-                      (int)c.vocab_size, lm->tokens, lm->state);
+    return launch_pdl(zq::lm::next_token_kernel, dim3(1), dim3(256), 0, s, am, lm->head_blocks, (int)c.vocab_size,
+                      lm->tokens, lm->state);
 }
 
 zq::lm::LinDesc lin_desc(const zq_weight* w, const float* bias) {
@@ -1698,7 +1722,8 @@ cudaError_t prepare_persistent(zq_lm* lm, cudaStream_t st) {
     if (e == cudaSuccess) e = dev_alloc(lm, &lm->bar, 1);
     if (e == cudaSuccess) e = dev_alloc(lm, &lm->keys, 2);
     if (e == cudaSuccess) e = dev_alloc(lm, &lm->nan_flags, 2);
-    if (e == cudaSuccess) e = dev_alloc(lm, &lm->head_slots, (size_t)linear_blocks(lm->head));
+    lm->head_blocks = head_blocks_for(lm->head);
+    if (e == cudaSuccess) e = dev_alloc(lm, &lm->head_slots, (size_t)lm->head_blocks);
     if (e != cudaSuccess) return e;
     lm->xmax = (kmax + 31) / 32 * 32;
     using namespace zq::lm;

@@ -417,10 +417,10 @@ def run_gemv_workload(args):
             for M in (1, 8):
                 x = torch.randn((M, K), generator=g, device=dev)
                 for kind in (1, 2):
-                    L.zq_set_decode_kernel(kind)
+                    W.set_decode_kernel(kind)
                     for _ in range(3):
                         y = zb.matmul(x, W)
-                L.zq_set_decode_kernel(0)
+                W.set_decode_kernel(0)
         torch.cuda.synchronize()
         print(json.dumps({"workload": "decode_gemv_K4096_N11008", "once": True, "checksum": float(y.abs().sum())}))
         return
@@ -462,7 +462,8 @@ def run_gemv_workload(args):
                                            C.c_void_p(y.data_ptr()), C.c_void_p(wp), wsb, sp))
 
                 for kname, kind in (("tensor_core", 1), ("cuda_core", 2)):
-                    L.zq_set_decode_kernel(kind)
+                    for W in Ws:
+                        W.set_decode_kernel(kind)
                     res[kname] = {}
                     for name, fn in (("kernel", kernel_only), ("matmul_call", full_call)):
                         for i in range(copies):
@@ -486,7 +487,8 @@ def run_gemv_workload(args):
                         byts = payload + 4 * N + M * Kp + 4 * M * N
                         res[kname][name] = {"us": us, "GBs": byts / us / 1e3, "frac_of_hbm": byts / us / 1e3 / peak}
                         del graph
-                L.zq_set_decode_kernel(0)
+                for W in Ws:
+                    W.set_decode_kernel(0)
             cases[f"{'int8' if qt == 1 else 'int4'}_M{M}"] = res
     # end to end through the host entry point (M=1, INT8): pinned host x in, host y out
     W0 = zb.quantize(torch.randn((K, N), device=dev).mul_(0.02), zb.Type.Int8)

@@ -163,7 +163,10 @@ zq_status zq_matmul_codes(const zq_weight* w, const int8_t* q, const float* row_
  * the library (ZQ_NOALLOC_SCRATCH_BYTES per device, held until exit); calls
  * needing more (zq_matmul_workspace_bytes(w, m) larger than that) fail with
  * ZQ_ERR_INVALID_ARGUMENT.  Allocates nothing.  The first call on each device
- * resolves the array's device address and should precede any stream capture.
+ * resolves the array's device address and should precede any stream capture;
+ * the address is kept for the life of the process, so a cudaDeviceReset()
+ * invalidates it and the entry point must not be used on that device after
+ * one.
  * All calls on a device share the array: calls that may overlap on the GPU
  * race and must be serialised.  Same results as zq_matmul. */
 #define ZQ_NOALLOC_SCRATCH_BYTES (8u << 20)
@@ -242,29 +245,49 @@ zq_status zq_ipc_import(const zq_ipc_handle* h, void** dev_ptr);
 /* Unmap what zq_ipc_import mapped (pass the pointer it returned). */
 zq_status zq_ipc_close(void* dev_ptr);
 
-/* Keep `sms` streaming multiprocessors out of the matmul kernels' persistent
- * grids (process-wide, default 0), so work running concurrently on other
- * streams -- e.g. an NCCL collective of the previous output block -- finds
- * free SMs.  Returns the previous value. */
-int zq_set_reserved_sms(int sms);
-
-/* Which kernel runs plain matmuls with few activation rows (process-wide):
- *   ZQ_DECODE_TENSOR_CORE: the tcgen05 decode kernel for m <= 16 (weights
- *     streamed by TMA, work split evenly over the SMs);
- *   ZQ_DECODE_CUDA_CORE: the dp4a warp-per-column GEMV for m <= 8;
- *   ZQ_DECODE_AUTO (default): the GEMV for m <= 4, the tcgen05 kernel for
- *     5 <= m <= 16.
- * Larger m always runs the tcgen05 GEMM.  Results are identical.  Returns the
- * previous value. */
+/* Options of one weight's matmuls (every call with that weight, on any
+ * thread; results never depend on them).  *previous (may be NULL) receives
+ * the old value.
+ *   ZQ_OPT_DECODE_KERNEL: the kernel for plain matmuls with few activation
+ *     rows --
+ *       ZQ_DECODE_TENSOR_CORE: the tcgen05 decode kernel for m <= 16 (weights
+ *         streamed by TMA, work split evenly over the SMs);
+ *       ZQ_DECODE_CUDA_CORE: the dp4a warp-per-column GEMV for m <= 8;
+ *       ZQ_DECODE_AUTO (default): the GEMV for m <= 4, the tcgen05 kernel for
+ *         5 <= m <= 16.
+ *     Larger m always runs the tcgen05 GEMM.
+ *   ZQ_OPT_RESERVED_SMS: streaming multiprocessors kept out of the matmul
+ *     kernels' grids (default 0), so work running concurrently on other
+ *     streams -- e.g. a collective of the previous output block -- finds free
+ *     SMs.
+ *   ZQ_OPT_GEMM_GROUP_M: M-tiles per group of the GEMM's tile order (default
+ *     32; 0 = all), which bounds the L2 working set of large GEMMs.
+ * No counterpart in the reference (its matmul has no kernel choices). */
+#define ZQ_OPT_DECODE_KERNEL 1
+#define ZQ_OPT_RESERVED_SMS 2
+#define ZQ_OPT_GEMM_GROUP_M 3
 #define ZQ_DECODE_AUTO 0
 #define ZQ_DECODE_TENSOR_CORE 1
 #define ZQ_DECODE_CUDA_CORE 2
-int zq_set_decode_kernel(int kind);
+zq_status zq_weight_set_option(zq_weight* w, int option, int value, int* previous);
 
 /* Synchronise `stream`, then read and clear the current device's error word
  * (0 = none; otherwise which bounded wait gave up).  Returns
  * ZQ_ERR_DEVICE_TIMEOUT when the word was set. */
 zq_status zq_device_error(void* stream, uint32_t* code);
+
+/* Failure-path test of the bounded device waits (no counterpart in the
+ * reference; not for production use).  Runs zq_matmul_codes on the tcgen05
+ * decode kernel (1 <= m <= 16) with the finisher of every column block that
+ * several CTAs share waiting for one more partial sum than exists, so that
+ * wait gives up after limit_ns (1e5 to 1e9 ns): the kernel records the
+ * timeout in the error word, skips those blocks' outputs, releases its
+ * resources and returns.  The call succeeds; zq_device_error() then returns
+ * ZQ_ERR_DEVICE_TIMEOUT with code 5 and clears the word, and later calls run
+ * normally.  Nothing faults and nothing waits without a limit. */
+zq_status zq_test_decode_wait_timeout(const zq_weight* w, const int8_t* q, const float* row_scale, size_t m,
+                                      float* y, void* workspace, size_t workspace_bytes, uint64_t limit_ns,
+                                      void* stream);
 
 /* ---- quantized language model (device-resident decode) ----------------- */
 
@@ -292,6 +315,15 @@ zq_status zq_lm_load(const void* bytes, size_t len, void* stream, zq_lm** out);
 
 zq_status zq_lm_get_info(const zq_lm* lm, zq_lm_info* info);
 
+/* Options of one model's decode loop.  *previous (may be NULL) receives the
+ * old value.
+ *   ZQ_LM_OPT_PERSISTENT: 1 runs every greedy step without penalties in one
+ *     cooperative launch of a persistent kernel (when the device allows it),
+ *     0 (default) replays the chain of per-phase kernels from CUDA graphs.
+ *     Both give the same tokens. */
+#define ZQ_LM_OPT_PERSISTENT 1
+zq_status zq_lm_set_option(zq_lm* lm, int option, int value, int* previous);
+
 /* QuantizedLanguageModel::generate with GenerationConfig{top_k = 1} (greedy;
  * quantized_language_model.cpp:496-547).  Writes prompt + new tokens to
  * out_tokens (capacity out_cap) and their count to *out_len; generation stops
@@ -306,7 +338,51 @@ zq_status zq_lm_generate_greedy(zq_lm* lm, const int64_t* prompt, size_t prompt_
                                 int64_t* out_tokens, size_t out_cap, size_t* out_len, float* step_logits,
                                 void* stream);
 
+/* GenerationConfig (include/zyron/model/generation.hpp:13-21).  The
+ * reference's quantized sampler validates `temperature` but does not use it
+ * (quantized_language_model.cpp:71-80, 82-174); neither does this library. */
+typedef struct zq_generation_config {
+    size_t max_new_tokens;
+    float temperature;
+    size_t top_k;          /* 0: no top-k cut; 1: greedy */
+    float top_p;           /* in (0, 1] */
+    float repetition_penalty;   /* >= 1; 1 = off */
+    size_t no_repeat_ngram_size; /* 0 = off */
+    uint32_t seed;         /* std::mt19937 seed of the draws */
+} zq_generation_config;
+
+/* QuantizedLanguageModel::generate (quantized_language_model.cpp:496-547) for
+ * any GenerationConfig: same validation order and messages, and, given the
+ * same logits, the same tokens as the reference's sample_next (82-174).
+ *   - top_k == 1 without penalties: greedy on the device (as
+ *     zq_lm_generate_greedy);
+ *   - top_k == 1 with repetition_penalty != 1 or no_repeat_ngram_size > 0:
+ *     the penalty and the n-gram block are applied on the device, over the
+ *     device token history, before the greedy choice (lowest id on ties);
+ *   - any other top_k: each step's logits are copied to the host and sampled
+ *     there with the reference's softmax, std::sort, top-k/top-p cuts and one
+ *     std::mt19937(seed) draw per token (zq_sample_next).
+ * Output, step_logits and stream are as for zq_lm_generate_greedy. */
+zq_status zq_lm_generate(zq_lm* lm, const int64_t* prompt, size_t prompt_len, const zq_generation_config* config,
+                         int64_t* out_tokens, size_t out_cap, size_t* out_len, float* step_logits, void* stream);
+
 zq_status zq_lm_destroy(zq_lm* lm);
+
+/* ---- token sampling (host) --------------------------------------------- */
+
+/* The state of sample_next's random draws: std::mt19937(seed), as created
+ * once per generate call (quantized_language_model.cpp:520). */
+typedef struct zq_sampler zq_sampler;
+zq_status zq_sampler_create(uint32_t seed, zq_sampler** out);
+zq_status zq_sampler_destroy(zq_sampler* s);
+
+/* sample_next (quantized_language_model.cpp:82-174) over one row of `vocab`
+ * host logits: repetition penalty over `history` (the prompt and the tokens
+ * generated so far), n-gram block, softmax, sort by probability, top-k, top-p
+ * and one draw from `s`.  Host only; no device work.  Validates `config` as
+ * validate_generation_config does (71-80), and top_k <= vocab. */
+zq_status zq_sample_next(zq_sampler* s, const float* logits, size_t vocab, const int64_t* history,
+                         size_t history_len, const zq_generation_config* config, int64_t* token);
 
 #ifdef __cplusplus
 }

@@ -177,6 +177,8 @@ def ref():
         R.ref_qlm_load.argtypes = [C.c_char_p, C.POINTER(vp)]
         R.ref_qlm_forward.argtypes = [vp, vp, sz, vp]
         R.ref_qlm_generate_greedy.argtypes = [vp, vp, sz, sz, vp, C.POINTER(sz)]
+        R.ref_qlm_generate.argtypes = [vp, vp, sz, sz, C.c_float, sz, C.c_float, C.c_float, sz, C.c_uint32, vp,
+                                       C.POINTER(sz)]
         _ref = R
     return _ref
 
@@ -266,3 +268,50 @@ class RefMatrix:
 def ref_set_threads(n):
     ref().ref_set_threads(n)
     return int(ref().ref_num_threads())
+
+
+class RefQlm:
+    """A reference zyron::model::QuantizedLanguageModel (quantized_language_model.hpp)."""
+
+    def __init__(self, handle, vocab):
+        self.h, self.vocab = handle, vocab
+
+    @classmethod
+    def create(cls, vocab, hidden, layers, heads, kv_heads, ffn, max_seq, use_rope=True, use_rms_norm=True,
+               tie=True, seed=0, qtype=INT8):
+        """LanguageModel(config, seed) quantized to ``qtype``."""
+        h = C.c_void_p()
+        _chk(ref().ref_qlm_create(vocab, hidden, layers, heads, kv_heads, ffn, max_seq, int(use_rope),
+                                  int(use_rms_norm), int(tie), seed, qtype, C.byref(h)))
+        return cls(h, vocab)
+
+    @classmethod
+    def load(cls, path, vocab):
+        h = C.c_void_p()
+        _chk(ref().ref_qlm_load(str(path).encode(), C.byref(h)))
+        return cls(h, vocab)
+
+    def __del__(self):
+        if getattr(self, "h", None) is not None and _ref is not None:
+            _ref.ref_qlm_free(self.h)
+            self.h = None
+
+    def save(self, path):
+        _chk(ref().ref_qlm_save(self.h, str(path).encode()))
+
+    def forward(self, ids):
+        """Logits [T][vocab] of forward(ids)."""
+        a = np.ascontiguousarray(ids, dtype=np.uint64)
+        out = np.zeros((a.size, self.vocab), dtype=np.float32)
+        _chk(ref().ref_qlm_forward(self.h, _vp(a), a.size, _vp(out)))
+        return out
+
+    def generate(self, ids, max_new_tokens, temperature=1.0, top_k=0, top_p=1.0, repetition_penalty=1.0,
+                 no_repeat_ngram_size=0, seed=0):
+        """generate(ids, GenerationConfig{...}) -> prompt + new tokens."""
+        a = np.ascontiguousarray(ids, dtype=np.uint64)
+        out = np.zeros(a.size + max_new_tokens + 1, dtype=np.uint64)
+        n = C.c_size_t()
+        _chk(ref().ref_qlm_generate(self.h, _vp(a), a.size, max_new_tokens, temperature, top_k, top_p,
+                                    repetition_penalty, no_repeat_ngram_size, seed, _vp(out), C.byref(n)))
+        return [int(t) for t in out[: n.value]]

@@ -229,4 +229,25 @@ int ref_qlm_generate_greedy(const void* h, const std::size_t* ids, std::size_t T
     });
 }
 
+// generate() with a full GenerationConfig (include/zyron/model/generation.hpp:
+// 13-21).  out receives prompt + new tokens; *out_len its length.
+int ref_qlm_generate(const void* h, const std::size_t* ids, std::size_t T, std::size_t max_new, float temperature,
+                     std::size_t top_k, float top_p, float repetition_penalty, std::size_t no_repeat_ngram_size,
+                     std::uint32_t seed, std::size_t* out, std::size_t* out_len) {
+    return guarded([&] {
+        std::vector<std::size_t> v(ids, ids + T);
+        zyron::model::GenerationConfig gc;
+        gc.max_new_tokens = max_new;
+        gc.temperature = temperature;
+        gc.top_k = top_k;
+        gc.top_p = top_p;
+        gc.repetition_penalty = repetition_penalty;
+        gc.no_repeat_ngram_size = no_repeat_ngram_size;
+        gc.seed = seed;
+        auto res = static_cast<const RefQlm*>(h)->m->generate(v, gc);
+        std::memcpy(out, res.data(), res.size() * sizeof(std::size_t));
+        *out_len = res.size();
+    });
+}
+
 }  // extern "C"

@@ -37,13 +37,24 @@ def _rank(rank, world, port, q):
         b, e = column_ranges(N, world)[rank]
         W = zb.quantize(torch.from_numpy(np.ascontiguousarray(w[:, b:e])).to(dev), zb.Type.Int8)
         out = PeerOutputs(M, N, dev)
-        y = sharded_matmul_gathered(torch.from_numpy(x).to(dev), W, out)
-        torch.cuda.synchronize(dev)
         pay, sc = O.quantize_weights(w, O.INT8)  # per-column quantization: the shards' codes are the full matrix's
-        want = O.matmul(x, O.INT8, pay, sc, N)[3]
-        got = y.cpu().numpy()
-        q.put((rank, bool(np.array_equal(got.view(np.uint32), want.view(np.uint32))), zb.device_error()))
+        xs = [x, rng.standard_normal((M, K)).astype(np.float32), rng.standard_normal((M, K)).astype(np.float32)]
+        wants = [O.matmul(xi, O.INT8, pay, sc, N)[3] for xi in xs]
+        # call 1, then call 2 issued before call 1's output is read: the
+        # double-buffered outputs keep y1 intact while call 2 runs
+        y1 = sharded_matmul_gathered(torch.from_numpy(xs[0]).to(dev), W, out)
+        y2 = sharded_matmul_gathered(torch.from_numpy(xs[1]).to(dev), W, out)
+        got1 = y1.cpu().numpy()
+        got2 = y2.cpu().numpy()
+        # call 3 reuses call 1's buffers
+        y3 = sharded_matmul_gathered(torch.from_numpy(xs[2]).to(dev), W, out)
+        got3 = y3.cpu().numpy()
+        torch.cuda.synchronize(dev)
+        ok = all(np.array_equal(g.view(np.uint32), wv.view(np.uint32)) for g, wv in zip((got1, got2, got3), wants))
+        ok = ok and y3.data_ptr() == y1.data_ptr() and y2.data_ptr() != y1.data_ptr()
+        q.put((rank, bool(ok), zb.device_error()))
         dist.barrier()
+        out.close()
     finally:
         dist.destroy_process_group()
 

@@ -25,17 +25,19 @@ def test_damaged_zyqmodel_matches_reference(native_lib, qgold):
         assert L.zq_last_error().decode() == str(msg), name
 
 
-def test_generation_config_validation():
-    from zyron_b200 import _lib
-    from zyron_b200.qlm import GenerationConfig, _validate_generation
+def test_generation_config_validation(native_lib):
+    """validate_generation_config (quantized_language_model.cpp:71-80) and the
+    top_k check (517) run in the C library, with the reference's messages."""
+    from zyron_b200.qlm import GenerationConfig, Sampler
 
-    info = _lib.LmInfo()
-    info.vocab_size = 10
-    with pytest.raises(ValueError, match="invalid temperature"):
-        _validate_generation(GenerationConfig(temperature=0.0), info)
-    with pytest.raises(ValueError, match="invalid top_p"):
-        _validate_generation(GenerationConfig(top_p=1.5), info)
-    with pytest.raises(ValueError, match="invalid repetition_penalty"):
-        _validate_generation(GenerationConfig(repetition_penalty=0.5), info)
-    with pytest.raises(ValueError, match="top_k exceeds vocabulary"):
-        _validate_generation(GenerationConfig(top_k=11), info)
+    s = Sampler(0)
+    row = np.zeros(10, dtype=np.float32)
+    for cfg, msg in [(GenerationConfig(temperature=0.0), "invalid temperature"),
+                     (GenerationConfig(temperature=float("inf")), "invalid temperature"),
+                     (GenerationConfig(top_p=1.5), "invalid top_p"),
+                     (GenerationConfig(top_p=0.0), "invalid top_p"),
+                     (GenerationConfig(repetition_penalty=0.5), "invalid repetition_penalty"),
+                     (GenerationConfig(repetition_penalty=float("nan")), "invalid repetition_penalty"),
+                     (GenerationConfig(top_k=11), "top_k exceeds vocabulary")]:
+        with pytest.raises(ValueError, match=msg):
+            s.next(row, [1, 2], cfg)

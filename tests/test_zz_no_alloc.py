@@ -5,9 +5,9 @@ their scratch from a fixed array inside the library.  This file is collected
 last on purpose, so a run that stops at the first failure has already run
 every other test; it also passes on its own in a fresh process.  The check:
 two calls in a row through the C ABI give exactly the same output as
-zq_matmul with a caller workspace (the library's results are bit-exact, so
-the tolerance is zero), and a request larger than the fixed array is refused
-with a clear error.
+zq_matmul with a caller workspace and as the oracle (the library's results
+are bit-exact, so the tolerance is zero), and a request larger than the fixed
+array is refused with a clear error.
 """
 import ctypes as C
 
@@ -45,6 +45,8 @@ def test_noalloc_matches_workspace_entry_point(cuda, qt, M, K, N):
         g = got.cpu().numpy().view(np.uint32)
         e = want.cpu().numpy().view(np.uint32)
         assert np.array_equal(g, e), f"call {call}: {(g != e).sum()} outputs differ from zq_matmul"
+        o = O.matmul(x.cpu().numpy(), qt, pay, sc, N, bias.cpu().numpy())[3].view(np.uint32)
+        assert np.array_equal(g, o), f"call {call}: {(g != o).sum()} outputs differ from the oracle"
     assert zb.device_error() == 0
 
 

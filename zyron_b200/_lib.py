@@ -108,16 +108,29 @@ SIGNATURES = {
     "zq_matmul_host": (st, [vp, vp, sz, vp, vp, vp]),
     "zq_dequantize": (st, [vp, vp, vp]),
     "zq_device_error": (st, [vp, C.POINTER(C.c_uint32)]),
-    "zq_set_reserved_sms": (C.c_int, [C.c_int]),
-    "zq_set_decode_kernel": (C.c_int, [C.c_int]),
+    "zq_weight_set_option": (st, [vp, C.c_int, C.c_int, C.POINTER(C.c_int)]),
+    "zq_test_decode_wait_timeout": (st, [vp, vp, vp, sz, vp, vp, sz, C.c_uint64, vp]),
+    "zq_lm_set_option": (st, [vp, C.c_int, C.c_int, C.POINTER(C.c_int)]),
     "zq_ipc_export": (st, [vp, vp]),
     "zq_ipc_import": (st, [vp, C.POINTER(vp)]),
     "zq_ipc_close": (st, [vp]),
     "zq_lm_load": (st, [vp, sz, vp, C.POINTER(vp)]),
     "zq_lm_get_info": (st, [vp, vp]),
     "zq_lm_generate_greedy": (st, [vp, vp, sz, sz, vp, sz, C.POINTER(sz), vp, vp]),
+    "zq_lm_generate": (st, [vp, vp, sz, vp, vp, sz, C.POINTER(sz), vp, vp]),
     "zq_lm_destroy": (st, [vp]),
+    "zq_sampler_create": (st, [C.c_uint32, C.POINTER(vp)]),
+    "zq_sampler_destroy": (st, [vp]),
+    "zq_sample_next": (st, [vp, vp, sz, vp, sz, vp, C.POINTER(C.c_int64)]),
 }
+
+
+class GenerationConfigC(C.Structure):
+    """zq_generation_config (include/zq.h)."""
+
+    _fields_ = [("max_new_tokens", C.c_size_t), ("temperature", C.c_float), ("top_k", C.c_size_t),
+                ("top_p", C.c_float), ("repetition_penalty", C.c_float), ("no_repeat_ngram_size", C.c_size_t),
+                ("seed", C.c_uint32)]
 
 
 class IpcHandle(C.Structure):

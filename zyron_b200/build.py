@@ -25,6 +25,12 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 CU_SOURCES = ["zq_api.cu", "zq_quant.cu", "zq_gemv.cu", "zq_gemm_sm100.cu", "zq_skinny_sm100.cu", "zq_noalloc.cu",
               "zq_lm.cu", "zq_sharded.cu"]
 CU_HEADERS = ["zq_common.cuh", "zq_dot.cuh", "zq_tcgen05.cuh", "zq_kernels.h", "zq_internal.h"]
+# Host-only C++ of the library.  zq_sample.cpp restates the reference's token
+# sampler, whose std::sort order and std::mt19937 draws come from the C++
+# standard library, so it is built by g++ with the reference's own Release
+# flags (-std=c++20 -O3 -DNDEBUG).
+HOST_SOURCES = ["zq_sample.cpp"]
+HOST_FLAGS = ["-std=c++20", "-O3", "-DNDEBUG", "-fPIC"]
 CPP_SOURCES = ["src/quantization.cpp", "src/quantized_linear.cpp", "src/tensor.cpp"]
 
 NVCC_FLAGS = [
@@ -51,7 +57,8 @@ def _run(cmd):
 
 def build_cuda(force=False):
     srcs = [os.path.join(CSRC, s) for s in CU_SOURCES]
-    deps = srcs + [os.path.join(CSRC, h) for h in CU_HEADERS] + [os.path.join(ROOT, "include", "zq.h")]
+    hsrcs = [os.path.join(CSRC, s) for s in HOST_SOURCES]
+    deps = srcs + hsrcs + [os.path.join(CSRC, h) for h in CU_HEADERS] + [os.path.join(ROOT, "include", "zq.h")]
     if not force and not _newer(LIB, deps):
         return LIB
     objdir = os.path.join(HERE, "_build")
@@ -59,7 +66,11 @@ def build_cuda(force=False):
     objs = []
     for s in srcs:
         o = os.path.join(objdir, os.path.basename(s) + ".o")
-        _run([NVCC, *NVCC_FLAGS, "-I", os.path.join(ROOT, "include"), "-I", CSRC, "-dc" if False else "-c", s, "-o", o])
+        _run([NVCC, *NVCC_FLAGS, "-I", os.path.join(ROOT, "include"), "-I", CSRC, "-c", s, "-o", o])
+        objs.append(o)
+    for s in hsrcs:
+        o = os.path.join(objdir, os.path.basename(s) + ".o")
+        _run(["g++", *HOST_FLAGS, "-I", os.path.join(ROOT, "include"), "-c", s, "-o", o])
         objs.append(o)
     _run([NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", LIB, *objs, "-cudart", "static",
           "-ldl"])

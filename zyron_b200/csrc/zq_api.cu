@@ -199,16 +199,6 @@ zq_status download_payload(const zq_weight* w, void* payload, cudaStream_t st) {
     return ZQ_OK;
 }
 
-// GEMM tile-order group size (M-tiles per group); ZQ_GEMM_GROUP_M overrides
-// the default for tuning sweeps.
-int gemm_group_m() {
-    static const int g = [] {
-        const char* e = std::getenv("ZQ_GEMM_GROUP_M");
-        return e ? std::atoi(e) : 32;
-    }();
-    return g;
-}
-
 // Packed INT4 panel [N][Kp/2] bytes, box 64 bytes (128 codes) x 128 columns,
 // unswizzled: the decode kernel unpacks it in shared memory.
 zq_status encode_packed_int4(CUtensorMap* map, const void* base, size_t cols, int Kp) {
@@ -538,37 +528,45 @@ zq::OutDesc single_output(float* y, size_t N) {
 // Dot + epilogue on activation codes q [m][Kp] (row stride Kp) and row
 // scales rs; the GEMM path writes through `out` (several destinations when
 // gathering), the GEMV path to out.base[0] with row stride N.
-// Kernel for decode-sized matmuls (zq_set_decode_kernel).
-std::atomic<int> g_decode_kernel{ZQ_DECODE_AUTO};
-
-// Whether a plain-output matmul with M rows runs the dp4a GEMV.  Default:
-// the GEMV for 1-4 rows, where the weight stream alone sets the time and it
-// has the least fixed cost per launch; the tensor cores above that, where
-// dp4a and shared-memory reads of the activation rows limit the GEMV.
+// Whether a plain-output matmul with M rows runs the dp4a GEMV (the weight's
+// ZQ_OPT_DECODE_KERNEL option).  Default: the GEMV for 1-4 rows, where the
+// weight stream alone sets the time and it has the least fixed cost per
+// launch; the tensor cores above that, where dp4a and shared-memory reads of
+// the activation rows limit the GEMV.
 bool use_gemv(const zq_weight* w, int M) {
-    const int decode = g_decode_kernel.load(std::memory_order_relaxed);
+    const int decode = w->opt_decode.load(std::memory_order_relaxed);
     const bool fits = M <= zq::kGemvMaxRows && zq::gemv_smem_bytes(M, w->Kp) <= 200 * 1024;
     return fits && (decode == ZQ_DECODE_CUDA_CORE || (decode == ZQ_DECODE_AUTO && M <= 4));
 }
 
+// Failure-path testing of the decode kernel's bounded waits
+// (zq_test_decode_wait_timeout); absent in every other call.
+struct WaitTest {
+    int wait_extra;
+    uint64_t limit_ns;
+};
+
 zq_status run_codes_out(const zq_weight* w, const int8_t* codes, const float* rs, size_t m, const float* bias,
-                        const zq::OutDesc& out, uint8_t* scratch, cudaStream_t st, bool pdl);
+                        const zq::OutDesc& out, uint8_t* scratch, cudaStream_t st, bool pdl,
+                        const WaitTest* test = nullptr);
 
 zq_status run_codes(const zq_weight* w, const int8_t* codes, const float* rs, size_t m, const float* bias, float* y,
-                    uint8_t* scratch, cudaStream_t st, bool pdl) {
-    return run_codes_out(w, codes, rs, m, bias, single_output(y, w->N), scratch, st, pdl);
+                    uint8_t* scratch, cudaStream_t st, bool pdl, const WaitTest* test = nullptr) {
+    return run_codes_out(w, codes, rs, m, bias, single_output(y, w->N), scratch, st, pdl, test);
 }
 
 zq_status run_codes_out(const zq_weight* w, const int8_t* codes, const float* rs, size_t m, const float* bias,
-                        const zq::OutDesc& out, uint8_t* scratch, cudaStream_t st, bool pdl) {
+                        const zq::OutDesc& out, uint8_t* scratch, cudaStream_t st, bool pdl, const WaitTest* test) {
     float* y = out.base[0];
     uint32_t* err = nullptr;
     zq_status s = device_error_ptr(&err);
     if (s != ZQ_OK) return s;
     const int M = (int)m, N = (int)w->N, Kp = w->Kp;
+    const int reserved = w->opt_reserved_sms.load(std::memory_order_relaxed);
     const bool plain = out.count == 1 && out.ldy == (long long)N && out.col_offset == 0;
-    if (plain && use_gemv(w, M)) {
+    if (plain && !test && use_gemv(w, M)) {
         zq::GemvArgs a{w->type, w->panel, N, Kp, w->scales, codes, rs, bias, y, M};
+        a.reserved_sms = reserved;
         ZQ_CUDA(zq::launch_gemv(a, st, pdl));
         return ZQ_OK;
     }
@@ -604,6 +602,11 @@ zq_status run_codes_out(const zq_weight* w, const int8_t* codes, const float* rs
             }
         }
         zq::SkinnyArgs a{w->type, tmap_w, &tmap_x, M, N, Kp, rs, w->scales, bias, y, counters, partials, err};
+        a.reserved_sms = reserved;
+        if (test) {
+            a.wait_extra = test->wait_extra;
+            a.peer_limit_ns = test->limit_ns;
+        }
         ZQ_CUDA(zq::launch_skinny(a, st, true));
         return ZQ_OK;
     }
@@ -631,7 +634,9 @@ zq_status run_codes_out(const zq_weight* w, const int8_t* codes, const float* rs
         tmap_b = &tmap_b_local;
         pdl = true;  // the GEMM follows the expand kernel directly
     }
-    zq::GemmArgs g{&tmap_a, tmap_b, M, N, Kp, bn, rs, w->scales, bias, out, err, gemm_group_m()};
+    zq::GemmArgs g{&tmap_a, tmap_b, M, N, Kp, bn, rs, w->scales, bias, out, err,
+                   w->opt_group_m.load(std::memory_order_relaxed)};
+    g.reserved_sms = reserved;
     ZQ_CUDA(zq::launch_gemm(g, st, pdl));
     return ZQ_OK;
 }
@@ -647,6 +652,7 @@ zq_status matmul_in_workspace_out(const zq_weight* w, const float* x, size_t m, 
         zq::GemvArgs a{w->type, w->panel, (int)w->N, w->Kp, w->scales, nullptr, nullptr, bias, out.base[0], (int)m};
         a.x = x;
         a.K = (int)w->K;
+        a.reserved_sms = w->opt_reserved_sms.load(std::memory_order_relaxed);
         ZQ_CUDA(zq::launch_gemv(a, st, false));
         return ZQ_OK;
     }
@@ -905,11 +911,48 @@ zq_status zq_dequantize_host(const zq_weight* w, float* out_host, void* stream) 
     return ZQ_OK;
 }
 
-int zq_set_reserved_sms(int sms) { return zq::set_reserved_sms(sms); }
+zq_status zq_weight_set_option(zq_weight* w, int option, int value, int* previous) {
+    if (!w) return fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON quantization: weights are empty");
+    std::atomic<int>* slot = nullptr;
+    switch (option) {
+        case ZQ_OPT_DECODE_KERNEL:
+            if (value < ZQ_DECODE_AUTO || value > ZQ_DECODE_CUDA_CORE)
+                return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: unknown decode kernel");
+            slot = &w->opt_decode;
+            break;
+        case ZQ_OPT_RESERVED_SMS:
+            if (value < 0) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: reserved SM count must be >= 0");
+            slot = &w->opt_reserved_sms;
+            break;
+        case ZQ_OPT_GEMM_GROUP_M:
+            if (value < 0) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: GEMM group size must be >= 0");
+            slot = &w->opt_group_m;
+            break;
+        default:
+            return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: unknown weight option");
+    }
+    const int old = slot->exchange(value);
+    if (previous) *previous = old;
+    return ZQ_OK;
+}
 
-int zq_set_decode_kernel(int kind) {
-    if (kind < ZQ_DECODE_AUTO || kind > ZQ_DECODE_CUDA_CORE) kind = ZQ_DECODE_AUTO;
-    return g_decode_kernel.exchange(kind);
+zq_status zq_test_decode_wait_timeout(const zq_weight* w, const int8_t* q, const float* row_scale, size_t m,
+                                      float* y, void* workspace, size_t workspace_bytes, uint64_t limit_ns,
+                                      void* stream) {
+    if (!w) return fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON quantization: weights are empty");
+    if (m == 0 || m > (size_t)zq::kSkinnyMaxRows)
+        return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: the decode kernel takes 1 to 16 rows");
+    if (!row_scale) return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null row scales");
+    if (limit_ns < 100000ull || limit_ns > 1000000000ull)
+        return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: limit_ns must be within [1e5, 1e9]");
+    zq_status s = validate_matmul(w, m, q, y, workspace, workspace_bytes);
+    if (s != ZQ_OK) return s;
+    if ((reinterpret_cast<uintptr_t>(q) & 15u) != 0)
+        return fail(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: codes must be 16-byte aligned");
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    uint8_t* scratch = ws + align256(m * (size_t)w->Kp) + align256(m * sizeof(float));
+    const WaitTest t{1, limit_ns};
+    return run_codes(w, q, row_scale, m, nullptr, y, scratch, as_stream(stream), false, &t);
 }
 
 zq_status zq_ipc_export(const void* dev_ptr, zq_ipc_handle* out) {

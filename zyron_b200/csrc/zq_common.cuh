@@ -182,6 +182,25 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     }
 }
 
+// Bounded wait for this CTA's own copies or MMAs before it exits (the drain
+// after a loop ended, normally or on an error).  Unlike mbar_wait_bounded it
+// does not give up when another CTA has recorded an error: whatever this CTA
+// issued must land before its shared memory and TMEM are released.  It still
+// gives up after `limit_ns`, recording `code`.
+__device__ __forceinline__ bool mbar_drain_bounded(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t code,
+                                                   uint64_t limit_ns = 4000000000ull) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    uint32_t spins = 0;
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((++spins & 255u) == 0u && global_timer_ns() - t0 > limit_ns) {
+            atomicCAS(err, kDevErrNone, code);
+            return false;
+        }
+    }
+}
+
 // TMA 2D tiled load into shared memory, completion on an mbarrier.
 __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_t* bar, int x, int y) {
     asm volatile(

@@ -282,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // Drain: every copy this thread issued must land before the CTA
             // can exit (on the normal path these waits return at once).
             for (int s = 0; s < STAGES; ++s)
-                if (issued[s]) mbar_wait_bounded(&full[s], last_phase[s], err, kDevErrTimeoutDrain);
+                if (issued[s]) mbar_drain_bounded(&full[s], last_phase[s], err, kDevErrTimeoutDrain);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -318,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // All MMAs issued by this thread complete before TMEM is freed.
             umma_commit(mma_done);
-            mbar_wait_bounded(mma_done, 0, err, kDevErrTimeoutDrain);
+            mbar_drain_bounded(mma_done, 0, err, kDevErrTimeoutDrain);
         }
     } else {
         // Epilogue warps 2..5 own TMEM lane quarters (warp % 4) * 32.
@@ -378,7 +378,7 @@ cudaError_t launch_gemm_t(const GemmArgs& a, cudaStream_t stream, bool pdl) {
     const int smem = S::kTotal + (gather ? kEpiBytes : 0);
     cudaError_t e = ensure_smem_attr(kern, smem);
     if (e != cudaSuccess) return e;
-    const int sms = sm_count();
+    const int sms = sm_count(a.reserved_sms);
     const int tiles = ((a.M + kBM - 1) / kBM) * ((a.N + BN - 1) / BN);
     const int grid = tiles < sms ? tiles : sms;
 
@@ -562,9 +562,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int s = 0; s < kStages2; ++s) {
                 if (!issued[s]) continue;
                 if (leader)
-                    mbar_wait_bounded(&full[s], last_phase[s], err, kDevErrTimeoutDrain);
+                    mbar_drain_bounded(&full[s], last_phase[s], err, kDevErrTimeoutDrain);
                 else
-                    mbar_wait_bounded(&empty[s], last_phase[s], err, kDevErrTimeoutDrain);
+                    mbar_drain_bounded(&empty[s], last_phase[s], err, kDevErrTimeoutDrain);
             }
         }
     } else if (warp == 1) {
@@ -599,11 +599,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (++acc == 2) acc = 0, acc_phase ^= 1u;
             }
             umma_commit_pair(mma_done);
-            mbar_wait_bounded(mma_done, 0, err, kDevErrTimeoutDrain);
+            mbar_drain_bounded(mma_done, 0, err, kDevErrTimeoutDrain);
         } else if (lane == 0) {
             // peer: its TMEM is written by the leader's MMAs; wait for them to
             // finish before the final barrier frees TMEM
-            mbar_wait_bounded(mma_done, 0, err, kDevErrTimeoutDrain);
+            mbar_drain_bounded(mma_done, 0, err, kDevErrTimeoutDrain);
         }
     } else {
         const int quarter = warp & 3;
@@ -656,7 +656,7 @@ cudaError_t launch_gemm_pair(const GemmArgs& a, cudaStream_t stream, bool pdl) {
     const int smem = S::kTotal + (gather ? kEpiBytes : 0);
     cudaError_t e = ensure_smem_attr(kern, smem);
     if (e != cudaSuccess) return e;
-    const int sms = sm_count();
+    const int sms = sm_count(a.reserved_sms);
     const int tiles = ((a.M + 255) / 256) * ((a.N + 255) / 256);
     int clusters = sms / 2;
     if (clusters < 1) clusters = 1;
@@ -696,9 +696,7 @@ cudaError_t ensure_smem_attr_ptr(const void* kern, size_t bytes) {
     return e;
 }
 
-std::atomic<int> g_reserved_sms{0};
-
-int sm_count() {
+int sm_count(int reserved) {
     static int cached[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -711,11 +709,9 @@ int sm_count() {
         }
         sms = cached[dev];
     }
-    const int avail = sms - g_reserved_sms.load(std::memory_order_relaxed);
+    const int avail = sms - (reserved > 0 ? reserved : 0);
     return avail >= 2 ? avail : 2;
 }
-
-int set_reserved_sms(int sms) { return g_reserved_sms.exchange(sms < 0 ? 0 : sms); }
 
 int gemm_block_n(int M, int N) {
     // 2-SM 256 x 256 tiles when there are at least two per SM pair;

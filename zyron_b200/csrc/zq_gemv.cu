@@ -247,7 +247,7 @@ cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
     auto kern = gemv_kernel<kType, kM, kCols, kUnroll, kFused, kThreads>;
     cudaError_t e = ensure_smem_attr(kern, smem);
     if (e != cudaSuccess) return e;
-    const int sms = sm_count();
+    const int sms = sm_count(a.reserved_sms);
     int per_sm = 0;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
     if (e != cudaSuccess) return e;

@@ -5,6 +5,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
 #include <mutex>
@@ -28,6 +29,10 @@ struct zq_weight {
     // INT4: tensor map over the packed panel for the decode kernel.
     CUtensorMap tmap_w4;
     bool tmap_w4_ready = false;
+    // Options of this weight's matmuls (zq_weight_set_option).
+    std::atomic<int> opt_decode{ZQ_DECODE_AUTO};
+    std::atomic<int> opt_reserved_sms{0};
+    std::atomic<int> opt_group_m{32};
 };
 
 namespace zq {

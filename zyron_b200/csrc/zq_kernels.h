@@ -32,6 +32,7 @@ struct GemvArgs {
     int M;
     const float* x = nullptr; // fp32 activations [M][K], quantized inside the kernel (M <= 4)
     int K = 0;
+    int reserved_sms = 0;     // SMs left out of the grid
 };
 
 // Where the GEMM epilogue writes: element (row, col) of the matmul goes to
@@ -57,6 +58,7 @@ struct GemmArgs {
     OutDesc out;
     uint32_t* err;
     int group_m;  // tile-order group size in M-tiles (0 = all M-tiles)
+    int reserved_sms = 0;  // SMs left out of the persistent grid
 };
 
 // `zero` (n_zero ints, may be NULL) is cleared by the same launch: the
@@ -90,6 +92,12 @@ struct SkinnyArgs {
     int* counters;  // skinny_counter_words(N), zero when the kernel starts
     int* partials;  // kSkinnyMaxCtas * 2 * M * 128
     uint32_t* err;
+    // Failure-path testing only (0 otherwise): a split block's finisher waits
+    // for wait_extra more partial sums than exist, giving up after
+    // peer_limit_ns (0: the default 4 s).
+    int wait_extra = 0;
+    uint64_t peer_limit_ns = 0;
+    int reserved_sms = 0;  // SMs left out of the grid
 };
 int skinny_blocks(int N);
 // Arrival and publication counters of the split blocks (8 per block).
@@ -102,9 +110,8 @@ cudaError_t launch_skinny(const SkinnyArgs& a, cudaStream_t stream, bool pdl);
 int gemm_block_n(int M, int N);
 
 // Multiprocessors of the current device available to the persistent kernels
-// (device count cached per device, minus the reserved count).
-int sm_count();
-int set_reserved_sms(int sms);
+// (device count cached per device, minus `reserved`, at least 2).
+int sm_count(int reserved = 0);
 
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) at most once per kernel
 // (keyed by the kernel's address) and size: host-side launch overhead matters

@@ -45,10 +45,17 @@
 #include <cstdlib>
 #include <cstring>
 #include <limits>
+#include <random>
 #include <string>
 #include <vector>
 
 namespace zq {
+
+// zq_sample.cpp: validate_generation_config and sample_next on the host.
+zq_status check_generation_config(const zq_generation_config* c);
+std::size_t sample_row(std::mt19937& rng, const float* logits, std::size_t vocab, const int64_t* history,
+                       std::size_t len, const zq_generation_config& cfg);
+
 namespace lm {
 
 constexpr int kThreads = 256;
@@ -458,6 +465,114 @@ __global__ void __launch_bounds__(256) next_token_kernel(ArgmaxArgs am, int nslo
         tokens[pos + 1] = token_from_key(best, __ldcg(am.nan), V);
         *am.nan = 0;  // ready for the next step's lm_head
     }
+    st->pos = pos + 1;
+}
+
+// Repetition penalty and n-gram block of a greedy step, read by the captured
+// step from device memory so that one graph serves every setting.
+struct PenaltyCfg {
+    float rep;  // repetition_penalty (1 = off)
+    int ngram;  // no_repeat_ngram_size (0 = off)
+};
+
+constexpr int kPenaltyThreads = 1024;
+
+// Block-wide maximum of 64-bit keys; every thread gets the result.
+__device__ unsigned long long block_max_key(unsigned long long v, unsigned long long* sh) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, v, o);
+        if (other > v) v = other;
+    }
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+    __syncthreads();
+    unsigned long long best = sh[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+        if (sh[w] > best) best = sh[w];
+    return best;
+}
+
+// Greedy choice with the repetition penalty and the n-gram block of
+// sample_next (82-174, with top_k = 1) over the full logits row and the token
+// history tokens[0, pos] (the prompt and the tokens generated so far):
+//   value = logit, divided by the penalty (value >= 0) or multiplied by it
+//   (value < 0) for tokens of the history; -inf for tokens that followed an
+//   earlier occurrence of the last n - 1 tokens; if no value is finite and a
+//   block applied, the raw logits instead (120-128).  The token is the
+//   largest value (lowest id on ties), or 0 when the reference's softmax
+//   denominator is not finite: a NaN value, or a maximum of +-inf.
+// One block; `bits` holds 2 * ceil(V / 32) words of dynamic shared memory.
+__global__ void __launch_bounds__(kPenaltyThreads) next_token_penalized_kernel(const float* logits, int V,
+                                                                               int32_t* tokens, State* st,
+                                                                               const PenaltyCfg* pc, int* nan_flag) {
+    extern __shared__ uint32_t bits[];
+    __shared__ unsigned long long red[kPenaltyThreads / 32];
+    __shared__ int flags;  // bit 0: a block applies; 1: NaN value; 2: finite value; 3: NaN logit
+    pdl_launch_dependents();
+    pdl_wait_primary();
+    const int tid = threadIdx.x;
+    const int pos = __ldcg(&st->pos);
+    if (pos + 1 < __ldcg(&st->prompt_len)) {  // prefill: no choice
+        if (tid == 0) st->pos = pos + 1;
+        return;
+    }
+    const int words = (V + 31) >> 5;
+    uint32_t* seen = bits;
+    uint32_t* blocked = bits + words;
+    for (int i = tid; i < 2 * words; i += kPenaltyThreads) bits[i] = 0u;
+    if (tid == 0) flags = 0;
+    __syncthreads();
+    const float rep = pc->rep;
+    const int n = pc->ngram;
+    const int len = pos + 1;
+    if (rep != 1.0f)
+        for (int i = tid; i < len; i += kPenaltyThreads) {
+            const int t = __ldcg(tokens + i);
+            if (t >= 0 && t < V) atomicOr(&seen[t >> 5], 1u << (t & 31));
+        }
+    if (n > 0 && len >= n) {
+        const int pl = n - 1;
+        for (int start = tid; start + n <= len; start += kPenaltyThreads) {
+            bool match = true;
+            for (int k = 0; k < pl && match; ++k) match = __ldcg(tokens + start + k) == __ldcg(tokens + len - pl + k);
+            if (!match) continue;
+            const int t = __ldcg(tokens + start + pl);
+            atomicOr(&flags, 1);
+            if (t >= 0 && t < V) atomicOr(&blocked[t >> 5], 1u << (t & 31));
+        }
+    }
+    __syncthreads();
+    const bool have_block = flags & 1;
+    unsigned long long best = 0ull, best_raw = 0ull;
+    int f = 0;
+    for (int id = tid; id < V; id += kPenaltyThreads) {
+        const float raw = __ldcg(logits + id);
+        float v = raw;
+        if (rep != 1.0f && ((seen[id >> 5] >> (id & 31)) & 1u)) v = v >= 0.0f ? __fdiv_rn(v, rep) : __fmul_rn(v, rep);
+        if (have_block && ((blocked[id >> 5] >> (id & 31)) & 1u)) v = -INFINITY;
+        if (isnan(v)) {
+            f |= 2;
+        } else {
+            const unsigned long long k = argmax_key(v, id);
+            if (k > best) best = k;
+            if (isfinite(v)) f |= 4;
+        }
+        if (isnan(raw)) {
+            f |= 8;
+        } else {
+            const unsigned long long k = argmax_key(raw, id);
+            if (k > best_raw) best_raw = k;
+        }
+    }
+    if (f) atomicOr(&flags, f);
+    best = block_max_key(best, red);
+    best_raw = block_max_key(best_raw, red);
+    if (tid != 0) return;
+    const int fl = flags;
+    const bool use_raw = !(fl & 4) && (fl & 1);
+    tokens[pos + 1] = use_raw ? token_from_key(best_raw, fl & 8, V) : token_from_key(best, fl & 2, V);
+    *nan_flag = 0;  // the lm_head raised it on a NaN logit; unused here
     st->pos = pos + 1;
 }
 
@@ -1452,6 +1567,11 @@ struct zq_lm {
     std::vector<void*> allocations;
     cudaGraphExec_t graph_one = nullptr;
     cudaGraphExec_t graph_chunk = nullptr;
+    // the same step ending in the penalised greedy choice
+    cudaGraphExec_t graph_one_pen = nullptr;
+    cudaGraphExec_t graph_chunk_pen = nullptr;
+    zq::lm::PenaltyCfg* penalty = nullptr;  // read by next_token_penalized_kernel
+    size_t penalty_smem = 0;                // its bitmaps
     // persistent decode (step_kernel): layer descriptors, barrier, argmax keys
     zq::lm::LayerDesc* layer_desc = nullptr;
     unsigned int* bar = nullptr;
@@ -1463,6 +1583,7 @@ struct zq_lm {
     size_t step_smem = 0;
     int xmax = 0;
     int chunk = 16;
+    int persistent = 0;  // ZQ_LM_OPT_PERSISTENT
     // Used when the caller passes no stream: graph capture needs a stream
     // that is not a default stream.
     cudaStream_t own_stream = nullptr;
@@ -1475,6 +1596,8 @@ zq_lm::~zq_lm() {
     if (cur != device) cudaSetDevice(device);
     if (graph_one) cudaGraphExecDestroy(graph_one);
     if (graph_chunk) cudaGraphExecDestroy(graph_chunk);
+    if (graph_one_pen) cudaGraphExecDestroy(graph_one_pen);
+    if (graph_chunk_pen) cudaGraphExecDestroy(graph_chunk_pen);
     if (own_stream) cudaStreamDestroy(own_stream);
     zq_weight_destroy(emb);
     zq_weight_destroy(head);
@@ -1637,8 +1760,9 @@ cudaError_t launch_normed(bool rms, const float* x, const float* nw, const float
                : launch_linear<zq::lm::kProLayer, kEpi>(x, nw, nb, eps, w, bias, y, st, skip, s);
 }
 
-// Enqueue one decode step (all kernels) on `s`.
-cudaError_t enqueue_step(zq_lm* lm, cudaStream_t s) {
+// Enqueue one decode step (all kernels) on `s`; `penalized` ends it with the
+// greedy choice under the repetition penalty and n-gram block.
+cudaError_t enqueue_step(zq_lm* lm, cudaStream_t s, bool penalized = false) {
     const zq_lm_info& c = lm->info;
     const int hd = (int)(c.hidden_size / c.num_heads);
     const int kvh = (int)(c.num_kv_heads == 0 ? c.num_heads : c.num_kv_heads);
@@ -1687,6 +1811,10 @@ cudaError_t enqueue_step(zq_lm* lm, cudaStream_t s) {
     e = launch_linear<zq::lm::kProRms, zq::lm::kEpiLogits>(lm->h, lm->final_w, nullptr, eps, lm->head, lm->b_head,
                                                            lm->logits, lm->state, 1, s, {}, am, lm->head_blocks);
     if (e != cudaSuccess) return e;
+    if (penalized)
+        return launch_pdl(zq::lm::next_token_penalized_kernel, dim3(1), dim3(zq::lm::kPenaltyThreads),
+                          lm->penalty_smem, s, (const float*)lm->logits, (int)c.vocab_size, lm->tokens, lm->state,
+                          (const zq::lm::PenaltyCfg*)lm->penalty, lm->nan_flags);
     return launch_pdl(zq::lm::next_token_kernel, dim3(1), dim3(256), 0, s, am, lm->head_blocks, (int)c.vocab_size,
                       lm->tokens, lm->state);
 }
@@ -1807,11 +1935,11 @@ cudaError_t launch_persistent(zq_lm* lm, int steps, int prompt_len, float* step_
                                   : cudaLaunchKernelEx(&cfg, zq::lm::step_kernel<zq::kInt4>, p);
 }
 
-cudaError_t build_graph(zq_lm* lm, int steps, cudaGraphExec_t* out, cudaStream_t s) {
+cudaError_t build_graph(zq_lm* lm, int steps, cudaGraphExec_t* out, cudaStream_t s, bool penalized = false) {
     cudaGraph_t g = nullptr;
     cudaError_t e = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
     if (e != cudaSuccess) return e;
-    for (int i = 0; i < steps && e == cudaSuccess; ++i) e = enqueue_step(lm, s);
+    for (int i = 0; i < steps && e == cudaSuccess; ++i) e = enqueue_step(lm, s, penalized);
     cudaError_t e2 = cudaStreamEndCapture(s, &g);
     if (e == cudaSuccess) e = e2;
     if (e == cudaSuccess) e = cudaGraphInstantiate(out, g, 0);
@@ -2000,6 +2128,15 @@ zq_status zq_lm_load(const void* bytes, size_t len, void* stream, zq_lm** out) {
         e = dev_alloc(lm, &lm->attn_part, c.num_heads * (size_t)lm->attn_splits * (zq::lm::kMaxHeadDim + 2));
     if (e == cudaSuccess) e = dev_alloc(lm, &lm->tokens, T + 2);
     if (e == cudaSuccess) e = dev_alloc(lm, &lm->state, 1);
+    if (e == cudaSuccess) e = dev_alloc(lm, &lm->penalty, 1);
+    lm->penalty_smem = 2 * ((V + 31) / 32) * sizeof(uint32_t);
+    if (e == cudaSuccess && lm->penalty_smem > 48 * 1024) {
+        if (lm->penalty_smem <= kMaxLinearSmem)
+            e = cudaFuncSetAttribute(zq::lm::next_token_penalized_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)lm->penalty_smem);
+        else
+            lm->penalty_smem = 0;  // vocabulary too large for the device bitmaps: penalties are applied on the host
+    }
     if (e == cudaSuccess && c.use_rope) {
         // apply_rope factors (quantized_language_model.cpp:367-374), computed
         // with the same float formula: angle = pos / pow(theta, 2p / hd).
@@ -2028,36 +2165,53 @@ zq_status zq_lm_load(const void* bytes, size_t len, void* stream, zq_lm** out) {
     return ZQ_OK;
 }
 
+zq_status zq_lm_set_option(zq_lm* lm, int option, int value, int* previous) {
+    if (!lm) return fail_lm(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null model");
+    if (option != ZQ_LM_OPT_PERSISTENT) return fail_lm(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: unknown model option");
+    if (value != 0 && value != 1) return fail_lm(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: option value must be 0 or 1");
+    if (previous) *previous = lm->persistent;
+    lm->persistent = value;
+    return ZQ_OK;
+}
+
 zq_status zq_lm_get_info(const zq_lm* lm, zq_lm_info* info) {
     if (!lm || !info) return fail_lm(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null argument");
     *info = lm->info;
     return ZQ_OK;
 }
 
-zq_status zq_lm_generate_greedy(zq_lm* lm, const int64_t* prompt, size_t prompt_len, size_t max_new_tokens,
-                                int64_t* out_tokens, size_t out_cap, size_t* out_len, float* step_logits,
-                                void* stream) {
+zq_status zq_lm_generate(zq_lm* lm, const int64_t* prompt, size_t prompt_len, const zq_generation_config* config,
+                         int64_t* out_tokens, size_t out_cap, size_t* out_len, float* step_logits, void* stream) {
     if (!lm) return fail_lm(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null model");
     const zq_lm_info& c = lm->info;
-    // generate_batch checks (quantized_language_model.cpp:503-517)
+    // generate_batch checks, in its order (quantized_language_model.cpp:503-517)
+    zq_status vs = zq::check_generation_config(config);
+    if (vs != ZQ_OK) return vs;
+    const zq_generation_config& cfg = *config;
     if (prompt_len == 0 || !prompt) return fail_lm(ZQ_ERR_INVALID_ARGUMENT, "ZYRON QuantizedLanguageModel: empty prompt");
     if (prompt_len > c.max_sequence_length)
         return fail_lm(ZQ_ERR_INVALID_ARGUMENT, "ZYRON QuantizedLanguageModel: prompt exceeds context");
-    for (size_t i = 0; i < prompt_len; ++i)
-        if (prompt[i] < 0 || (uint64_t)prompt[i] >= c.vocab_size)
-            return fail_lm(ZQ_ERR_OUT_OF_RANGE, "ZYRON QuantizedLanguageModel: token id out of range");
+    if (cfg.top_k > c.vocab_size)
+        return fail_lm(ZQ_ERR_INVALID_ARGUMENT, "ZYRON QuantizedLanguageModel: top_k exceeds vocabulary");
     // tokens stop growing once they reach max_sequence_length (539-545)
     size_t n_new = 0;
-    if (max_new_tokens > 0) {
+    if (cfg.max_new_tokens > 0) {
         const size_t room = c.max_sequence_length > prompt_len ? c.max_sequence_length - prompt_len : 1;
-        n_new = max_new_tokens < room ? max_new_tokens : room;
+        n_new = cfg.max_new_tokens < room ? cfg.max_new_tokens : room;
     }
     const size_t total = prompt_len + n_new;
     if (out_len) *out_len = total;
     if (!out_tokens || out_cap < total)
         return fail_lm(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: output token buffer too small");
+    if (n_new == 0) {  // the reference's loop never runs, so nothing reads the ids
+        for (size_t i = 0; i < prompt_len; ++i) out_tokens[i] = prompt[i];
+        return ZQ_OK;
+    }
+    // token_lookup (271-282), which the first forward runs
+    for (size_t i = 0; i < prompt_len; ++i)
+        if (prompt[i] < 0 || (uint64_t)prompt[i] >= c.vocab_size)
+            return fail_lm(ZQ_ERR_OUT_OF_RANGE, "ZYRON QuantizedLanguageModel: token id out of range");
     for (size_t i = 0; i < prompt_len; ++i) out_tokens[i] = prompt[i];
-    if (n_new == 0) return ZQ_OK;
 
     int cur = 0;
     LM_CUDA(cudaGetDevice(&cur));
@@ -2068,14 +2222,48 @@ zq_status zq_lm_generate_greedy(zq_lm* lm, const int64_t* prompt, size_t prompt_
     State s0{0, (int)prompt_len, {0, 0}};
     LM_CUDA(cudaMemcpyAsync(lm->tokens, tok.data(), tok.size() * sizeof(int32_t), cudaMemcpyHostToDevice, st));
     LM_CUDA(cudaMemcpyAsync(lm->state, &s0, sizeof s0, cudaMemcpyHostToDevice, st));
+    // the lm_head's argmax key starts cleared
+    LM_CUDA(cudaMemsetAsync(lm->keys, 0, 2 * sizeof(unsigned long long), st));
+    LM_CUDA(cudaMemsetAsync(lm->nan_flags, 0, 2 * sizeof(int), st));
 
     const size_t steps = prompt_len - 1 + n_new;  // last step produces the last new token
-    // ZQ_LM_PERSISTENT=1: every step in one cooperative launch of
+    const bool penalties = cfg.repetition_penalty != 1.0f || cfg.no_repeat_ngram_size > 0;
+    const bool greedy = cfg.top_k == 1 && (!penalties || lm->penalty_smem > 0);
+
+    if (!greedy) {
+        // Sampling: every step's logits go to the host, where the reference's
+        // sample_next (82-174) picks the token from std::mt19937(seed)
+        // (520), which is then written into the device token history.  The
+        // prompt's positions need no choice and run as graph replays.
+        std::mt19937 rng(cfg.seed);
+        std::vector<float> row(c.vocab_size);
+        if (!lm->graph_one) LM_CUDA(build_graph(lm, 1, &lm->graph_one, st));
+        for (size_t i = 0; i + 1 < prompt_len; ++i) LM_CUDA(cudaGraphLaunch(lm->graph_one, st));
+        for (size_t g = 0; g < n_new; ++g) {
+            LM_CUDA(cudaGraphLaunch(lm->graph_one, st));
+            LM_CUDA(cudaMemcpyAsync(row.data(), lm->logits, c.vocab_size * sizeof(float), cudaMemcpyDeviceToHost, st));
+            LM_CUDA(cudaStreamSynchronize(st));
+            if (step_logits) std::memcpy(step_logits + g * c.vocab_size, row.data(), c.vocab_size * sizeof(float));
+            const size_t t = zq::sample_row(rng, row.data(), c.vocab_size, out_tokens, prompt_len + g, cfg);
+            out_tokens[prompt_len + g] = (int64_t)t;
+            tok[prompt_len + g] = (int32_t)t;
+            // the step's own greedy choice sits in the same slot; overwrite it
+            if (g + 1 < n_new)
+                LM_CUDA(cudaMemcpyAsync(lm->tokens + prompt_len + g, &tok[prompt_len + g], sizeof(int32_t),
+                                        cudaMemcpyHostToDevice, st));
+        }
+        LM_CUDA(cudaStreamSynchronize(st));
+        return ZQ_OK;
+    }
+
+    if (penalties) {
+        const zq::lm::PenaltyCfg pc{cfg.repetition_penalty, (int)std::min<size_t>(cfg.no_repeat_ngram_size, 1u << 30)};
+        LM_CUDA(cudaMemcpyAsync(lm->penalty, &pc, sizeof pc, cudaMemcpyHostToDevice, st));
+    }
+    // ZQ_LM_OPT_PERSISTENT: every step in one cooperative launch of
     // step_kernel (when the device allows it); otherwise the kernel chain
-    // replayed from CUDA graphs, which measured marginally faster on B200
-    // (0.479 vs 0.487 ms per token, 768-wide 12-layer model).
-    const char* persistent = std::getenv("ZQ_LM_PERSISTENT");
-    if (lm->step_grid > 0 && persistent && persistent[0] == '1') {
+    // replayed from CUDA graphs.
+    if (!penalties && lm->step_grid > 0 && lm->persistent) {
         // persistent decode: every step in one cooperative launch
         uint32_t* err = nullptr;
         zq_status es = zq::device_error_word(&err);
@@ -2087,39 +2275,49 @@ zq_status zq_lm_generate_greedy(zq_lm* lm, const int64_t* prompt, size_t prompt_
             le = cudaMemcpyAsync(step_logits, dlog, n_new * c.vocab_size * sizeof(float), cudaMemcpyDeviceToHost, st);
         if (dlog) cudaFreeAsync(dlog, st);
         LM_CUDA(le);
+    } else if (step_logits) {
+        // parity mode: per step, copy the logits that chose each new token
+        for (size_t i = 0; i < steps; ++i) {
+            LM_CUDA(enqueue_step(lm, st, penalties));
+            if (i + 1 >= prompt_len) {
+                const size_t g = i + 1 - prompt_len;
+                LM_CUDA(cudaMemcpyAsync(step_logits + g * c.vocab_size, lm->logits, c.vocab_size * sizeof(float),
+                                        cudaMemcpyDeviceToHost, st));
+            }
+        }
     } else {
-        // the kernel chain; the lm_head's argmax key starts cleared
-        LM_CUDA(cudaMemsetAsync(lm->keys, 0, 2 * sizeof(unsigned long long), st));
-        LM_CUDA(cudaMemsetAsync(lm->nan_flags, 0, 2 * sizeof(int), st));
-        if (step_logits) {
-            // parity mode: per step, copy the logits that chose each new token
-            for (size_t i = 0; i < steps; ++i) {
-                LM_CUDA(enqueue_step(lm, st));
-                if (i + 1 >= prompt_len) {
-                    const size_t g = i + 1 - prompt_len;
-                    LM_CUDA(cudaMemcpyAsync(step_logits + g * c.vocab_size, lm->logits, c.vocab_size * sizeof(float),
-                                            cudaMemcpyDeviceToHost, st));
-                }
-            }
-        } else {
-            if (!lm->graph_one) LM_CUDA(build_graph(lm, 1, &lm->graph_one, st));
-            if (!lm->graph_chunk && steps >= (size_t)lm->chunk)
-                LM_CUDA(build_graph(lm, lm->chunk, &lm->graph_chunk, st));
-            size_t done = 0;
-            while (steps - done >= (size_t)lm->chunk && lm->graph_chunk) {
-                LM_CUDA(cudaGraphLaunch(lm->graph_chunk, st));
-                done += lm->chunk;
-            }
-            while (done < steps) {
-                LM_CUDA(cudaGraphLaunch(lm->graph_one, st));
-                ++done;
-            }
+        cudaGraphExec_t& one = penalties ? lm->graph_one_pen : lm->graph_one;
+        cudaGraphExec_t& chunk = penalties ? lm->graph_chunk_pen : lm->graph_chunk;
+        if (!one) LM_CUDA(build_graph(lm, 1, &one, st, penalties));
+        if (!chunk && steps >= (size_t)lm->chunk) LM_CUDA(build_graph(lm, lm->chunk, &chunk, st, penalties));
+        size_t done = 0;
+        while (steps - done >= (size_t)lm->chunk && chunk) {
+            LM_CUDA(cudaGraphLaunch(chunk, st));
+            done += lm->chunk;
+        }
+        while (done < steps) {
+            LM_CUDA(cudaGraphLaunch(one, st));
+            ++done;
         }
     }
     LM_CUDA(cudaMemcpyAsync(tok.data(), lm->tokens, total * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
     LM_CUDA(cudaStreamSynchronize(st));
     for (size_t i = prompt_len; i < total; ++i) out_tokens[i] = tok[i];
     return ZQ_OK;
+}
+
+zq_status zq_lm_generate_greedy(zq_lm* lm, const int64_t* prompt, size_t prompt_len, size_t max_new_tokens,
+                                int64_t* out_tokens, size_t out_cap, size_t* out_len, float* step_logits,
+                                void* stream) {
+    zq_generation_config cfg{};
+    cfg.max_new_tokens = max_new_tokens;
+    cfg.temperature = 1.0f;
+    cfg.top_k = 1;
+    cfg.top_p = 1.0f;
+    cfg.repetition_penalty = 1.0f;
+    cfg.no_repeat_ngram_size = 0;
+    cfg.seed = 0;
+    return zq_lm_generate(lm, prompt, prompt_len, &cfg, out_tokens, out_cap, out_len, step_logits, stream);
 }
 
 zq_status zq_lm_destroy(zq_lm* lm) {

@@ -13,7 +13,10 @@
 // Set-up: the first call on each device looks up the array's device address
 // with cudaGetSymbolAddress while that device is current (the array's name is
 // only a host-side stand-in in host code).  That first call may load the
-// library's device code and so should come before any stream capture.
+// library's device code and so should come before any stream capture.  The
+// address is cached for the life of the process: after a cudaDeviceReset() on
+// a device it no longer names the array, and this entry point must not be
+// called on that device again.
 //
 // Sharing: every call on a device uses the same array, which keeps the last
 // call's contents.  The kernels overwrite every scratch byte they read (codes,

@@ -113,7 +113,8 @@ __global__ void __launch_bounds__(SkCfg<kType>::kThreads, 1)
     skinny_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x, int M,
                   int N, int KB, long long T, const float* __restrict__ row_scale,
                   const float* __restrict__ col_scale, const float* __restrict__ bias, float* __restrict__ y,
-                  int* __restrict__ counters, int* __restrict__ partials, uint32_t* __restrict__ err) {
+                  int* __restrict__ counters, int* __restrict__ partials, uint32_t* __restrict__ err,
+                  int wait_extra, unsigned long long peer_limit_ns) {
     using C = SkCfg<kType>;
     constexpr int S = C::kStages;
     constexpr uint32_t kTmemCols = 32;  // two 16-column accumulators
@@ -199,7 +200,7 @@ __global__ void __launch_bounds__(SkCfg<kType>::kThreads, 1)
             }
             // Every copy this thread issued lands before the CTA may exit.
             for (int s = 0; s < S; ++s)
-                if (issued[s]) mbar_wait_bounded(&full[s], last_phase[s], err, kDevErrTimeoutDrain);
+                if (issued[s]) mbar_drain_bounded(&full[s], last_phase[s], err, kDevErrTimeoutDrain);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -240,7 +241,7 @@ __global__ void __launch_bounds__(SkCfg<kType>::kThreads, 1)
             }
             // All MMAs issued by this thread complete before TMEM is freed.
             umma_commit(mma_done);
-            mbar_wait_bounded(mma_done, 0, err, kDevErrTimeoutDrain);
+            mbar_drain_bounded(mma_done, 0, err, kDevErrTimeoutDrain);
         }
     } else if (warp < 6) {
         // Epilogue: warp w reads TMEM lanes (w % 4) * 32 .. +31, i.e. 32
@@ -282,7 +283,11 @@ __global__ void __launch_bounds__(SkCfg<kType>::kThreads, 1)
                 finisher = ticket == g1 - g0;
                 if (finisher) {
                     int fine = 1;
-                    if (lane == 0) fine = wait_count_bounded(published, g1 - g0, err, kDevErrTimeoutPeer) ? 1 : 0;
+                    if (lane == 0)
+                        fine = wait_count_bounded(published, g1 - g0 + wait_extra, err, kDevErrTimeoutPeer,
+                                                  peer_limit_ns)
+                                   ? 1
+                                   : 0;
                     ok = __shfl_sync(0xffffffffu, fine, 0) != 0;
                     if (ok) {
                         (void)ld_acquire_gpu(published);  // orders this lane's loads after the publications
@@ -393,7 +398,7 @@ cudaError_t launch_skinny_t(const SkinnyArgs& a, cudaStream_t stream, bool pdl) 
     if (e != cudaSuccess) return e;
     const int KB = (a.Kp + kSkKBlock - 1) / kSkKBlock;
     const long long T = (long long)skinny_blocks(a.N) * KB;
-    long long G = sm_count();
+    long long G = sm_count(a.reserved_sms);
     if (G > kSkinnyMaxCtas) G = kSkinnyMaxCtas;
     if (G > T) G = T;
     cudaLaunchConfig_t cfg = {};
@@ -407,7 +412,8 @@ cudaError_t launch_skinny_t(const SkinnyArgs& a, cudaStream_t stream, bool pdl) 
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kern, *a.tmap_w, *a.tmap_x, a.M, a.N, KB, T, a.row_scale, a.col_scale, a.bias,
-                              a.y, a.counters, a.partials, a.err);
+                              a.y, a.counters, a.partials, a.err, a.wait_extra,
+                              (unsigned long long)(a.peer_limit_ns ? a.peer_limit_ns : 4000000000ull));
 }
 
 }  // namespace

@@ -4,7 +4,7 @@ loop (``zq_lm_*`` in include/zq.h).
 ``QuantizedLanguageModel.load(path)`` reads the reference's ``.zyqmodel``
 format (src/model/quantized_language_model.cpp:615-642) and keeps weights,
 KV cache and activations on the GPU; ``generate(ids, config)`` is the
-reference's generate (496-547) for greedy decoding (``top_k == 1``).
+reference's generate (496-547) for every GenerationConfig.
 
 ``random_zyqmodel`` builds a ``.zyqmodel`` image of a randomly initialised
 model of a given architecture.  Weight shapes and init follow the reference's
@@ -109,6 +109,13 @@ class QuantizedLanguageModel:
     def type(self):
         return Type(self._info.type)
 
+    def set_persistent(self, on: bool) -> bool:
+        """Greedy decoding as one persistent cooperative kernel (True) or the
+        graph-replayed kernel chain (False, default); returns the old value."""
+        prev = C.c_int()
+        check(lib().zq_lm_set_option(self._h, 1, int(bool(on)), C.byref(prev)))  # ZQ_LM_OPT_PERSISTENT
+        return bool(prev.value)
+
     def quantized_bytes(self):
         return self._info.quantized_bytes
 
@@ -120,13 +127,12 @@ class QuantizedLanguageModel:
         return 0.0 if q == 0 else self.float_reference_bytes() / q
 
     def generate(self, input_ids, config: GenerationConfig = GenerationConfig(), stream=None, return_logits=False):
-        """Greedy generate (config.top_k must be 1).  Returns the prompt plus
-        the new tokens; with ``return_logits`` also the [new, vocab] logits
-        each new token was chosen from."""
-        _validate_generation(config, self._info)
-        if config.top_k != 1:
-            raise _lib.ZQInvalidArgument(
-                "zyron_b200: the device decode loop implements greedy decoding (top_k = 1) only")
+        """QuantizedLanguageModel::generate (496-547) for any GenerationConfig.
+        Returns the prompt plus the new tokens; with ``return_logits`` also
+        the [new, vocab] logits each new token was chosen from.  Greedy
+        decoding (top_k == 1, with or without repetition penalty and n-gram
+        block) runs entirely on the device; other configurations sample each
+        step's logits on the host with the reference's sampler."""
         ids = np.ascontiguousarray(np.asarray(input_ids, dtype=np.int64))
         cap = ids.size + max(config.max_new_tokens, 0) + 1
         out = np.zeros(cap, dtype=np.int64)
@@ -134,27 +140,49 @@ class QuantizedLanguageModel:
         logits = None
         if return_logits:
             logits = np.zeros((max(config.max_new_tokens, 1), self._info.vocab_size), dtype=np.float32)
-        check(lib().zq_lm_generate_greedy(self._h, ids.ctypes.data_as(C.c_void_p) if ids.size else None, ids.size,
-                                          config.max_new_tokens, out.ctypes.data_as(C.c_void_p), cap, C.byref(n),
-                                          None if logits is None else logits.ctypes.data_as(C.c_void_p),
-                                          None if stream is None else C.c_void_p(stream.cuda_stream)))
+        cfg = _config_c(config)
+        check(lib().zq_lm_generate(self._h, ids.ctypes.data_as(C.c_void_p) if ids.size else None, ids.size,
+                                   C.byref(cfg), out.ctypes.data_as(C.c_void_p), cap, C.byref(n),
+                                   None if logits is None else logits.ctypes.data_as(C.c_void_p),
+                                   None if stream is None else C.c_void_p(stream.cuda_stream)))
         toks = [int(t) for t in out[: n.value]]
         if return_logits:
             return toks, logits[: n.value - ids.size]
         return toks
 
 
-def _validate_generation(cfg: GenerationConfig, info):
-    """validate_generation_config (quantized_language_model.cpp:71-80) and the
-    top_k check of generate_batch (517)."""
-    if not (cfg.temperature > 0) or not np.isfinite(cfg.temperature):
-        raise _lib.ZQInvalidArgument("ZYRON QuantizedLanguageModel: invalid temperature")
-    if not (cfg.top_p > 0) or cfg.top_p > 1 or not np.isfinite(cfg.top_p):
-        raise _lib.ZQInvalidArgument("ZYRON QuantizedLanguageModel: invalid top_p")
-    if not (cfg.repetition_penalty >= 1) or not np.isfinite(cfg.repetition_penalty):
-        raise _lib.ZQInvalidArgument("ZYRON QuantizedLanguageModel: invalid repetition_penalty")
-    if cfg.top_k > info.vocab_size:
-        raise _lib.ZQInvalidArgument("ZYRON QuantizedLanguageModel: top_k exceeds vocabulary")
+def _config_c(cfg: GenerationConfig):
+    if cfg.max_new_tokens < 0 or cfg.top_k < 0 or cfg.no_repeat_ngram_size < 0:
+        raise _lib.ZQInvalidArgument("zyron_b200: negative GenerationConfig count")
+    return _lib.GenerationConfigC(int(cfg.max_new_tokens), float(cfg.temperature), int(cfg.top_k), float(cfg.top_p),
+                                  float(cfg.repetition_penalty), int(cfg.no_repeat_ngram_size),
+                                  int(cfg.seed) & 0xFFFFFFFF)
+
+
+class Sampler:
+    """sample_next (quantized_language_model.cpp:82-174) on the host, with the
+    std::mt19937(seed) state that generate keeps across steps (520)."""
+
+    def __init__(self, seed: int = 0):
+        h = C.c_void_p()
+        check(lib().zq_sampler_create(int(seed) & 0xFFFFFFFF, C.byref(h)))
+        self._h = h
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and _lib._lib is not None:
+            _lib._lib.zq_sampler_destroy(h)
+            self._h = None
+
+    def next(self, logits, history, config: GenerationConfig) -> int:
+        row = np.ascontiguousarray(logits, dtype=np.float32).reshape(-1)
+        hist = np.ascontiguousarray(np.asarray(history, dtype=np.int64))
+        tok = C.c_int64()
+        cfg = _config_c(config)
+        check(lib().zq_sample_next(self._h, row.ctypes.data_as(C.c_void_p), row.size,
+                                   hist.ctypes.data_as(C.c_void_p) if hist.size else None, hist.size, C.byref(cfg),
+                                   C.byref(tok)))
+        return int(tok.value)
 
 
 # ---------------------------------------------------------------------------

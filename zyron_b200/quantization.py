@@ -187,6 +187,18 @@ class QuantizedMatrix:
         check(lib().zq_weight_slice_cols(self._h, begin, end, _stream_ptr(stream), C.byref(h)))
         return QuantizedMatrix(h)
 
+    def set_option(self, option: int, value: int) -> int:
+        """zq_weight_set_option on this weight (ZQ_OPT_* of include/zq.h);
+        returns the old value.  Results never depend on the options."""
+        prev = C.c_int()
+        check(lib().zq_weight_set_option(self._h, int(option), int(value), C.byref(prev)))
+        return prev.value
+
+    def set_decode_kernel(self, kind: int) -> int:
+        """Kernel for this weight's matmuls with few rows: 0 automatic,
+        1 tcgen05 decode kernel, 2 dp4a GEMV (ZQ_DECODE_*)."""
+        return self.set_option(1, kind)  # ZQ_OPT_DECODE_KERNEL
+
     @property
     def handle(self):
         return self._h

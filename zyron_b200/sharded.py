@@ -83,17 +83,21 @@ def sharded_matmul(x, weight_shard, n_cols: int, group=None, gather: bool = True
 
 
 class PeerOutputs:
-    """A full [rows, cols] fp32 output on every rank of the process group,
-    each rank holding device pointers to all the others' copies (CUDA IPC
-    handles from ``zq_ipc_export``, opened with ``zq_ipc_import`` while this
-    rank's device is current, so its kernels reach them over NVLink).
+    """Full [rows, cols] fp32 outputs on every rank of the process group, each
+    rank holding device pointers to all the others' copies (CUDA IPC handles
+    from ``zq_ipc_export``, opened with ``zq_ipc_import`` while this rank's
+    device is current, so its kernels reach them over NVLink).
 
     ``sharded_matmul_gathered`` lets the matmul epilogue store every output
     tile straight into all these buffers (``zq_matmul_multi``), so the
     all-gather of column-sharded outputs happens inside the matmul.
+
+    There are ``buffers`` sets of outputs (default 2), used in turn: the
+    output of one call stays intact while the next call runs, and is
+    overwritten by the call after that.
     """
 
-    def __init__(self, rows, cols, device, group=None):
+    def __init__(self, rows, cols, device, group=None, buffers=2):
         import ctypes as C
 
         import torch
@@ -101,30 +105,43 @@ class PeerOutputs:
 
         from . import _lib
 
+        if buffers < 1:
+            raise ValueError("buffers must be >= 1")
         L = _lib.lib()
         self.rows, self.cols = rows, cols
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
-        self.local = torch.empty((rows, cols), dtype=torch.float32, device=device)
-        h = _lib.IpcHandle()
-        _lib.check(L.zq_ipc_export(C.c_void_p(self.local.data_ptr()), C.byref(h)))
-        handles = [None] * self.world
-        dist.all_gather_object(handles, bytes(h), group=group)
-        # import the peers' buffers with this rank's device current, so the
-        # matmul running here may store into them (peer access over NVLink)
+        self.buffers = [torch.empty((rows, cols), dtype=torch.float32, device=device) for _ in range(buffers)]
         self._imported = []
-        with torch.cuda.device(device):
-            for r, raw in enumerate(handles):
-                if r == self.rank:
-                    continue
-                ph = _lib.IpcHandle.from_buffer_copy(raw)
-                p = C.c_void_p()
-                _lib.check(L.zq_ipc_import(C.byref(ph), C.byref(p)))
-                self._imported.append(p.value)
-        # destination order: own buffer first, then the peers
-        self.pointers = [self.local.data_ptr()] + self._imported
+        self._pointers = []
+        for buf in self.buffers:
+            h = _lib.IpcHandle()
+            _lib.check(L.zq_ipc_export(C.c_void_p(buf.data_ptr()), C.byref(h)))
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(h), group=group)
+            # import the peers' buffers with this rank's device current, so the
+            # matmul running here may store into them (peer access over NVLink)
+            peers = []
+            with torch.cuda.device(device):
+                for r, raw in enumerate(handles):
+                    if r == self.rank:
+                        continue
+                    ph = _lib.IpcHandle.from_buffer_copy(raw)
+                    p = C.c_void_p()
+                    _lib.check(L.zq_ipc_import(C.byref(ph), C.byref(p)))
+                    peers.append(p.value)
+            self._imported += peers
+            # destination order: own buffer first, then the peers
+            self._pointers.append([buf.data_ptr()] + peers)
+        self.turn = 0  # the buffer set the next call writes
+        self.local = self.buffers[0]  # the last call's output on this rank
         self._flag = torch.zeros(1, dtype=torch.float32, device=device)
+
+    @property
+    def pointers(self):
+        """Destinations of the next call: this rank's buffer, then the peers'."""
+        return self._pointers[self.turn]
 
     def close(self):
         from . import _lib
@@ -132,11 +149,11 @@ class PeerOutputs:
         for p in self._imported:
             _lib.lib().zq_ipc_close(p)
         self._imported = []
+        self._pointers = []
 
     def barrier(self):
-        """Stream-ordered completion barrier: returns (on the stream) once every
-        rank's matmul -- and so every peer store into this rank's output --
-        has finished."""
+        """Stream-ordered barrier: completes (on the stream) once every rank's
+        stream has reached it."""
         import torch.distributed as dist
 
         dist.all_reduce(self._flag, group=self.group)
@@ -144,9 +161,20 @@ class PeerOutputs:
 
 def sharded_matmul_gathered(x, weight_shard, peer_out: PeerOutputs, bias_shard=None, workspace=None, stream=None):
     """y = matmul(x, W) with W column-sharded over the group; every rank ends
-    with the full [M, N] output in ``peer_out.local``.  The matmul epilogue
-    writes each tile to all ranks' outputs over NVLink; no separate
-    collective moves the data."""
+    with the full [M, N] output.  The matmul epilogue writes each tile to all
+    ranks' outputs over NVLink; no separate collective moves the data.
+
+    Ordering, on the stream of the call (all ranks must make the same calls
+    in the same order):
+      - a barrier before the matmul: no rank stores into a peer's buffer
+        until every rank's stream has reached this call, so work the peers
+        queued before it (reads of older outputs) has finished;
+      - a barrier after it: every rank's stores into this rank's output have
+        landed when the returned tensor is read on the stream.
+    The returned tensor is one of ``peer_out.buffers``, reused in turn: it
+    holds this call's result until this rank issues the call after next
+    (with the default two buffers).  Reads of it on another stream must be
+    ordered with this one."""
     import ctypes as C
 
     import torch
@@ -163,12 +191,18 @@ def sharded_matmul_gathered(x, weight_shard, peer_out: PeerOutputs, bias_shard=N
     m = x.shape[0]
     s = stream if stream is not None else torch.cuda.current_stream(x.device)
     ws, ws_bytes = workspace if workspace is not None else get_workspace(weight_shard, m, x.device, s.cuda_stream)
-    ptrs = (C.c_void_p * len(peer_out.pointers))(*peer_out.pointers)
-    _lib.check(L.zq_matmul_multi(weight_shard.handle, C.c_void_p(x.data_ptr()), m,
-                                 None if bias_shard is None else C.c_void_p(bias_shard.data_ptr()),
-                                 ptrs, len(peer_out.pointers), peer_out.cols, b, C.c_void_p(ws), ws_bytes,
-                                 C.c_void_p(s.cuda_stream)))
-    peer_out.barrier()
+    turn = peer_out.turn
+    dst = peer_out.pointers
+    ptrs = (C.c_void_p * len(dst))(*dst)
+    with torch.cuda.stream(s):
+        peer_out.barrier()
+        _lib.check(L.zq_matmul_multi(weight_shard.handle, C.c_void_p(x.data_ptr()), m,
+                                     None if bias_shard is None else C.c_void_p(bias_shard.data_ptr()),
+                                     ptrs, len(dst), peer_out.cols, b, C.c_void_p(ws), ws_bytes,
+                                     C.c_void_p(s.cuda_stream)))
+        peer_out.barrier()
+    peer_out.turn = (turn + 1) % len(peer_out.buffers)
+    peer_out.local = peer_out.buffers[turn]
     return peer_out.local
 
 

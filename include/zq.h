@@ -368,6 +368,23 @@ zq_status zq_lm_generate(zq_lm* lm, const int64_t* prompt, size_t prompt_len, co
 
 zq_status zq_lm_destroy(zq_lm* lm);
 
+/* ---- checkpoint conversion --------------------------------------------- */
+
+/* zyron_quantize (tools/zyron_quantize.cpp:33-48): a .zyron training
+ * checkpoint (src/model/checkpoint.cpp:145-232; versions 1-4) in memory to a
+ * .zyqmodel image (QuantizedLanguageModel(model, type) then save,
+ * quantized_language_model.cpp:178-269, 615-625), byte-identical to the
+ * reference tool's output.  The checkpoint is validated with the reference's
+ * checks, order and messages (format, config, optimizer and scheduler
+ * hyper-parameters, parameter and moment shapes, tokenizer data); every
+ * weight matrix is quantized on the current device.  *out receives a buffer
+ * of *out_len bytes to release with zq_free_buffer; *compression_ratio (may
+ * be NULL) QuantizedLanguageModel::compression_ratio() of the result.
+ * Synchronous. */
+zq_status zq_quantize_checkpoint(const void* checkpoint, size_t len, int type, void* stream, void** out,
+                                 size_t* out_len, double* compression_ratio);
+void zq_free_buffer(void* p);
+
 /* ---- token sampling (host) --------------------------------------------- */
 
 /* The state of sample_next's random draws: std::mt19937(seed), as created

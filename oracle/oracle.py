@@ -177,6 +177,8 @@ def ref():
         R.ref_qlm_load.argtypes = [C.c_char_p, C.POINTER(vp)]
         R.ref_qlm_forward.argtypes = [vp, vp, sz, vp]
         R.ref_qlm_generate_greedy.argtypes = [vp, vp, sz, sz, vp, C.POINTER(sz)]
+        R.ref_checkpoint_save.argtypes = [C.c_char_p, sz, sz, sz, sz, sz, sz, sz, C.c_int, C.c_int, C.c_int,
+                                          C.c_uint32]
         R.ref_qlm_generate.argtypes = [vp, vp, sz, sz, C.c_float, sz, C.c_float, C.c_float, sz, C.c_uint32, vp,
                                        C.POINTER(sz)]
         _ref = R
@@ -315,3 +317,25 @@ class RefQlm:
         _chk(ref().ref_qlm_generate(self.h, _vp(a), a.size, max_new_tokens, temperature, top_k, top_p,
                                     repetition_penalty, no_repeat_ngram_size, seed, _vp(out), C.byref(n)))
         return [int(t) for t in out[: n.value]]
+
+
+def ref_tool_path():
+    """The reference's zyron_quantize executable, built by oracle/Makefile."""
+    return os.path.join(HERE, "_ref", "zyron_quantize")
+
+
+def ref_checkpoint_save(path, vocab, hidden, layers, heads, kv_heads, ffn, max_seq, use_rope=True,
+                        use_rms_norm=True, tie=True, seed=0):
+    """A reference .zyron checkpoint with non-trivial parameter values
+    (ref_harness.cpp: ref_checkpoint_save)."""
+    _chk(ref().ref_checkpoint_save(str(path).encode(), vocab, hidden, layers, heads, kv_heads, ffn, max_seq,
+                                   int(use_rope), int(use_rms_norm), int(tie), seed))
+
+
+def ref_quantize_tool(checkpoint, output, bits=8):
+    """Run the reference's zyron_quantize: (exit code, stdout, stderr)."""
+    import subprocess
+
+    p = subprocess.run([ref_tool_path(), "--checkpoint", str(checkpoint), "--output", str(output), "--bits",
+                        str(bits)], capture_output=True, text=True, timeout=600)
+    return p.returncode, p.stdout, p.stderr

@@ -14,6 +14,10 @@
 //   QuantizedLanguageModel   (include/zyron/model/quantized_language_model.hpp)
 //   runtime::set_num_threads / num_threads (include/zyron/core/runtime.hpp:16-17)
 #include "zyron/core/runtime.hpp"
+#include "zyron/model/checkpoint.hpp"
+#include "zyron/tokenizer/bpe.hpp"
+#include "zyron/training/adamw.hpp"
+#include "zyron/training/scheduler.hpp"
 #include "zyron/core/tensor.hpp"
 #include "zyron/model/language_model.hpp"
 #include "zyron/model/quantized_language_model.hpp"
@@ -25,6 +29,7 @@
 #include <cstring>
 #include <exception>
 #include <memory>
+#include <random>
 #include <sstream>
 #include <string>
 #include <vector>
@@ -247,6 +252,47 @@ int ref_qlm_generate(const void* h, const std::size_t* ids, std::size_t T, std::
         auto res = static_cast<const RefQlm*>(h)->m->generate(v, gc);
         std::memcpy(out, res.data(), res.size() * sizeof(std::size_t));
         *out_len = res.size();
+    });
+}
+
+// Checkpoint::save (src/model/checkpoint.cpp:106-143) of LanguageModel(config,
+// seed) whose parameters and optimizer moments are overwritten with
+// uniform(-0.5, 0.5) draws (std::mt19937(seed + 1000 + i) for tensor i, so
+// no two tensors are alike), an AdamW(lr 3e-4) and a warmup-cosine scheduler
+// (3e-4, 10, 100, 1e-5), and a BPE tokenizer trained to 270 tokens on a
+// fixed text.  Written as version 4, the format the reference saves.
+int ref_checkpoint_save(const char* path, std::size_t vocab, std::size_t hidden, std::size_t layers,
+                        std::size_t heads, std::size_t kv_heads, std::size_t ffn, std::size_t max_seq, int use_rope,
+                        int use_rms_norm, int tie, std::uint32_t seed) {
+    return guarded([&] {
+        auto cfg = zyron::transformer::tiny(vocab);
+        cfg.vocab_size = vocab;
+        cfg.hidden_size = hidden;
+        cfg.num_layers = layers;
+        cfg.num_heads = heads;
+        cfg.num_kv_heads = kv_heads;
+        cfg.intermediate_size = ffn;
+        cfg.max_sequence_length = max_seq;
+        cfg.use_rope = use_rope != 0;
+        cfg.use_rms_norm = use_rms_norm != 0;
+        cfg.tie_word_embeddings = tie != 0;
+        cfg.dropout = 0.0f;
+        cfg.validate();
+        zyron::model::LanguageModel lm(cfg, seed);
+        auto params = lm.parameters();
+        for (std::size_t i = 0; i < params.size(); ++i) {
+            std::mt19937 rng(seed + 1000u + static_cast<std::uint32_t>(i));
+            std::uniform_real_distribution<float> d(-0.5f, 0.5f);
+            auto& t = params[i]->value();
+            for (std::size_t k = 0; k < t.size(); ++k) t[k] = d(rng);
+        }
+        zyron::training::AdamW opt(params, 3e-4f, 0.9f, 0.95f, 1e-8f, 0.1f);
+        zyron::training::WarmupCosineScheduler sched(3e-4f, 10, 100, 1e-5f);
+        zyron::tokenizer::BPE tok;
+        tok.train_text("the quick brown fox jumps over the lazy dog; the lazy dog sleeps. "
+                       "quantized models run fast on tensor cores, the quick fox said.",
+                       270);
+        zyron::model::Checkpoint::save(path, lm, opt, sched, tok, 7);
     });
 }
 

@@ -172,27 +172,46 @@ def test_penalized_greedy_all_blocked_falls_back(cuda, tmp_path):
         _check_against_reference(lm, ref, [1, 2, 3], 20, cfg)
 
 
-def test_baseline_lm_matches_reference(cuda, tmp_path):
-    """The benchmark's model -- 768 wide, 12 layers, 12 heads, 4 KV heads, FFN
-    3072, vocabulary 16384, context 576 -- built by the reference's own
-    LanguageModel(config, seed) and QuantizedLanguageModel(model, Int8)
-    (quantized_language_model.cpp:178-269), with a 64-token uniform prompt:
-    the device's greedy tokens equal the reference's over 16 steps, and its
-    logits at the first, middle and last step are within LOGIT_RTOL of the
-    reference's forward()."""
+# The benchmark's model (768 wide, 12 heads, 4 KV heads, FFN 3072, vocabulary
+# 16384, context 576) built by the reference's own LanguageModel(config, seed)
+# and QuantizedLanguageModel(model, Int8) (quantized_language_model.cpp:
+# 178-269), with a 64-token uniform prompt.
+#
+# With 1-2 layers the device's logits equal the reference's to the last ulp or
+# two: the quantized matmuls are exact and the fp32 parts differ only in their
+# summation order.  Deeper models occasionally meet an activation that sits on
+# a rounding boundary of the per-row quantizer, where a 1-ulp difference flips
+# its int8 code by one; from there on the logits move by up to about 1e-2 of
+# their span (measured: 4.1e-3 after 4 layers, 7.3e-3 after 12), while most
+# logits stay much closer.
+FLIP_RTOL = 2e-2   # max |difference| / span, 12 layers
+MEAN_RTOL = 2e-3   # mean |difference| / span, 12 layers
+ULP_RTOL = 1e-5    # max |difference| / span, 2 layers
+
+
+def _baseline_model(layers, tmp_path):
     import os as _os
 
     from oracle import oracle as O
-    from zyron_b200.qlm import GenerationConfig, QuantizedLanguageModel
+    from zyron_b200.qlm import QuantizedLanguageModel
 
     if not O.ref_available():
         pytest.skip("compiled reference not present")
     O.ref_set_threads(_os.cpu_count() or 1)
-    ref = O.RefQlm.create(16384, 768, 12, 12, 4, 3072, 576, seed=0)
-    p = tmp_path / "cfg4.zyqmodel"
+    ref = O.RefQlm.create(16384, 768, layers, 12, 4, 3072, 576, seed=0)
+    p = tmp_path / f"baseline_{layers}.zyqmodel"
     ref.save(p)
-    lm = QuantizedLanguageModel.load(p)
     prompt = [int(t) for t in np.random.default_rng(0).integers(0, 16384, 64)]
+    return ref, QuantizedLanguageModel.load(p), prompt
+
+
+def test_baseline_lm_matches_reference(cuda, tmp_path):
+    """12 layers: the device's greedy tokens equal the reference's over 16
+    steps; logits at the first, middle and last step within FLIP_RTOL (max) and
+    MEAN_RTOL (mean) of the reference's forward()."""
+    from zyron_b200.qlm import GenerationConfig
+
+    ref, lm, prompt = _baseline_model(12, tmp_path)
     n_new = 16
     want = ref.generate(prompt, n_new, top_k=1)
     toks, logits = lm.generate(prompt, GenerationConfig(max_new_tokens=n_new, top_k=1), return_logits=True)
@@ -201,6 +220,23 @@ def test_baseline_lm_matches_reference(cuda, tmp_path):
     for g in (0, n_new // 2, n_new - 1):
         r = ref.forward(want[: len(prompt) + g])[-1]
         span = float(r.max() - r.min())
-        err = float(np.abs(logits[g] - r).max())
-        assert err <= LOGIT_RTOL * span, f"step {g}: max logit error {err:.3g} (range {span:.3g})"
+        d = np.abs(logits[g] - r)
+        assert d.max() <= FLIP_RTOL * span, f"step {g}: max logit error {d.max():.3g} (range {span:.3g})"
+        assert d.mean() <= MEAN_RTOL * span, f"step {g}: mean logit error {d.mean():.3g} (range {span:.3g})"
     assert lm.generate(prompt, GenerationConfig(max_new_tokens=n_new, top_k=1)) == want
+
+
+def test_baseline_width_two_layers_logits_to_the_ulp(cuda, tmp_path):
+    """2 layers of the same width: no activation code flips, so every logit of
+    4 greedy steps equals the reference's within ULP_RTOL of the span."""
+    from zyron_b200.qlm import GenerationConfig
+
+    ref, lm, prompt = _baseline_model(2, tmp_path)
+    want = ref.generate(prompt, 4, top_k=1)
+    toks, logits = lm.generate(prompt, GenerationConfig(max_new_tokens=4, top_k=1), return_logits=True)
+    assert toks == want
+    for g in range(4):
+        r = ref.forward(want[: len(prompt) + g])[-1]
+        span = float(r.max() - r.min())
+        err = float(np.abs(logits[g] - r).max())
+        assert err <= ULP_RTOL * span, f"step {g}: max logit error {err:.3g} (range {span:.3g})"

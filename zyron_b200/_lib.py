@@ -119,6 +119,8 @@ SIGNATURES = {
     "zq_lm_generate_greedy": (st, [vp, vp, sz, sz, vp, sz, C.POINTER(sz), vp, vp]),
     "zq_lm_generate": (st, [vp, vp, sz, vp, vp, sz, C.POINTER(sz), vp, vp]),
     "zq_lm_destroy": (st, [vp]),
+    "zq_quantize_checkpoint": (st, [vp, sz, C.c_int, vp, C.POINTER(vp), C.POINTER(sz), C.POINTER(C.c_double)]),
+    "zq_free_buffer": (None, [vp]),
     "zq_sampler_create": (st, [C.c_uint32, C.POINTER(vp)]),
     "zq_sampler_destroy": (st, [vp]),
     "zq_sample_next": (st, [vp, vp, sz, vp, sz, vp, C.POINTER(C.c_int64)]),

@@ -25,11 +25,12 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 CU_SOURCES = ["zq_api.cu", "zq_quant.cu", "zq_gemv.cu", "zq_gemm_sm100.cu", "zq_skinny_sm100.cu", "zq_noalloc.cu",
               "zq_lm.cu", "zq_sharded.cu"]
 CU_HEADERS = ["zq_common.cuh", "zq_dot.cuh", "zq_tcgen05.cuh", "zq_kernels.h", "zq_internal.h"]
-# Host-only C++ of the library.  zq_sample.cpp restates the reference's token
-# sampler, whose std::sort order and std::mt19937 draws come from the C++
-# standard library, so it is built by g++ with the reference's own Release
-# flags (-std=c++20 -O3 -DNDEBUG).
-HOST_SOURCES = ["zq_sample.cpp"]
+# Host-only C++ of the library, built by g++ with the reference's own Release
+# flags (-std=c++20 -O3 -DNDEBUG): zq_sample.cpp restates the reference's
+# token sampler, whose std::sort order and std::mt19937 draws come from the
+# C++ standard library, and zq_checkpoint.cpp writes the sinusoidal position
+# table with the same libm calls as the reference.
+HOST_SOURCES = ["zq_sample.cpp", "zq_checkpoint.cpp"]
 HOST_FLAGS = ["-std=c++20", "-O3", "-DNDEBUG", "-fPIC"]
 CPP_SOURCES = ["src/quantization.cpp", "src/quantized_linear.cpp", "src/tensor.cpp"]
 

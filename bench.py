@@ -379,6 +379,21 @@ def run_ours(args, rank, world, local_rank):
     }
     if world > 1:
         line["e2e"]["value"] = ops(M, N, K) / (e2e_ms * 1e-3) / 1e12
+        # What the gathered step is made of: every rank's GEMM on its own
+        # column shard, and the (world-1)/world of the fp32 output each GPU
+        # receives over NVLink from the peers' epilogues.
+        recv = (world - 1) / world * M * N * 4
+        link_gbs = 770.0  # measured peer-copy bandwidth per direction on this pool
+        line["multi_gpu"] = {
+            "gemm_only_ms_per_rank": gemm_ms, "quantize_ms_per_rank": quant_ms,
+            "gemm_only_tops_per_rank": gemm_tops, "gemm_only_tops_all_ranks": ops(M, N, K) / (gemm_ms * 1e-3) / 1e12,
+            "gather_ms_beyond_compute": max(ms - gemm_ms - quant_ms, 0.0),
+            "nvlink_bytes_received_per_gpu": recv, "nvlink_gbs_received_per_gpu": recv / (ms * 1e-3) / 1e9,
+            "link_floor_ms": recv / (link_gbs * 1e9) * 1e3, "frac_of_link_floor": recv / (link_gbs * 1e9) / (ms * 1e-3),
+            "link_floor_basis": "770 GB/s per direction per GPU (measured peer copy)",
+            "barriers_per_step": 2}
+    if world == 1 and not args.no_secondary:
+        line["secondary"] = secondary_block(args)
     print(json.dumps(line), flush=True)
 
 
@@ -393,10 +408,13 @@ def hbm_peak():
         return 6650.0, "fallback: 6.65 TB/s (earlier pool measurement)"
 
 
-def run_gemv_workload(args):
-    """Decode GEMV M in {1, 8}, K=4096, N=11008, INT8 and INT4 weights ~N(0,0.02),
-    x ~N(0,1).  Weight copies rotate so the streamed bytes exceed 2 x L2;
-    launches are replayed from a CUDA graph (device back to back)."""
+def decode_cases(args, kinds=(("default", 0),), min_region_s=0.25):
+    """Decode GEMV M in {1, 8}, K=4096, N=11008, INT8 and INT4 weights
+    ~N(0,0.02), x ~N(0,1).  For each case and decode kernel: the matmul kernel
+    alone on precomputed codes (zq_matmul_codes) and the whole zq_matmul call.
+    Weight copies rotate so the streamed bytes exceed 2 x L2; launches are
+    replayed from a CUDA graph (device back to back), for at least
+    `min_region_s` per measurement, with the SM clocks sampled meanwhile."""
     import torch
 
     import zyron_b200 as zb
@@ -406,26 +424,9 @@ def run_gemv_workload(args):
     dev = torch.device("cuda:0")
     K, N = 4096, 11008
     peak, peak_src = hbm_peak()
-    if args.once:
-        # profiling aid: three eager zq_matmul calls per case and decode
-        # kernel, in the order int8 M=1, M=8, int4 M=1, M=8, each with the
-        # tensor-core kernel first, then the dp4a GEMV; no timing
-        g = torch.Generator(device=dev)
-        g.manual_seed(2)
-        for qt in (1, 2):
-            W = zb.quantize(torch.randn((K, N), generator=g, device=dev).mul_(0.02), zb.Type(qt))
-            for M in (1, 8):
-                x = torch.randn((M, K), generator=g, device=dev)
-                for kind in (1, 2):
-                    W.set_decode_kernel(kind)
-                    for _ in range(3):
-                        y = zb.matmul(x, W)
-                W.set_decode_kernel(0)
-        torch.cuda.synchronize()
-        print(json.dumps({"workload": "decode_gemv_K4096_N11008", "once": True, "checksum": float(y.abs().sum())}))
-        return
     s = torch.cuda.Stream()
     cases = {}
+    launches = 0
     for qt in (1, 2):
         payload = K * N if qt == 1 else K * N // 2
         copies = max(3, int(2 * 126e6 / payload) + 2)
@@ -461,7 +462,7 @@ def run_gemv_workload(args):
                     _lib.check(L.zq_matmul(Ws[i % copies].handle, C.c_void_p(x.data_ptr()), M, None,
                                            C.c_void_p(y.data_ptr()), C.c_void_p(wp), wsb, sp))
 
-                for kname, kind in (("tensor_core", 1), ("cuda_core", 2)):
+                for kname, kind in kinds:
                     for W in Ws:
                         W.set_decode_kernel(kind)
                     res[kname] = {}
@@ -477,26 +478,72 @@ def run_gemv_workload(args):
                         for _ in range(args.warmup):
                             graph.replay()
                         s.synchronize()
+                        # replays for about min_region_s of device time
                         a, b = torch.cuda.Event(True), torch.cuda.Event(True)
                         a.record(s)
-                        for _ in range(args.steps):
-                            graph.replay()
+                        graph.replay()
                         b.record(s)
                         s.synchronize()
-                        us = a.elapsed_time(b) / (args.steps * reps) * 1e3
+                        n_rep = max(args.steps, int(min_region_s * 1e3 / max(a.elapsed_time(b), 1e-3)) + 1)
+                        sampler = ClockSampler(0)
+                        with sampler:
+                            a.record(s)
+                            for _ in range(n_rep):
+                                graph.replay()
+                            b.record(s)
+                            s.synchronize()
+                        launches += n_rep * reps * (1 if name == "kernel" else 2)
+                        us = a.elapsed_time(b) / (n_rep * reps) * 1e3
                         byts = payload + 4 * N + M * Kp + 4 * M * N
-                        res[kname][name] = {"us": us, "GBs": byts / us / 1e3, "frac_of_hbm": byts / us / 1e3 / peak}
+                        res[kname][name] = {"us": us, "GBs": byts / us / 1e3, "frac_of_hbm": byts / us / 1e3 / peak,
+                                            "bytes": byts, "clocks": sampler.summary()}
                         del graph
                 for W in Ws:
                     W.set_decode_kernel(0)
             cases[f"{'int8' if qt == 1 else 'int4'}_M{M}"] = res
+        del Ws
+        torch.cuda.empty_cache()
+    return cases, peak, peak_src, launches
+
+
+def run_gemv_workload(args):
+    """Decode GEMV M in {1, 8}, K=4096, N=11008 through both decode kernels
+    (see decode_cases), the host entry point, and the reference's CPU
+    matmul."""
+    import torch
+
+    import zyron_b200 as zb
+    from zyron_b200 import _lib
+
+    L = _lib.lib()
+    dev = torch.device("cuda:0")
+    K, N = 4096, 11008
+    if args.once:
+        # profiling aid: three eager zq_matmul calls per case and decode
+        # kernel, in the order int8 M=1, M=8, int4 M=1, M=8, each with the
+        # tensor-core kernel first, then the dp4a GEMV; no timing
+        g = torch.Generator(device=dev)
+        g.manual_seed(2)
+        for qt in (1, 2):
+            W = zb.quantize(torch.randn((K, N), generator=g, device=dev).mul_(0.02), zb.Type(qt))
+            for M in (1, 8):
+                x = torch.randn((M, K), generator=g, device=dev)
+                for kind in (1, 2):
+                    W.set_decode_kernel(kind)
+                    for _ in range(3):
+                        y = zb.matmul(x, W)
+                W.set_decode_kernel(0)
+        torch.cuda.synchronize()
+        print(json.dumps({"workload": "decode_gemv_K4096_N11008", "once": True, "checksum": float(y.abs().sum())}))
+        return
+    cases, peak, peak_src, launches = decode_cases(args, kinds=(("tensor_core", 1), ("cuda_core", 2)),
+                                                   min_region_s=0.05)
     # end to end through the host entry point (M=1, INT8): pinned host x in, host y out
     W0 = zb.quantize(torch.randn((K, N), device=dev).mul_(0.02), zb.Type.Int8)
     xh = torch.randn((1, K)).pin_memory()
     yh = torch.empty((1, N)).pin_memory()
     for _ in range(args.warmup):
         _lib.check(L.zq_matmul_host(W0.handle, C.c_void_p(xh.data_ptr()), 1, None, C.c_void_p(yh.data_ptr()), None))
-    import time
     t0 = time.perf_counter()
     for _ in range(args.steps * 10):
         _lib.check(L.zq_matmul_host(W0.handle, C.c_void_p(xh.data_ptr()), 1, None, C.c_void_p(yh.data_ptr()), None))
@@ -520,10 +567,11 @@ def run_gemv_workload(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": "decode_gemv_K4096_N11008", "M": [1, 8], "types": ["int8", "int4"],
                        "l2": "weights rotate over enough copies to stream > 2 x L2 per pass"},
+            "gpu_launches": launches, "clocks": head["clocks"],
             "roofline": {"bound": "hbm", "kernel": "gemv_kernel<int8, M=1> (dp4a, warp per column)",
                          "achieved": head["GBs"], "peak": peak,
                          "unit": "GB/s", "frac": head["frac_of_hbm"], "peak_source": peak_src,
-                         "bytes_per_launch": K * N + 4 * N + 16 * ((K + 15) // 16) + 4 * N},
+                         "bytes_per_launch": head["bytes"]},
             "cases": cases,
             "e2e": {"value": (K * N) / e2e_us / 1e3, "unit": "GB/s", "us_per_step": e2e_us,
                     "h2d_bytes_per_step": 4 * K, "d2h_bytes_per_step": 4 * N, "api": "zq_matmul_host"},
@@ -687,14 +735,16 @@ def run_small_workload(args):
     print(json.dumps(line), flush=True)
 
 
-def run_qlm_workload(args):
-    """QuantizedLanguageModel decode: d_model 768, 12 layers, 12 heads, 4 KV
-    heads, GELU FFN 3072, tied vocab 16384, INT8, batch 1, 64-token prompt,
-    512 greedy tokens (random init of that architecture)."""
-    import tempfile
-    import time
+QLM_WORKLOAD = "qlm_decode_d768_L12_H12_KV4_F3072_V16384_prompt64_new512"
 
-    import numpy as np
+
+def qlm_measure(args, cpu_baseline=True):
+    """QuantizedLanguageModel decode: d_model 768, 12 layers, 12 heads, 4 KV
+    heads, GELU FFN 3072, tied vocab 16384, INT8, batch 1, 64-token uniform
+    prompt, 512 greedy tokens.  Per-token time = (generate(512) -
+    generate(1)) / 511, best of 3, with the SM clocks sampled meanwhile."""
+    import tempfile
+
     import torch
 
     from zyron_b200.qlm import Config, GenerationConfig, QuantizedLanguageModel, random_zyqmodel
@@ -704,11 +754,6 @@ def run_qlm_workload(args):
     img = random_zyqmodel(cfg, seed=0)
     lm = QuantizedLanguageModel.load_bytes(img)
     prompt = np.random.default_rng(0).integers(0, 16384, 64).tolist()
-    if args.once:
-        # profiling aid: one 4-token generation after the 64-token prompt
-        toks = lm.generate(prompt, GenerationConfig(max_new_tokens=4, top_k=1))
-        print(json.dumps({"workload": "qlm_decode_d768_L12", "once": True, "tokens": list(map(int, toks))}))
-        return
     lm.generate(prompt, GenerationConfig(max_new_tokens=512, top_k=1))  # builds the graphs
     s = torch.cuda.Stream()
 
@@ -726,13 +771,15 @@ def run_qlm_workload(args):
             best = t if best is None else min(best, t)
         return best
 
-    t1 = timed(1)
-    t512 = timed(512)
+    sampler = ClockSampler(0)
+    with sampler:
+        t1 = timed(1)
+        t512 = timed(512)
     per_tok = (t512 - t1) / 511
     weight_bytes = 12 * (768 * (768 + 256 + 256 + 768 + 3072) + 3072 * 768) + 768 * 16384
     peak, peak_src = hbm_peak()
     cpu = None
-    if not args.skip_cpu_baseline:
+    if cpu_baseline:
         from oracle import oracle as O
 
         if O.ref_available():
@@ -754,18 +801,60 @@ def run_qlm_workload(args):
                     cpu = {"value": 1.0 / tc, "unit": "tok/s", "cores": threads, "kind": "reference",
                            "sample": "2 greedy tokens after the 64-token prompt (the reference recomputes the whole "
                                      "prefix for every token; later tokens cost more)"}
-    line = {"metric": "quantized-LM decode tok/s (QuantizedLanguageModel::generate, greedy)", "value": 1.0 / per_tok,
-            "unit": "tok/s", "n_gpus": 1, "steps": 512, "warmup": args.warmup, "ms_per_step": per_tok * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": "qlm_decode_d768_L12_H12_KV4_F3072_V16384_prompt64_new512",
-                       "weights": "random init of the architecture (numpy), INT8"},
+    return {"tok_s": 1.0 / per_tok, "ms_per_token": per_tok * 1e3, "generate_512_tok_s": 512.0 / t512,
+            "prefill_ms": t1 * 1e3, "clocks": sampler.summary(),
             "roofline": {"bound": "hbm", "achieved": weight_bytes / per_tok / 1e9, "peak": peak, "unit": "GB/s",
                          "frac": weight_bytes / per_tok / 1e9 / peak, "peak_source": peak_src,
                          "note": "weight bytes per token / time per token; the 88 MB of weights fit in L2"},
-            "e2e": {"value": 512.0 / t512, "unit": "tok/s", "note": "whole generate call incl. 64-token prefill",
-                    "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "prefill_ms": t1 * 1e3, "cpu_baseline": cpu}
+            "launches_per_token": 2 + 5 * 12, "cpu_baseline": cpu}
+
+
+def run_qlm_workload(args):
+    """The LM decode workload on its own line (see qlm_measure)."""
+    from zyron_b200.qlm import Config, GenerationConfig, QuantizedLanguageModel, random_zyqmodel
+
+    if args.once:
+        # profiling aid: one 4-token generation after the 64-token prompt
+        cfg = Config(vocab_size=16384, hidden_size=768, num_layers=12, num_heads=12, num_kv_heads=4,
+                     intermediate_size=3072, max_sequence_length=576)
+        lm = QuantizedLanguageModel.load_bytes(random_zyqmodel(cfg, seed=0))
+        prompt = np.random.default_rng(0).integers(0, 16384, 64).tolist()
+        toks = lm.generate(prompt, GenerationConfig(max_new_tokens=4, top_k=1))
+        print(json.dumps({"workload": "qlm_decode_d768_L12", "once": True, "tokens": list(map(int, toks))}))
+        return
+    r = qlm_measure(args, cpu_baseline=not args.skip_cpu_baseline)
+    line = {"metric": "quantized-LM decode tok/s (QuantizedLanguageModel::generate, greedy)", "value": r["tok_s"],
+            "unit": "tok/s", "n_gpus": 1, "steps": 512, "warmup": args.warmup, "ms_per_step": r["ms_per_token"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": QLM_WORKLOAD, "weights": "random init of the architecture, INT8"},
+            "clocks": r["clocks"], "roofline": r["roofline"],
+            "e2e": {"value": r["generate_512_tok_s"], "unit": "tok/s",
+                    "note": "whole generate call incl. 64-token prefill", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "prefill_ms": r["prefill_ms"], "cpu_baseline": r["cpu_baseline"]}
     print(json.dumps(line), flush=True)
+
+
+def secondary_block(args):
+    """The decode GEMV (weight GB/s) and LM decode (tok/s) figures of the
+    metric, measured after the headline in the same process, each with its
+    own clock record."""
+    out = {}
+    try:
+        cases, peak, peak_src, launches = decode_cases(args)
+        out["decode_gemv_K4096_N11008"] = {
+            "unit": "GB/s", "peak": peak, "peak_source": peak_src,
+            "dispatch": "zq_matmul default: dp4a GEMV with the quantizer fused for M <= 4, tcgen05 decode kernel "
+                        "for 5-16 rows",
+            "bytes": "payload + 4N scales + M*Kp codes + 4MN outputs per launch; weights rotate over > 2 x L2",
+            "cases": {k: v["default"] for k, v in cases.items()}, "gpu_launches": launches}
+    except Exception as exc:  # report, never lose the headline
+        out["decode_gemv_K4096_N11008"] = {"error": repr(exc)}
+    try:
+        out[QLM_WORKLOAD] = qlm_measure(args, cpu_baseline=not args.skip_cpu_baseline)
+    except Exception as exc:
+        out[QLM_WORKLOAD] = {"error": repr(exc)}
+    return out
 
 
 def main():
@@ -779,6 +868,8 @@ def main():
                     help="prefill (default line), gemv (decode GEMV), small (64x512x512 INT8 and "
                          "128x2048x2048 INT4) or qlm (LM decode)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling runs)")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the decode GEMV and LM decode figures after the headline (profiling runs)")
     ap.add_argument("--once", action="store_true",
                     help="gemv / small / qlm workloads: a few untimed calls of the kernels (for ncu captures)")
     ap.add_argument("--shape", type=lambda v: tuple(int(t) for t in v.split(",")),

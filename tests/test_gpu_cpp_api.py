@@ -25,3 +25,23 @@ def test_cpp_drop_in(cuda, tmp_path):
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "PASS" in r.stdout
+
+
+@pytest.mark.parametrize("program,banner", [("test_phase5", "ZYRON Phase 5 tests: PASS"),
+                                            ("test_final", "ZYRON final tests: PASS")])
+def test_reference_tests_over_drop_in(cuda, program, banner):
+    """The reference's own test programs (tests/test_phase5.cpp: quantize,
+    matmul, QuantizedLinear, QuantizedLanguageModel; tests/test_final.cpp:
+    .zyqmodel round trip, quantized batch generation), compiled unmodified
+    with the reference's QuantizedLanguageModel and the rest of its sources,
+    but with src/quantization replaced by the C++ drop-in (oracle/Makefile,
+    target dropin): every quantized matmul they run goes through
+    libzyron_b200.so on the GPU."""
+    exe = os.path.join(ROOT, "oracle", "_ref", "dropin", program)
+    if not os.path.exists(exe):
+        pytest.skip("oracle/_ref/dropin not built (needs the reference sources)")
+    ldd = subprocess.run(["ldd", exe], capture_output=True, text=True).stdout
+    assert os.path.join("zyron_b200", "libzyron_b200.so") in ldd, ldd
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert banner in r.stdout

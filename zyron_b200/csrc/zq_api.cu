@@ -653,7 +653,7 @@ zq_status matmul_in_workspace_out(const zq_weight* w, const float* x, size_t m, 
         a.x = x;
         a.K = (int)w->K;
         a.reserved_sms = w->opt_reserved_sms.load(std::memory_order_relaxed);
-        ZQ_CUDA(zq::launch_gemv(a, st, false));
+        ZQ_CUDA(zq::launch_gemv(a, st, true));
         return ZQ_OK;
     }
     int8_t* codes = reinterpret_cast<int8_t*>(ws);

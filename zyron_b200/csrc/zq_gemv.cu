@@ -110,8 +110,14 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const uint8_t* __restric
     const int groups = (N + kCols - 1) / kCols;
 
     const int chunks = (int)(col_bytes >> 4);  // 16-byte chunks per column
-    // Warm L2 with this warp's first column group while the quantizer (or
-    // the fused prologue) runs.  Prefetching a second group measured slower.
+    // No griddepcontrol.launch_dependents: a dependent launched early (at
+    // the start, or at each warp's last column) put its blocks and L2
+    // prefetches beside this grid's stream and measured slower (N = 11008,
+    // K = 4096, M = 1: INT8 8.0 -> 10.8 / 9.5 us, INT4 7.3 -> 7.9 / 7.8 us);
+    // the next kernel starts when this grid ends.
+    // Warm L2 with this warp's first column group while the kernel before
+    // (the quantizer, or the previous matmul) finishes.  Prefetching a
+    // second group measured slower.
     if (warp_global < groups) {
         for (int c = 0; c < kCols; ++c) {
             const int col = warp_global * kCols + c;
@@ -280,7 +286,10 @@ cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    // Always a programmatic dependent launch: the kernel reads only the
+    // weight panel before griddepcontrol.wait.
+    (void)pdl;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kern, a.panel, a.N, a.Kp, a.col_scale, a.q, a.row_scale, a.bias, a.y,

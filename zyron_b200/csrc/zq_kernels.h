@@ -11,6 +11,29 @@
 
 namespace zq {
 
+// Launches `kern` with programmatic dependent launch: it may start while the
+// kernel before it on the stream is still running, once that kernel has
+// executed griddepcontrol.launch_dependents (or at its end if it never does).
+// Every kernel launched this way reads only immutable data (weight panels,
+// scales) before its griddepcontrol.wait, and reads or writes everything else
+// after it; the wait returns when the kernels before it have completed and
+// their memory is visible.
+template <class... Params, class... Args>
+cudaError_t launch_pdl_kernel(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<Params>(args)...);
+}
+
 constexpr int kGemvMaxRows = 8;
 // GemmArgs::block_n value selecting the 2-SM (cluster pair) 256 x 256 tile kernel.
 constexpr int kPairBlockN = 512;

@@ -33,6 +33,7 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restr
                                                             int Kp, int8_t* __restrict__ q,
                                                             float* __restrict__ row_scale, int* zero, int n_zero) {
     pdl_launch_dependents();
+    pdl_wait_primary();  // x may come from, and q / counters be read by, the kernels before
     clear_words(zero, n_zero);
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -83,6 +84,7 @@ __global__ void __launch_bounds__(256) quantize_rows_reg_kernel(const float* __r
                                                                 float* __restrict__ row_scale, int* zero,
                                                                 int n_zero) {
     pdl_launch_dependents();
+    pdl_wait_primary();  // x may come from, and q / counters be read by, the kernels before
     clear_words(zero, n_zero);
     constexpr int kRowsPerBlock = 8 / kWarpsPerRow;
     constexpr int kT = 32 * kWarpsPerRow;
@@ -142,22 +144,25 @@ cudaError_t launch_quantize_rows(const float* x, int M, int K, int Kp, int8_t* q
         const int rows_per_block = 8 / wpr;
         const dim3 grid((M + rows_per_block - 1) / rows_per_block);
         switch (wpr) {
-            case 1: quantize_rows_reg_kernel<1, 8><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale, zero, n_zero); break;
-            case 2: quantize_rows_reg_kernel<2, 8><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale, zero, n_zero); break;
-            case 4: quantize_rows_reg_kernel<4, 8><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale, zero, n_zero); break;
-            default: quantize_rows_reg_kernel<8, 8><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale, zero, n_zero); break;
+            case 1: return launch_pdl_kernel(quantize_rows_reg_kernel<1, 8>, grid, dim3(256), 0, stream, x, M, K, Kp, q,
+                                             row_scale, zero, n_zero);
+            case 2: return launch_pdl_kernel(quantize_rows_reg_kernel<2, 8>, grid, dim3(256), 0, stream, x, M, K, Kp, q,
+                                             row_scale, zero, n_zero);
+            case 4: return launch_pdl_kernel(quantize_rows_reg_kernel<4, 8>, grid, dim3(256), 0, stream, x, M, K, Kp, q,
+                                             row_scale, zero, n_zero);
+            default: return launch_pdl_kernel(quantize_rows_reg_kernel<8, 8>, grid, dim3(256), 0, stream, x, M, K,
+                                              Kp, q, row_scale, zero, n_zero);
         }
-        return cudaGetLastError();
     }
     const int rows_per_block = 8;
     const dim3 grid((M + rows_per_block - 1) / rows_per_block);
     const bool vec = (K % 4 == 0) && (Kp % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) &&
                      ((reinterpret_cast<uintptr_t>(q) & 3u) == 0);
     if (vec)
-        quantize_rows_kernel<true><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale, zero, n_zero);
-    else
-        quantize_rows_kernel<false><<<grid, 256, 0, stream>>>(x, M, K, Kp, q, row_scale, zero, n_zero);
-    return cudaGetLastError();
+        return launch_pdl_kernel(quantize_rows_kernel<true>, grid, dim3(256), 0, stream, x, M, K, Kp, q, row_scale,
+                                 zero, n_zero);
+    return launch_pdl_kernel(quantize_rows_kernel<false>, grid, dim3(256), 0, stream, x, M, K, Kp, q, row_scale, zero,
+                             n_zero);
 }
 
 // ---------------------------------------------------------------------------

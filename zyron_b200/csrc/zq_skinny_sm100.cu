@@ -135,6 +135,10 @@ __global__ void __launch_bounds__(SkCfg<kType>::kThreads, 1)
     const int g = blockIdx.x;
     const long long it0 = sk_start(g, T, G);
     const long long it1 = sk_start(g + 1, T, G);
+    // The next kernel on the stream may launch now (it reads nothing of ours
+    // before its griddepcontrol.wait) and take over the SMs as this grid's
+    // CTAs finish.
+    pdl_launch_dependents();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -387,6 +391,7 @@ __global__ void __launch_bounds__(SkCfg<kType>::kThreads, 1)
 
 __global__ void zero_words_kernel(int* __restrict__ p, int n) {
     pdl_launch_dependents();
+    pdl_wait_primary();  // the kernel before may still use the counters
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = 0;
 }
 
@@ -433,8 +438,7 @@ cudaError_t launch_zero_words(int* p, int n, cudaStream_t stream) {
     const int threads = 256;
     int blocks = (n + threads - 1) / threads;
     if (blocks > 148) blocks = 148;
-    zero_words_kernel<<<blocks, threads, 0, stream>>>(p, n);
-    return cudaGetLastError();
+    return launch_pdl_kernel(zero_words_kernel, dim3(blocks), dim3(threads), 0, stream, p, n);
 }
 
 cudaError_t launch_skinny(const SkinnyArgs& a, cudaStream_t stream, bool pdl) {

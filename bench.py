@@ -582,10 +582,8 @@ def run_gemv_workload(args):
 def run_kernels_workload(args):
     """The HBM-bound helper kernels of the path at sizes larger than L2, each
     timed with CUDA events: the activation quantizer (x 8192 x 8192 fp32),
-    the device weight quantizer (W 8192 x 16384 fp32 -> INT8 / INT4 panel),
-    dequantize() of the INT8 panel, and the INT4 -> int8 panel expansion the
-    prefill GEMM runs first (timed as an INT4 matmul minus the same INT8
-    matmul).  GB/s are algorithmic bytes (every input read once, every output
+    the device weight quantizer (W 8192 x 16384 fp32 -> INT8 / INT4 panel) and
+    dequantize() of the INT8 panel.  GB/s are algorithmic bytes (every input read once, every output
     written once)."""
     import torch
 
@@ -646,16 +644,32 @@ def run_kernels_workload(args):
     add("dequantize INT8 (8192 x 16384 -> fp32)", timed(deq), K * N + 4 * N + 4 * K * N)
     del out
     torch.cuda.empty_cache()
-    m = 256
-    xm = torch.randn((m, K), generator=g, device=dev)
-    t4 = timed(lambda: zb.matmul(xm, W4), 5)
-    t8 = timed(lambda: zb.matmul(xm, W8), 5)
-    add("expand INT4 panel to int8 (inside an INT4 matmul, M=256)", max(t4 - t8, 1e-3), K * N // 2 + K * N)
+    # INT4 against INT8 weights in the prefill GEMM on the same shape: the
+    # INT4 kernel streams the packed panel and unpacks it in shared memory
+    gm = 8192
+    xg = torch.randn((gm, K), generator=g, device=dev)
+    yg = torch.empty((gm, N), device=dev)
+    Kp = L.zq_weight_padded_k(W8.handle)
+    codes = torch.empty((gm, Kp), dtype=torch.int8, device=dev)
+    rsg = torch.empty((gm,), device=dev)
+    _lib.check(L.zq_quantize_rows(C.c_void_p(xg.data_ptr()), gm, K, C.c_void_p(codes.data_ptr()), Kp,
+                                  C.c_void_p(rsg.data_ptr()), None))
+    gemm = {}
+    for name, W in (("int8", W8), ("int4", W4)):
+        wsb = L.zq_matmul_workspace_bytes(W.handle, gm)
+        ws = torch.empty(wsb + 256, dtype=torch.uint8, device=dev)
+        wp = (ws.data_ptr() + 255) & ~255
+        us = timed(lambda: _lib.check(L.zq_matmul_codes(W.handle, C.c_void_p(codes.data_ptr()),
+                                                        C.c_void_p(rsg.data_ptr()), gm, None,
+                                                        C.c_void_p(yg.data_ptr()), C.c_void_p(wp), wsb, None)), 10)
+        gemm[name] = {"us": us, "TOPS": 2.0 * gm * N * K / us / 1e6}
+    gemm["int4_over_int8"] = gemm["int4"]["TOPS"] / gemm["int8"]["TOPS"]
     line = {"metric": "helper kernels of the path (HBM-bound)", "value": cases["quantize_rows (activations 8192 x 8192)"]["GBs"],
             "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp32->int8", "data": "synthetic",
             "config": {"workload": "helper_kernels", "x": [M, K], "W": [K, N]},
-            "roofline": {"bound": "hbm", "peak": peak, "unit": "GB/s", "peak_source": peak_src}, "cases": cases}
+            "roofline": {"bound": "hbm", "peak": peak, "unit": "GB/s", "peak_source": peak_src}, "cases": cases,
+            "gemm_M8192_K8192_N16384": gemm}
     print(json.dumps(line), flush=True)
 
 

@@ -20,7 +20,7 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("qt,M,K,N", [(1, 1, 4096, 1000), (2, 8, 1000, 300), (1, 200, 1000, 300),
-                                      (2, 130, 256, 520)])
+                                      (2, 130, 256, 520), (2, 512, 4096, 11008)])
 def test_noalloc_matches_workspace_entry_point(cuda, qt, M, K, N):
     import torch
 

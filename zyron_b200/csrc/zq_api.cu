@@ -161,10 +161,8 @@ zq_status upload_payload(zq_weight* w, const void* payload, cudaStream_t st) {
     ZQ_CUDA(cudaMemsetAsync(w->panel, 0, w->panel_bytes, st));
     if (w->type == ZQ_TYPE_INT8) {
         ZQ_CUDA(cudaMemcpy2DAsync(w->panel, (size_t)w->Kp, payload, K, K, N, cudaMemcpyHostToDevice, st));
-    } else if (K % 2 == 0) {
-        ZQ_CUDA(cudaMemcpy2DAsync(w->panel, (size_t)w->Kp / 2, payload, K / 2, K / 2, N, cudaMemcpyHostToDevice,
-                                  st));
     } else {
+        // the reference's nibble stream, rearranged into the panel layout
         const size_t bytes = ref_payload_bytes(w->type, K, N);
         uint8_t* tmp = nullptr;
         ZQ_CUDA(cudaMalloc(&tmp, bytes));
@@ -181,10 +179,8 @@ zq_status download_payload(const zq_weight* w, void* payload, cudaStream_t st) {
     const size_t K = w->K, N = w->N;
     if (w->type == ZQ_TYPE_INT8) {
         ZQ_CUDA(cudaMemcpy2DAsync(payload, K, w->panel, (size_t)w->Kp, K, N, cudaMemcpyDeviceToHost, st));
-    } else if (K % 2 == 0) {
-        ZQ_CUDA(cudaMemcpy2DAsync(payload, K / 2, w->panel, (size_t)w->Kp / 2, K / 2, N, cudaMemcpyDeviceToHost,
-                                  st));
     } else {
+        // the panel layout, rearranged into the reference's nibble stream
         const size_t bytes = ref_payload_bytes(w->type, K, N);
         uint8_t* tmp = nullptr;
         ZQ_CUDA(cudaMalloc(&tmp, bytes));
@@ -199,14 +195,15 @@ zq_status download_payload(const zq_weight* w, void* payload, cudaStream_t st) {
     return ZQ_OK;
 }
 
-// Packed INT4 panel [N][Kp/2] bytes, box 64 bytes (128 codes) x 128 columns,
-// unswizzled: the decode kernel unpacks it in shared memory.
-zq_status encode_packed_int4(CUtensorMap* map, const void* base, size_t cols, int Kp) {
+// Packed INT4 panel [N][Kp/2] bytes, box 64 bytes (128 codes) x box_rows
+// columns, unswizzled: the decode kernel and the GEMMs unpack it in shared
+// memory.
+zq_status encode_packed_int4(CUtensorMap* map, const void* base, size_t cols, int Kp, int box_rows = 128) {
     zq_status s = get_encoder();
     if (s != ZQ_OK) return s;
     cuuint64_t dims[2] = {(cuuint64_t)(Kp / 2), (cuuint64_t)cols};
     cuuint64_t strides[1] = {(cuuint64_t)(Kp / 2)};
-    cuuint32_t box[2] = {64u, 128u};
+    cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1u, 1u};
     CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -465,14 +462,10 @@ zq_status zq_weight_destroy(zq_weight* w) {
 size_t zq_matmul_workspace_bytes(const zq_weight* w, size_t m) {
     if (!w || m == 0) return 0;
     size_t b = align256(m * (size_t)w->Kp) + align256(m * sizeof(float));
-    // scratch: decode counters and partial sums (m <= 16), or the INT4 panel
-    // expanded to int8 for the tensor-core GEMM (m > 8)
+    // scratch: decode counters and partial sums (m <= 16); the GEMMs need
+    // none (INT4 weights are unpacked in shared memory)
     size_t scratch = 0;
     if (m <= (size_t)zq::kSkinnyMaxRows) scratch = zq::skinny_scratch_bytes((int)w->N, (int)m);
-    if (w->type == ZQ_TYPE_INT4 && m > (size_t)zq::kGemvMaxRows) {
-        const size_t e = align256(w->N * (size_t)w->Kp);
-        if (e > scratch) scratch = e;
-    }
     return b + scratch;
 }
 
@@ -610,33 +603,38 @@ zq_status run_codes_out(const zq_weight* w, const int8_t* codes, const float* rs
         ZQ_CUDA(zq::launch_skinny(a, st, true));
         return ZQ_OK;
     }
-    const int bn = zq::gemm_block_n(M, N);
+    int bn = zq::gemm_block_n(M, N);
+    if (w->type == ZQ_TYPE_INT4 && bn == 256) bn = 128;  // INT4 tiles: 128 columns or the 2-SM pair
     CUtensorMap tmap_a;
     s = encode_kmajor(&tmap_a, codes, m, Kp, 128);
     if (s != ZQ_OK) return s;
     const CUtensorMap* tmap_b = nullptr;
-    CUtensorMap tmap_b_local;
-    if (w->type == ZQ_TYPE_INT8) {
+    {
         zq_weight* mw = const_cast<zq_weight*>(w);
         std::lock_guard<std::mutex> lk(mw->mu);
         const int ti = tile_index(bn);
-        if (!mw->tmap_ready[ti]) {
-            s = encode_kmajor(&mw->tmap_b[ti], w->panel, w->N, Kp, box_rows_b(bn));
-            if (s != ZQ_OK) return s;
-            mw->tmap_ready[ti] = true;
+        if (w->type == ZQ_TYPE_INT8) {
+            if (!mw->tmap_ready[ti]) {
+                s = encode_kmajor(&mw->tmap_b[ti], w->panel, w->N, Kp, box_rows_b(bn));
+                if (s != ZQ_OK) return s;
+                mw->tmap_ready[ti] = true;
+            }
+            tmap_b = &mw->tmap_b[ti];
+        } else {
+            // packed panel; the GEMM unpacks each box in shared memory
+            if (!mw->tmap_p_ready[ti]) {
+                s = encode_packed_int4(&mw->tmap_p[ti], w->panel, w->N, Kp, box_rows_b(bn));
+                if (s != ZQ_OK) return s;
+                mw->tmap_p_ready[ti] = true;
+            }
+            tmap_b = &mw->tmap_p[ti];
         }
-        tmap_b = &mw->tmap_b[ti];
-    } else {
-        int8_t* panel8 = reinterpret_cast<int8_t*>(scratch);
-        ZQ_CUDA(zq::launch_expand_int4(w->panel, N, Kp, panel8, st));
-        s = encode_kmajor(&tmap_b_local, panel8, w->N, Kp, box_rows_b(bn));
-        if (s != ZQ_OK) return s;
-        tmap_b = &tmap_b_local;
-        pdl = true;  // the GEMM follows the expand kernel directly
     }
+    (void)scratch;
     zq::GemmArgs g{&tmap_a, tmap_b, M, N, Kp, bn, rs, w->scales, bias, out, err,
                    w->opt_group_m.load(std::memory_order_relaxed)};
     g.reserved_sms = reserved;
+    g.w4 = w->type == ZQ_TYPE_INT4;
     ZQ_CUDA(zq::launch_gemm(g, st, pdl));
     return ZQ_OK;
 }

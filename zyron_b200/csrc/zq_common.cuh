@@ -86,34 +86,51 @@ __device__ __forceinline__ float zq_epilogue_bias(int32_t acc, float s_row, floa
     return x86_add(zq_epilogue(acc, s_row, s_col), b);
 }
 
-// Sign-extend the eight 4-bit codes of a 32-bit word into two words of four
-// int8 codes each: `even` holds the low nibbles (even linear index), `odd`
-// the high nibbles (quantization.cpp:52-57).
-__device__ __forceinline__ void zq_unpack_int4x8(uint32_t w, uint32_t& even, uint32_t& odd) {
+// Device INT4 panel layout: a column's codes in groups of eight (four
+// bytes); byte j of group g holds code 8g + j in its low nibble and code
+// 8g + j + 4 in its high nibble.  A 32-bit word of the panel therefore holds
+// codes 0..3 of its group in its low nibbles and codes 4..7 in its high
+// nibbles, both in k order, so unpacking needs no byte shuffles.
+__host__ __device__ __forceinline__ int panel_int4_byte(int k) { return ((k >> 3) << 2) | (k & 3); }
+__host__ __device__ __forceinline__ int panel_int4_shift(int k) { return k & 4; }  // 0: low nibble, 4: high
+
+// 8 codes of a panel word -> int8 codes: k 0..3 in `lo4`, 4..7 in `hi4`,
+// sign-extended (v | ((v & 8) * 0x1E) per byte sets the high nibble to 0xF
+// for negatives).
+__device__ __forceinline__ void zq_unpack_int4x8(uint32_t w, uint32_t& lo4, uint32_t& hi4) {
     const uint32_t lo = w & 0x0F0F0F0Fu;
     const uint32_t hi = (w >> 4) & 0x0F0F0F0Fu;
-    // v | ((v & 8) * 0x1E) per byte sets the high nibble to 0xF for negatives.
-    even = lo | ((lo & 0x08080808u) * 0x1Eu);
-    odd = hi | ((hi & 0x08080808u) * 0x1Eu);
+    lo4 = lo | ((lo & 0x08080808u) * 0x1Eu);
+    hi4 = hi | ((hi & 0x08080808u) * 0x1Eu);
 }
 
-// 32 packed INT4 codes (16 bytes, low nibble = even k) -> 32 int8 codes in
-// k order: codes 0..15 in `lo`, 16..31 in `hi`.
-__device__ __forceinline__ void zq_expand_int4x32(const uint4& w, uint4& lo, uint4& hi) {
-    uint32_t e[4], o[4];
-    zq_unpack_int4x8(w.x, e[0], o[0]);
-    zq_unpack_int4x8(w.y, e[1], o[1]);
-    zq_unpack_int4x8(w.z, e[2], o[2]);
-    zq_unpack_int4x8(w.w, e[3], o[3]);
-    lo.x = __byte_perm(e[0], o[0], 0x5140);
-    lo.y = __byte_perm(e[0], o[0], 0x7362);
-    lo.z = __byte_perm(e[1], o[1], 0x5140);
-    lo.w = __byte_perm(e[1], o[1], 0x7362);
-    hi.x = __byte_perm(e[2], o[2], 0x5140);
-    hi.y = __byte_perm(e[2], o[2], 0x7362);
-    hi.z = __byte_perm(e[3], o[3], 0x5140);
-    hi.w = __byte_perm(e[3], o[3], 0x7362);
+// The same as 16 x the codes: a nibble moved to the top of its byte, read as
+// int8, is exactly 16 times its signed value.  Three operations instead of
+// nine; a dot over such codes is 16 times the dot (exact while it fits in
+// int32), so callers shift it back by 4.
+__device__ __forceinline__ void zq_unpack_int4x8_x16(uint32_t w, uint32_t& lo4, uint32_t& hi4) {
+    lo4 = (w << 4) & 0xF0F0F0F0u;
+    hi4 = w & 0xF0F0F0F0u;
 }
+
+// 32 codes (16 panel bytes) -> int8 codes in k order: 0..15 in `lo`, 16..31
+// in `hi`.
+__device__ __forceinline__ void zq_expand_int4x32(const uint4& w, uint4& lo, uint4& hi) {
+    zq_unpack_int4x8(w.x, lo.x, lo.y);
+    zq_unpack_int4x8(w.y, lo.z, lo.w);
+    zq_unpack_int4x8(w.z, hi.x, hi.y);
+    zq_unpack_int4x8(w.w, hi.z, hi.w);
+}
+__device__ __forceinline__ void zq_expand_int4x32_x16(const uint4& w, uint4& lo, uint4& hi) {
+    zq_unpack_int4x8_x16(w.x, lo.x, lo.y);
+    zq_unpack_int4x8_x16(w.y, lo.z, lo.w);
+    zq_unpack_int4x8_x16(w.z, hi.x, hi.y);
+    zq_unpack_int4x8_x16(w.w, hi.z, hi.w);
+}
+
+// A dot over codes unpacked as 16 x the code fits in int32 when
+// 16 x 128 x 8 x Kp does (the extreme codes -128 and -8 included): Kp < 2^17.
+__host__ __device__ __forceinline__ bool int4_x16_fits(int Kp) { return Kp < (1 << 17); }
 
 // ---------------------------------------------------------------------------
 // PTX wrappers (sm_100a)
@@ -172,6 +189,38 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     uint32_t spins = 0;
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
+        if ((++spins & 255u) == 0u) {
+            if (*(volatile uint32_t*)err != kDevErrNone) return false;  // someone else failed
+            if (global_timer_ns() - t0 > limit_ns) {
+                atomicCAS(err, kDevErrNone, code);
+                return false;
+            }
+        }
+    }
+}
+
+// mbar_wait_bounded for a barrier that threads of other CTAs of the cluster
+// arrive on (release at cluster scope): acquire at cluster scope, so their
+// shared-memory writes before the arrival are visible after the wait.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_bounded_cluster(uint64_t* bar, uint32_t parity, uint32_t* err,
+                                                          uint32_t code, uint64_t limit_ns = 4000000000ull) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    uint32_t spins = 0;
+    while (true) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
         if ((++spins & 255u) == 0u) {
             if (*(volatile uint32_t*)err != kDevErrNone) return false;  // someone else failed
             if (global_timer_ns() - t0 > limit_ns) {

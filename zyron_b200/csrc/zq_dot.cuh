@@ -19,30 +19,32 @@ __device__ __forceinline__ void dot16_int8(const uint4 w, const int8_t* __restri
     }
 }
 
-// 16 packed bytes = 32 INT4 codes covering k = kcode .. kcode+31.  Shared
-// activations for INT4 are stored "even/odd split" per group of 8 codes:
-// [k0 k2 k4 k6 | k1 k3 k5 k7], matching the nibble unpack order.
-template <int kM>
+// 16 panel bytes = 32 INT4 codes covering k = kcode .. kcode+31 (the panel
+// layout keeps them in k order, see panel_int4_byte), against activation
+// codes in k order.  kX16: the codes are unpacked as 16 x the code (three
+// operations per eight codes) and the dot is 16 times the true one; the
+// caller shifts the finished sum right by 4 (exact; int4_x16_fits(Kp)).
+template <int kM, bool kX16 = false>
 __device__ __forceinline__ void dot16_int4(const uint4 w, const int8_t* __restrict__ sq, int Kp, int kcode,
                                            int (&acc)[kM]) {
-    uint32_t ev[4], od[4];
-    zq_unpack_int4x8(w.x, ev[0], od[0]);
-    zq_unpack_int4x8(w.y, ev[1], od[1]);
-    zq_unpack_int4x8(w.z, ev[2], od[2]);
-    zq_unpack_int4x8(w.w, ev[3], od[3]);
+    uint4 lo, hi;
+    if (kX16)
+        zq_expand_int4x32_x16(w, lo, hi);
+    else
+        zq_expand_int4x32(w, lo, hi);
 #pragma unroll
     for (int m = 0; m < kM; ++m) {
         const uint4 a0 = *reinterpret_cast<const uint4*>(sq + m * Kp + kcode);
         const uint4 a1 = *reinterpret_cast<const uint4*>(sq + m * Kp + kcode + 16);
         int s = acc[m];
-        s = __dp4a((int)ev[0], (int)a0.x, s);
-        s = __dp4a((int)od[0], (int)a0.y, s);
-        s = __dp4a((int)ev[1], (int)a0.z, s);
-        s = __dp4a((int)od[1], (int)a0.w, s);
-        s = __dp4a((int)ev[2], (int)a1.x, s);
-        s = __dp4a((int)od[2], (int)a1.y, s);
-        s = __dp4a((int)ev[3], (int)a1.z, s);
-        s = __dp4a((int)od[3], (int)a1.w, s);
+        s = __dp4a((int)lo.x, (int)a0.x, s);
+        s = __dp4a((int)lo.y, (int)a0.y, s);
+        s = __dp4a((int)lo.z, (int)a0.z, s);
+        s = __dp4a((int)lo.w, (int)a0.w, s);
+        s = __dp4a((int)hi.x, (int)a1.x, s);
+        s = __dp4a((int)hi.y, (int)a1.y, s);
+        s = __dp4a((int)hi.z, (int)a1.z, s);
+        s = __dp4a((int)hi.w, (int)a1.w, s);
         acc[m] = s;
     }
 }

@@ -22,7 +22,24 @@
 //   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, exact
 //               fp32 rescale (+ bias), 128-bit global stores.
 // Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap
-// the main loop of tile i+1.  Every mbarrier wait is bounded (see
+// the main loop of tile i+1.
+//
+// INT4 weights (kW4) stay packed in HBM and in the TMA copy.  The A boxes
+// keep their own ring, as deep as the INT8 kernel's; k-block i's packed
+// BNx64-byte B box goes to slot i % 4, which also holds its unpacked
+// 128-byte-swizzled BNx128-byte int8 tile.  Eight more warps (6..13) own the
+// slots, two per slot: they unpack slot u's box for k-blocks u, u + 4, ...,
+// release the packed box to the producer and the tile to the MMA, which
+// reads it with the stage's A box and frees it with a second commit.  Every
+// release of a tile needs a generic-to-async proxy fence; with slots owned
+// by warps, four slots' fences run at once instead of one k-block's after
+// another (one group of warps taking every k-block in turn ran the tensor
+// pipe at 40 %).  Each barrier has one waiting role that takes all its
+// phases in order, so no parity wait can match an older phase.  The weight
+// bytes crossing HBM and L2 are the packed ones; nothing is expanded in
+// global memory.
+//
+// Every mbarrier wait is bounded (see
 // mbar_wait_bounded): on timeout the kernel records an error code, drains its
 // own in-flight copies and MMAs, frees TMEM and returns.
 #include "zq_common.cuh"
@@ -44,6 +61,16 @@ constexpr int kBK = 128;  // bytes == int8 codes per k-block (one 128 B swizzle 
 constexpr int kUmmaK = 32;
 constexpr int kThreads = 192;
 constexpr int kEpilogueThreads = 128;
+constexpr int kUnpackThreads = 256;  // warps 6..13 of an INT4-weight kernel
+constexpr int kUnpackWarps = kUnpackThreads / 32;
+constexpr int kSlots = 4;              // packed + unpacked B tiles of an INT4-weight kernel
+constexpr int kSlotWarps = kUnpackWarps / kSlots;  // unpack warps per slot
+template <bool kW4>
+constexpr int threads_for() { return kW4 ? kThreads + kUnpackThreads : kThreads; }
+
+// An accumulator word: the int32 dot, or (INT4 weights unpacked as 16 x the
+// code, see unpack_stage) 16 x the dot, shifted back exactly.
+__device__ __forceinline__ int32_t acc_of(uint32_t r, int shift) { return (int32_t)r >> shift; }
 
 // Epilogue staging: each epilogue warp turns its 32 rows x 32 columns of
 // accumulators around in shared memory so that global stores are 128-byte
@@ -51,15 +78,59 @@ constexpr int kEpilogueThreads = 128;
 constexpr int kEpiPitch = 32;  // floats per staged row; float4 slots XOR-swizzled by row
 constexpr int kEpiBytes = 4 * 32 * kEpiPitch * 4;
 
-template <int BN, int STAGES>
+// Ring stage: [A 128x128 | B BNx128 int8, swizzled] (INT8) or [A] (INT4);
+// INT4 adds kSlots slots of [unpacked B BNx128, swizzled | packed B BNx64].
+template <int BN, int STAGES, bool kW4>
 struct Smem {
     static constexpr int kABytes = kBM * kBK;
     static constexpr int kBBytes = BN * kBK;
-    static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kBarrierBytes = (8 * (2 * STAGES + 4 + 1) + 16 + 127) / 128 * 128;  // keeps the staging area aligned
+    static constexpr int kPBytes = BN * kBK / 2;
+    static constexpr int kStageBytes = kABytes + (kW4 ? 0 : kBBytes);  // = TMA bytes per stage
+    static constexpr int kSlotOffset = STAGES * kStageBytes;
+    static constexpr int kSlotBytes = kBBytes + kPBytes;
+    static constexpr int kSlotsBytes = kW4 ? kSlots * kSlotBytes : 0;
+    static constexpr int kBarrierBytes = (8 * (2 * STAGES + 4 * kSlots + 6) + 16 + 127) / 128 * 128;  // keeps the staging area aligned
     // staging area last: it is only allocated when the output has peers
-    static constexpr int kTotal = 1024 /*alignment slack*/ + STAGES * kStageBytes + kBarrierBytes;
+    static constexpr int kTotal = 1024 /*alignment slack*/ + kSlotOffset + kSlotsBytes + kBarrierBytes;
 };
+
+// Unpack of one stage's packed INT4 tile (rows x 64 bytes of the panel
+// layout, unswizzled) into the 128-byte-swizzled int8 tile (rows x 128 bytes)
+// the MMA reads, by the unpack threads: 16-byte chunk i of the packed tile is row
+// i / 4, codes 32 (i % 4) .. +31, which land in the row's logical 16-byte
+// chunks 2 (i % 4) and 2 (i % 4) + 1, stored at physical chunk
+// (logical ^ row % 8).  Eight consecutive threads cover two rows:
+// conflict-free 16-byte reads and writes.
+//
+// scaled: the codes enter as 16 x the code (zq_expand_int4x32_x16: three
+// operations per eight codes instead of nine); the MMA then accumulates
+// exactly 16 x the dot, which the epilogue shifts back.  The caller uses it
+// while int4_x16_fits(Kp).
+template <int kRows>
+__device__ __forceinline__ void unpack_stage(const uint8_t* __restrict__ packed, uint8_t* __restrict__ conv, int tid,
+                                             bool scaled) {
+    constexpr int kT = 32 * kSlotWarps;  // threads unpacking one slot; a multiple of 32
+    static_assert(kT % 32 == 0, "");
+    // Chunk tid + kT j: row tid / 4 + (kT / 4) j, column tid % 4; kT / 4 is
+    // a multiple of 8, so the row's swizzle (row % 8) is the same for all j.
+    const int c = tid & 3, sw = (tid >> 2) & 7;
+    const uint8_t* src = packed + tid * 16;
+    uint8_t* dlo = conv + (tid >> 2) * 128 + (((2 * c) ^ sw) << 4);
+    uint8_t* dhi = conv + (tid >> 2) * 128 + (((2 * c + 1) ^ sw) << 4);
+#pragma unroll
+    for (int j = 0; j < kRows * 4 / kT; ++j) {
+        const uint4 v = *reinterpret_cast<const uint4*>(src + kT * 16 * j);
+        uint4 lo, hi;
+        if (scaled)
+            zq_expand_int4x32_x16(v, lo, hi);
+        else
+            zq_expand_int4x32(v, lo, hi);
+        *reinterpret_cast<uint4*>(dlo + (kT / 4) * 128 * j) = lo;
+        *reinterpret_cast<uint4*>(dhi + (kT / 4) * 128 * j) = hi;
+    }
+    // generic-proxy writes become visible to the tensor core's reads
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 
 
 
@@ -72,7 +143,7 @@ struct Smem {
 // packets instead of 16-byte ones.  Ragged blocks store element by element.
 __device__ __forceinline__ void store_block(const uint32_t (&r)[32], float* __restrict__ stage, int row0, int lane,
                                             int M, int n0, int N, float sr, const float* __restrict__ col_scale,
-                                            const float* __restrict__ bias, const OutDesc& out) {
+                                            const float* __restrict__ bias, const OutDesc& out, int shift) {
     const int row = row0 + lane;
     if (out.vec && n0 + 32 <= N) {
         const float4* cs4 = reinterpret_cast<const float4*>(col_scale + n0);
@@ -83,15 +154,15 @@ __device__ __forceinline__ void store_block(const uint32_t (&r)[32], float* __re
             const float4 s4 = __ldg(cs4 + j);
             if (b4) {
                 const float4 b = __ldg(b4 + j);
-                o[j].x = zq_epilogue_bias((int32_t)r[4 * j + 0], sr, s4.x, b.x);
-                o[j].y = zq_epilogue_bias((int32_t)r[4 * j + 1], sr, s4.y, b.y);
-                o[j].z = zq_epilogue_bias((int32_t)r[4 * j + 2], sr, s4.z, b.z);
-                o[j].w = zq_epilogue_bias((int32_t)r[4 * j + 3], sr, s4.w, b.w);
+                o[j].x = zq_epilogue_bias(acc_of(r[4 * j + 0], shift), sr, s4.x, b.x);
+                o[j].y = zq_epilogue_bias(acc_of(r[4 * j + 1], shift), sr, s4.y, b.y);
+                o[j].z = zq_epilogue_bias(acc_of(r[4 * j + 2], shift), sr, s4.z, b.z);
+                o[j].w = zq_epilogue_bias(acc_of(r[4 * j + 3], shift), sr, s4.w, b.w);
             } else {
-                o[j].x = zq_epilogue((int32_t)r[4 * j + 0], sr, s4.x);
-                o[j].y = zq_epilogue((int32_t)r[4 * j + 1], sr, s4.y);
-                o[j].z = zq_epilogue((int32_t)r[4 * j + 2], sr, s4.z);
-                o[j].w = zq_epilogue((int32_t)r[4 * j + 3], sr, s4.w);
+                o[j].x = zq_epilogue(acc_of(r[4 * j + 0], shift), sr, s4.x);
+                o[j].y = zq_epilogue(acc_of(r[4 * j + 1], shift), sr, s4.y);
+                o[j].z = zq_epilogue(acc_of(r[4 * j + 2], shift), sr, s4.z);
+                o[j].w = zq_epilogue(acc_of(r[4 * j + 3], shift), sr, s4.w);
             }
         }
         float4* st4 = reinterpret_cast<float4*>(stage);
@@ -121,7 +192,7 @@ __device__ __forceinline__ void store_block(const uint32_t (&r)[32], float* __re
         if (n < N) {
             const float sc = __ldg(col_scale + n);
             const float val =
-                bias ? zq_epilogue_bias((int32_t)r[j], sr, sc, __ldg(bias + n)) : zq_epilogue((int32_t)r[j], sr, sc);
+                bias ? zq_epilogue_bias(acc_of(r[j], shift), sr, sc, __ldg(bias + n)) : zq_epilogue(acc_of(r[j], shift), sr, sc);
             for (int d = 0; d < out.count; ++d) out.base[d][base_off + n] = val;
         }
     }
@@ -133,7 +204,8 @@ __device__ __forceinline__ void store_block(const uint32_t (&r)[32], float* __re
 template <int BN>
 __device__ __forceinline__ void store_tile_rows(uint32_t taddr, int row, bool row_ok, int nbase, int N, float sr,
                                                 const float* __restrict__ col_scale,
-                                                const float* __restrict__ bias, float* __restrict__ y, bool vec_ok) {
+                                                const float* __restrict__ bias, float* __restrict__ y, bool vec_ok,
+                                                int shift) {
     float* yrow = y + (size_t)(row_ok ? row : 0) * N;
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
@@ -152,15 +224,15 @@ __device__ __forceinline__ void store_tile_rows(uint32_t taddr, int row, bool ro
                 float4 o;
                 if (b4) {
                     const float4 b = __ldg(b4 + j);
-                    o.x = zq_epilogue_bias((int32_t)r[4 * j + 0], sr, s.x, b.x);
-                    o.y = zq_epilogue_bias((int32_t)r[4 * j + 1], sr, s.y, b.y);
-                    o.z = zq_epilogue_bias((int32_t)r[4 * j + 2], sr, s.z, b.z);
-                    o.w = zq_epilogue_bias((int32_t)r[4 * j + 3], sr, s.w, b.w);
+                    o.x = zq_epilogue_bias(acc_of(r[4 * j + 0], shift), sr, s.x, b.x);
+                    o.y = zq_epilogue_bias(acc_of(r[4 * j + 1], shift), sr, s.y, b.y);
+                    o.z = zq_epilogue_bias(acc_of(r[4 * j + 2], shift), sr, s.z, b.z);
+                    o.w = zq_epilogue_bias(acc_of(r[4 * j + 3], shift), sr, s.w, b.w);
                 } else {
-                    o.x = zq_epilogue((int32_t)r[4 * j + 0], sr, s.x);
-                    o.y = zq_epilogue((int32_t)r[4 * j + 1], sr, s.y);
-                    o.z = zq_epilogue((int32_t)r[4 * j + 2], sr, s.z);
-                    o.w = zq_epilogue((int32_t)r[4 * j + 3], sr, s.w);
+                    o.x = zq_epilogue(acc_of(r[4 * j + 0], shift), sr, s.x);
+                    o.y = zq_epilogue(acc_of(r[4 * j + 1], shift), sr, s.y);
+                    o.z = zq_epilogue(acc_of(r[4 * j + 2], shift), sr, s.z);
+                    o.w = zq_epilogue(acc_of(r[4 * j + 3], shift), sr, s.w);
                 }
                 dst[j] = o;
             }
@@ -170,8 +242,8 @@ __device__ __forceinline__ void store_tile_rows(uint32_t taddr, int row, bool ro
                 const int n = n0 + j;
                 if (n < N) {
                     const float sc = __ldg(col_scale + n);
-                    yrow[n] = bias ? zq_epilogue_bias((int32_t)r[j], sr, sc, __ldg(bias + n))
-                                   : zq_epilogue((int32_t)r[j], sr, sc);
+                    yrow[n] = bias ? zq_epilogue_bias(acc_of(r[j], shift), sr, sc, __ldg(bias + n))
+                                   : zq_epilogue(acc_of(r[j], shift), sr, sc);
                 }
             }
         }
@@ -195,25 +267,32 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
 // into the matmul).  A separate instantiation keeps the single-destination
 // epilogue lean: the gather path's staging roughly doubles the epilogue
 // warps' registers and costs the plain matmul about 8 % when compiled in.
-template <int BN, int STAGES, bool kGather>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, int STAGES, bool kGather, bool kW4>
+__global__ void __launch_bounds__(threads_for<kW4>(), 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    int M, int N, int Kp, const float* __restrict__ row_scale,
                    const float* __restrict__ col_scale, const float* __restrict__ bias,
-                   const __grid_constant__ OutDesc out, uint32_t* __restrict__ err, int group_m) {
-    using S = Smem<BN, STAGES>;
+                   const __grid_constant__ OutDesc out, uint32_t* __restrict__ err, int group_m, int shift) {
+    using S = Smem<BN, STAGES, kW4>;
     constexpr uint32_t kTmemCols = 2 * BN;  // power of two >= 32 for BN in {64,128,256}
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* stage_base = smem;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStageBytes);
-    float* epi_stage = reinterpret_cast<float*>(smem + STAGES * S::kStageBytes + S::kBarrierBytes);
+    uint8_t* slot_base = smem + S::kSlotOffset;  // INT4: [unpacked | packed] B tiles
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kSlotOffset + S::kSlotsBytes);
+    float* epi_stage = reinterpret_cast<float*>(smem + S::kSlotOffset + S::kSlotsBytes + S::kBarrierBytes);
     uint64_t* full = bars;
     uint64_t* empty = bars + STAGES;
     uint64_t* tfull = bars + 2 * STAGES;
     uint64_t* tempty = bars + 2 * STAGES + 2;
     uint64_t* mma_done = bars + 2 * STAGES + 4;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+    // INT4 slots: packed box landed (TMA) / read (unpack warps); unpacked
+    // tile ready (unpack warps) / read (MMA commit)
+    uint64_t* full_p = bars + 2 * STAGES + 6;
+    uint64_t* p_empty = full_p + kSlots;
+    uint64_t* conv_full = full_p + 2 * kSlots;
+    uint64_t* conv_empty = full_p + 3 * kSlots;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -227,6 +306,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
+        if (kW4)
+            for (int c = 0; c < kSlots; ++c) {
+                mbar_init(&full_p[c], 1);
+                mbar_init(&p_empty[c], kSlotWarps);
+                mbar_init(&conv_full[c], kSlotWarps);
+                mbar_init(&conv_empty[c], 1);
+            }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
             mbar_init(&tempty[a], kEpilogueThreads);
@@ -256,24 +342,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
+            int slot = 0;  // INT4: slot of this k-block's packed box
+            uint32_t pphase = 0;
             int issued[STAGES];
             uint32_t last_phase[STAGES];
+            int p_issued[kSlots];
+            uint32_t p_last[kSlots];
 #pragma unroll
             for (int s = 0; s < STAGES; ++s) issued[s] = 0, last_phase[s] = 0;
+#pragma unroll
+            for (int s = 0; s < kSlots; ++s) p_issued[s] = 0, p_last[s] = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
                 int mt, nt;
                 tile_coords(t, m_tiles, n_tiles, group_m, mt, nt);
                 for (int kb = 0; kb < k_blocks; ++kb) {
-                    if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, err, kDevErrTimeoutProducer)) {
+                    if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, err, kDevErrTimeoutProducer) ||
+                        (kW4 && !mbar_wait_bounded(&p_empty[slot], pphase ^ 1u, err, kDevErrTimeoutProducer))) {
                         ok = false;
                         break;
                     }
                     uint8_t* sa = stage_base + stage * S::kStageBytes;
-                    uint8_t* sb = sa + S::kABytes;
                     mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
                     tma_load_2d(sa, &tmap_a, &full[stage], kb * kBK, mt * kBM);
-                    tma_load_2d(sb, &tmap_b, &full[stage], kb * kBK, nt * BN);
+                    if (kW4) {
+                        mbar_arrive_expect_tx(&full_p[slot], S::kPBytes);
+                        tma_load_2d(slot_base + slot * S::kSlotBytes + S::kBBytes, &tmap_b, &full_p[slot],
+                                    kb * (kBK / 2), nt * BN);
+                        p_issued[slot] = 1;
+                        p_last[slot] = pphase;
+                        if (++slot == kSlots) slot = 0, pphase ^= 1u;
+                    } else {
+                        tma_load_2d(sa + S::kABytes, &tmap_b, &full[stage], kb * kBK, nt * BN);
+                    }
                     issued[stage] = 1;
                     last_phase[stage] = phase;
                     if (++stage == STAGES) stage = 0, phase ^= 1u;
@@ -283,12 +384,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             // can exit (on the normal path these waits return at once).
             for (int s = 0; s < STAGES; ++s)
                 if (issued[s]) mbar_drain_bounded(&full[s], last_phase[s], err, kDevErrTimeoutDrain);
+            for (int s = 0; s < kSlots; ++s)
+                if (p_issued[s]) mbar_drain_bounded(&full_p[s], p_last[s], err, kDevErrTimeoutDrain);
         }
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_i8(kBM, BN);
             int stage = 0;
             uint32_t phase = 0;
+            int slot = 0;  // INT4: slot of this k-block's unpacked tile
+            uint32_t cphase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
@@ -297,19 +402,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(acc * BN);
                 for (int kb = 0; kb < k_blocks; ++kb) {
-                    if (!mbar_wait_bounded(&full[stage], phase, err, kDevErrTimeoutMma)) {
+                    if (!mbar_wait_bounded(&full[stage], phase, err, kDevErrTimeoutMma) ||
+                        (kW4 && !mbar_wait_bounded(&conv_full[slot], cphase, err, kDevErrTimeoutMma))) {
                         ok = false;
                         break;
                     }
                     tmem_fence_after();
                     const uint32_t sa = smem_u32(stage_base + stage * S::kStageBytes);
-                    const uint32_t sb = sa + S::kABytes;
+                    const uint32_t sb = kW4 ? smem_u32(slot_base + slot * S::kSlotBytes) : sa + S::kABytes;
 #pragma unroll
                     for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
                         umma_i8(d, make_sw128_desc(sa + kk * kUmmaK), make_sw128_desc(sb + kk * kUmmaK), idesc,
                                 (kb > 0 || kk > 0) ? 1u : 0u);
                     }
                     umma_commit(&empty[stage]);
+                    if (kW4) {
+                        umma_commit(&conv_empty[slot]);
+                        if (++slot == kSlots) slot = 0, cphase ^= 1u;
+                    }
                     if (++stage == STAGES) stage = 0, phase ^= 1u;
                 }
                 if (!ok) break;
@@ -319,6 +429,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             // All MMAs issued by this thread complete before TMEM is freed.
             umma_commit(mma_done);
             mbar_drain_bounded(mma_done, 0, err, kDevErrTimeoutDrain);
+        }
+    } else if (kW4 && warp >= 6) {
+        // Unpack warps 6 + 2u and 7 + 2u own slot u: k-blocks u, u + 4, ...
+        const int u = (warp - 6) / kSlotWarps;  // the slot's warps are consecutive: different sub-partitions
+        const int tid = ((warp - 6) % kSlotWarps) * 32 + lane;  // within the slot's warps
+        uint8_t* conv = slot_base + u * S::kSlotBytes;
+        uint32_t ph = 0;
+        const long long total =
+            (long long)((num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) * k_blocks;
+        for (long long it = u; it < total; it += kSlots) {
+            if (!mbar_wait_bounded(&full_p[u], ph, err, kDevErrTimeoutMma) ||
+                !mbar_wait_bounded(&conv_empty[u], ph ^ 1u, err, kDevErrTimeoutMma))
+                break;
+            unpack_stage<BN>(conv + S::kBBytes, conv, tid, shift != 0);
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&p_empty[u]);
+                mbar_arrive(&conv_full[u]);
+            }
+            ph ^= 1u;
         }
     } else {
         // Epilogue warps 2..5 own TMEM lane quarters (warp % 4) * 32.
@@ -336,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float sr = row < M ? __ldg(row_scale + row) : 0.0f;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
             if constexpr (!kGather) {
-                store_tile_rows<BN>(taddr, row, row < M, nt * BN, N, sr, col_scale, bias, out.base[0], vec1);
+                store_tile_rows<BN>(taddr, row, row < M, nt * BN, N, sr, col_scale, bias, out.base[0], vec1, shift);
             } else {
                 float* stage = epi_stage + quarter * 32 * kEpiPitch;
 #pragma unroll 1
@@ -345,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_ld_32x32b_x32(taddr + c * 32, r);
                     tmem_ld_wait();
                     const int n0 = nt * BN + c * 32;
-                    if (row0 < M && n0 < N) store_block(r, stage, row0, lane, M, n0, N, sr, col_scale, bias, out);
+                    if (row0 < M && n0 < N) store_block(r, stage, row0, lane, M, n0, N, sr, col_scale, bias, out, shift);
                 }
             }
             tmem_fence_before();
@@ -370,11 +500,11 @@ bool general_output(const GemmArgs& a) {
     return a.out.count != 1 || a.out.ldy != (long long)a.N || a.out.col_offset != 0;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool kW4>
 cudaError_t launch_gemm_t(const GemmArgs& a, cudaStream_t stream, bool pdl) {
-    using S = Smem<BN, STAGES>;
+    using S = Smem<BN, STAGES, kW4>;
     const bool gather = general_output(a);
-    auto kern = gather ? gemm_i8_kernel<BN, STAGES, true> : gemm_i8_kernel<BN, STAGES, false>;
+    auto kern = gather ? gemm_i8_kernel<BN, STAGES, true, kW4> : gemm_i8_kernel<BN, STAGES, false, kW4>;
     const int smem = S::kTotal + (gather ? kEpiBytes : 0);
     cudaError_t e = ensure_smem_attr(kern, smem);
     if (e != cudaSuccess) return e;
@@ -384,7 +514,7 @@ cudaError_t launch_gemm_t(const GemmArgs& a, cudaStream_t stream, bool pdl) {
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(threads_for<kW4>());
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -395,8 +525,12 @@ cudaError_t launch_gemm_t(const GemmArgs& a, cudaStream_t stream, bool pdl) {
     const int m_tiles = (a.M + kBM - 1) / kBM;
     int group_m = a.group_m > 0 ? a.group_m : m_tiles;
     if (group_m > m_tiles) group_m = m_tiles;
+    // INT4: codes unpacked as 16 x the code while 16 x Kp products fit in an
+    // int32 accumulator even for the extreme codes -128 and -8 (16 x 128 x 8
+    // x 131040 < 2^31), exact sign extension beyond
+    const int shift = kW4 && int4_x16_fits(a.Kp) ? 4 : 0;
     return cudaLaunchKernelEx(&cfg, kern, *a.tmap_a, *a.tmap_b, a.M, a.N, a.Kp, a.row_scale, a.col_scale, a.bias,
-                              a.out, a.err, group_m);
+                              a.out, a.err, group_m, shift);
 }
 
 
@@ -409,15 +543,26 @@ cudaError_t launch_gemm_t(const GemmArgs& a, cudaStream_t stream, bool pdl) {
 // DRAM latency, a third less L2 -> SM traffic.  The even CTA (leader) issues
 // the MMAs; its commits arrive on both CTAs' barriers (CTA mask 0b11).  Each
 // CTA's accumulator rows live in its own TMEM, so the epilogue is unchanged.
+//
+// INT4 weights: the A boxes keep the pair's ring on the leader's barriers;
+// each CTA lands its packed 128x64-byte B box in slot i % 4 on its own
+// barrier, its slot-owning unpack warps write the swizzled int8 tile next to
+// it and arrive on the leader's `conv_full` barrier across the cluster; the
+// leader's MMA issuer waits there for both CTAs' tiles, and its commits free
+// the tile (`conv_empty`) in both CTAs.
 // ===========================================================================
-constexpr int kStages2 = 6;
-
+template <bool kW4>
 struct Smem2 {
+    static constexpr int kStages = 6;
     static constexpr int kABytes = 128 * kBK;  // this CTA's 128 rows of A
-    static constexpr int kBBytes = 128 * kBK;  // this CTA's 128 rows (columns of W) of B
-    static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kBarrierBytes = (8 * (2 * kStages2 + 4 + 1) + 16 + 127) / 128 * 128;
-    static constexpr int kTotal = 1024 + kStages2 * kStageBytes + kBarrierBytes;
+    static constexpr int kBBytes = 128 * kBK;  // this CTA's 128 rows (columns of W) of B, int8 swizzled
+    static constexpr int kPBytes = 128 * kBK / 2;  // packed INT4 B box
+    static constexpr int kStageBytes = kABytes + (kW4 ? 0 : kBBytes);  // = TMA bytes per stage and CTA
+    static constexpr int kSlotOffset = kStages * kStageBytes;
+    static constexpr int kSlotBytes = kBBytes + kPBytes;
+    static constexpr int kSlotsBytes = kW4 ? kSlots * kSlotBytes : 0;
+    static constexpr int kBarrierBytes = (8 * (2 * kStages + 4 * kSlots + 6) + 16 + 127) / 128 * 128;
+    static constexpr int kTotal = 1024 + kSlotOffset + kSlotsBytes + kBarrierBytes;
 };
 
 
@@ -471,25 +616,34 @@ __device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
         : "memory");
 }
 
-template <bool kGather>
-__global__ void __launch_bounds__(kThreads, 1)
+template <bool kGather, bool kW4>
+__global__ void __launch_bounds__(threads_for<kW4>(), 1)
     gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                         int M, int N, int Kp, const float* __restrict__ row_scale,
                         const float* __restrict__ col_scale, const float* __restrict__ bias,
-                        const __grid_constant__ OutDesc out, uint32_t* __restrict__ err, int group_m) {
-    using S = Smem2;
+                        const __grid_constant__ OutDesc out, uint32_t* __restrict__ err, int group_m, int shift) {
+    using S = Smem2<kW4>;
+    constexpr int kStages2 = S::kStages;
     constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* stage_base = smem;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages2 * S::kStageBytes);
-    float* epi_stage = reinterpret_cast<float*>(smem + kStages2 * S::kStageBytes + S::kBarrierBytes);
-    uint64_t* full = bars;                       // leader's copy used
+    uint8_t* slot_base = smem + S::kSlotOffset;  // INT4: [unpacked | packed] B tiles
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kSlotOffset + S::kSlotsBytes);
+    float* epi_stage = reinterpret_cast<float*>(smem + S::kSlotOffset + S::kSlotsBytes + S::kBarrierBytes);
+    uint64_t* full = bars;                       // INT8: leader's copy used; INT4: each CTA's own
     uint64_t* empty = bars + kStages2;           // both copies used
     uint64_t* tfull = bars + 2 * kStages2;       // both copies used
     uint64_t* tempty = bars + 2 * kStages2 + 2;  // leader's copy used
     uint64_t* mma_done = bars + 2 * kStages2 + 4;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages2 + 5);
+    // INT4 slots: packed box landed (own TMA) / read (own unpack warps);
+    // unpacked tiles ready (leader's copy, both CTAs' unpack warps) / read
+    // (MMA commit, both copies)
+    uint64_t* full_p = bars + 2 * kStages2 + 6;
+    uint64_t* p_empty = full_p + kSlots;
+    uint64_t* conv_full = full_p + 2 * kSlots;
+    uint64_t* conv_empty = full_p + 3 * kSlots;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -507,6 +661,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
+        if (kW4)
+            for (int c = 0; c < kSlots; ++c) {
+                mbar_init(&full_p[c], 1);
+                mbar_init(&p_empty[c], kSlotWarps);
+                mbar_init(&conv_full[c], 2 * kSlotWarps);  // both CTAs' slot warps
+                mbar_init(&conv_empty[c], 1);
+            }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
             mbar_init(&tempty[a], 2 * kEpilogueThreads);  // both CTAs' epilogue threads
@@ -532,25 +693,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
+            int slot = 0;  // INT4: slot of this k-block's packed box
+            uint32_t pphase = 0;
             int issued[kStages2];
             uint32_t last_phase[kStages2];
+            int p_issued[kSlots];
+            uint32_t p_last[kSlots];
 #pragma unroll
             for (int s = 0; s < kStages2; ++s) issued[s] = 0, last_phase[s] = 0;
+#pragma unroll
+            for (int s = 0; s < kSlots; ++s) p_issued[s] = 0, p_last[s] = 0;
             bool ok = true;
             for (int t = cluster; t < num_tiles && ok; t += clusters) {
                 int mt, nt;
                 tile_coords(t, m_tiles, n_tiles, group_m, mt, nt);
                 for (int kb = 0; kb < k_blocks; ++kb) {
-                    if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, err, kDevErrTimeoutProducer)) {
+                    if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, err, kDevErrTimeoutProducer) ||
+                        (kW4 && !mbar_wait_bounded(&p_empty[slot], pphase ^ 1u, err, kDevErrTimeoutProducer))) {
                         ok = false;
                         break;
                     }
                     uint8_t* sa = stage_base + stage * S::kStageBytes;
-                    uint8_t* sb = sa + S::kABytes;
-                    // the leader expects both CTAs' bytes on its barrier
+                    // the leader expects both CTAs' A (and INT8 B) bytes on its barrier
                     if (leader) mbar_arrive_expect_tx(&full[stage], 2 * S::kStageBytes);
                     tma_load_2d_pair(sa, &tmap_a, &full[stage], kb * kBK, mt * 256 + (int)rank * 128);
-                    tma_load_2d_pair(sb, &tmap_b, &full[stage], kb * kBK, nt * 256 + (int)rank * 128);
+                    if (kW4) {
+                        // own barrier: this CTA's unpack warps wait for it
+                        mbar_arrive_expect_tx(&full_p[slot], S::kPBytes);
+                        tma_load_2d(slot_base + slot * S::kSlotBytes + S::kBBytes, &tmap_b, &full_p[slot],
+                                    kb * (kBK / 2), nt * 256 + (int)rank * 128);
+                        p_issued[slot] = 1;
+                        p_last[slot] = pphase;
+                        if (++slot == kSlots) slot = 0, pphase ^= 1u;
+                    } else {
+                        tma_load_2d_pair(sa + S::kABytes, &tmap_b, &full[stage], kb * kBK,
+                                         nt * 256 + (int)rank * 128);
+                    }
                     issued[stage] = 1;
                     last_phase[stage] = phase;
                     if (++stage == kStages2) stage = 0, phase ^= 1u;
@@ -559,6 +737,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // Drain: the leader can see every copy of the pair complete on its
             // full barriers; the peer's copies land before the leader's MMAs
             // release the stage (empty), so the peer waits on empty instead.
+            // Packed INT4 boxes land on each CTA's own barriers.
             for (int s = 0; s < kStages2; ++s) {
                 if (!issued[s]) continue;
                 if (leader)
@@ -566,12 +745,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 else
                     mbar_drain_bounded(&empty[s], last_phase[s], err, kDevErrTimeoutDrain);
             }
+            for (int s = 0; s < kSlots; ++s)
+                if (p_issued[s]) mbar_drain_bounded(&full_p[s], p_last[s], err, kDevErrTimeoutDrain);
         }
     } else if (warp == 1) {
         if (lane == 0 && leader) {
             constexpr uint32_t idesc = idesc_i8(256, 256);
             int stage = 0;
             uint32_t phase = 0;
+            int slot = 0;  // INT4: slot of this k-block's unpacked tiles
+            uint32_t cphase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
@@ -580,18 +763,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(acc * 256);
                 for (int kb = 0; kb < k_blocks; ++kb) {
-                    if (!mbar_wait_bounded(&full[stage], phase, err, kDevErrTimeoutMma)) {
+                    if (!mbar_wait_bounded(&full[stage], phase, err, kDevErrTimeoutMma) ||
+                        (kW4 && !mbar_wait_bounded_cluster(&conv_full[slot], cphase, err, kDevErrTimeoutMma))) {
                         ok = false;
                         break;
                     }
                     tmem_fence_after();
                     const uint32_t sa = smem_u32(stage_base + stage * S::kStageBytes);
-                    const uint32_t sb = sa + S::kABytes;
+                    const uint32_t sb = kW4 ? smem_u32(slot_base + slot * S::kSlotBytes) : sa + S::kABytes;
 #pragma unroll
                     for (int kk = 0; kk < kBK / kUmmaK; ++kk)
                         umma_i8_pair(d, make_sw128_desc(sa + kk * kUmmaK), make_sw128_desc(sb + kk * kUmmaK), idesc,
                                      (kb > 0 || kk > 0) ? 1u : 0u);
                     umma_commit_pair(&empty[stage]);
+                    if (kW4) {
+                        umma_commit_pair(&conv_empty[slot]);
+                        if (++slot == kSlots) slot = 0, cphase ^= 1u;
+                    }
                     if (++stage == kStages2) stage = 0, phase ^= 1u;
                 }
                 if (!ok) break;
@@ -604,6 +792,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             // peer: its TMEM is written by the leader's MMAs; wait for them to
             // finish before the final barrier frees TMEM
             mbar_drain_bounded(mma_done, 0, err, kDevErrTimeoutDrain);
+        }
+    } else if (kW4 && warp >= 6) {
+        // Unpack warps 6 + 2u and 7 + 2u (both CTAs) own slot u: this CTA's
+        // tiles of k-blocks u, u + 4, ..., announced on the leader's barrier.
+        const int u = (warp - 6) / kSlotWarps;  // the slot's warps are consecutive: different sub-partitions
+        const int tid = ((warp - 6) % kSlotWarps) * 32 + lane;  // within the slot's warps
+        uint8_t* conv = slot_base + u * S::kSlotBytes;
+        const uint32_t conv_leader = map_to_rank(&conv_full[u], 0);
+        uint32_t ph = 0;
+        const long long total = (long long)((num_tiles - cluster + clusters - 1) / clusters) * k_blocks;
+        for (long long it = u; it < total; it += kSlots) {
+            if (!mbar_wait_bounded(&full_p[u], ph, err, kDevErrTimeoutMma) ||
+                !mbar_wait_bounded(&conv_empty[u], ph ^ 1u, err, kDevErrTimeoutMma))
+                break;
+            unpack_stage<128>(conv + S::kBBytes, conv, tid, shift != 0);
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&p_empty[u]);
+                mbar_arrive_cluster(conv_leader);
+            }
+            ph ^= 1u;
         }
     } else {
         const int quarter = warp & 3;
@@ -621,7 +830,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float sr = row < M ? __ldg(row_scale + row) : 0.0f;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * 256);
             if constexpr (!kGather) {
-                store_tile_rows<256>(taddr, row, row < M, nt * 256, N, sr, col_scale, bias, out.base[0], vec1);
+                store_tile_rows<256>(taddr, row, row < M, nt * 256, N, sr, col_scale, bias, out.base[0], vec1, shift);
             } else {
                 float* stage = epi_stage + quarter * 32 * kEpiPitch;
 #pragma unroll 1
@@ -630,7 +839,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_ld_32x32b_x32(taddr + c * 32, r);
                     tmem_ld_wait();
                     const int n0 = nt * 256 + c * 32;
-                    if (row0 < M && n0 < N) store_block(r, stage, row0, lane, M, n0, N, sr, col_scale, bias, out);
+                    if (row0 < M && n0 < N) store_block(r, stage, row0, lane, M, n0, N, sr, col_scale, bias, out, shift);
                 }
             }
             tmem_fence_before();
@@ -649,10 +858,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+template <bool kW4>
 cudaError_t launch_gemm_pair(const GemmArgs& a, cudaStream_t stream, bool pdl) {
-    using S = Smem2;
+    using S = Smem2<kW4>;
     const bool gather = general_output(a);
-    auto kern = gather ? gemm_i8_pair_kernel<true> : gemm_i8_pair_kernel<false>;
+    auto kern = gather ? gemm_i8_pair_kernel<true, kW4> : gemm_i8_pair_kernel<false, kW4>;
     const int smem = S::kTotal + (gather ? kEpiBytes : 0);
     cudaError_t e = ensure_smem_attr(kern, smem);
     if (e != cudaSuccess) return e;
@@ -663,7 +873,7 @@ cudaError_t launch_gemm_pair(const GemmArgs& a, cudaStream_t stream, bool pdl) {
     if (clusters > tiles) clusters = tiles;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(threads_for<kW4>());
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
@@ -679,8 +889,12 @@ cudaError_t launch_gemm_pair(const GemmArgs& a, cudaStream_t stream, bool pdl) {
     int group_m = a.group_m > 0 ? (a.group_m + 1) / 2 : m_tiles;  // group size in 256-row tiles
     if (group_m > m_tiles) group_m = m_tiles;
     if (group_m < 1) group_m = 1;
+    // INT4: codes unpacked as 16 x the code while 16 x Kp products fit in an
+    // int32 accumulator even for the extreme codes -128 and -8 (16 x 128 x 8
+    // x 131040 < 2^31), exact sign extension beyond
+    const int shift = kW4 && int4_x16_fits(a.Kp) ? 4 : 0;
     return cudaLaunchKernelEx(&cfg, kern, *a.tmap_a, *a.tmap_b, a.M, a.N, a.Kp, a.row_scale, a.col_scale, a.bias,
-                              a.out, a.err, group_m);
+                              a.out, a.err, group_m, shift);
 }
 
 }  // namespace
@@ -727,11 +941,21 @@ int gemm_block_n(int M, int N) {
 }
 
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream, bool pdl) {
-    if (a.block_n == kPairBlockN) return launch_gemm_pair(a, stream, pdl);
+    if (a.w4) {
+        // INT4: 16 KiB A stages plus four 24 / 12 KiB slots; a 256-column
+        // tile's slots would leave too shallow an A ring
+        if (a.block_n == kPairBlockN) return launch_gemm_pair<true>(a, stream, pdl);
+        switch (a.block_n) {
+            case 128: return launch_gemm_t<128, 6, true>(a, stream, pdl);
+            case 64: return launch_gemm_t<64, 8, true>(a, stream, pdl);
+            default: return cudaErrorInvalidValue;
+        }
+    }
+    if (a.block_n == kPairBlockN) return launch_gemm_pair<false>(a, stream, pdl);
     switch (a.block_n) {
-        case 256: return launch_gemm_t<256, 4>(a, stream, pdl);
-        case 128: return launch_gemm_t<128, 6>(a, stream, pdl);
-        case 64: return launch_gemm_t<64, 8>(a, stream, pdl);
+        case 256: return launch_gemm_t<256, 4, false>(a, stream, pdl);
+        case 128: return launch_gemm_t<128, 6, false>(a, stream, pdl);
+        case 64: return launch_gemm_t<64, 8, false>(a, stream, pdl);
         default: return cudaErrorInvalidValue;
     }
 }

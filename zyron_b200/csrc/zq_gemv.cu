@@ -29,7 +29,7 @@ constexpr int kGemvThreads = 256;
 // 16-byte loads per lane per column in flight), warp-shuffle reduction, exact
 // epilogue.
 // kUnroll: 16-byte weight chunks in flight per lane per column.
-template <int kType, int kM, int kCols, int kUnroll>
+template <int kType, int kM, int kCols, int kUnroll, bool kX16>
 __device__ __forceinline__ void gemv_group(int g, const uint8_t* __restrict__ panel,
                                            int N, int Kp, size_t col_bytes, int chunks, const int8_t* __restrict__ sq,
                                            const float* __restrict__ col_scale, const float (&srow)[kM],
@@ -61,7 +61,7 @@ __device__ __forceinline__ void gemv_group(int g, const uint8_t* __restrict__ pa
                     if (kType == kInt8)
                         dot16_int8<kM>(w[c][u], sq, Kp, ch * 16, acc[c]);
                     else
-                        dot16_int4<kM>(w[c][u], sq, Kp, ch * 32, acc[c]);
+                        dot16_int4<kM, kX16>(w[c][u], sq, Kp, ch * 32, acc[c]);
                 }
             }
         }
@@ -73,6 +73,7 @@ __device__ __forceinline__ void gemv_group(int g, const uint8_t* __restrict__ pa
         for (int m = 0; m < kM; ++m) {
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) acc[c][m] += __shfl_xor_sync(0xffffffffu, acc[c][m], o);
+            if (kX16) acc[c][m] >>= 4;  // the codes entered as 16 x the code
         }
         const int col = col0 + c;
         if (col < N) {
@@ -95,7 +96,7 @@ __device__ __forceinline__ void gemv_group(int g, const uint8_t* __restrict__ pa
 // quantizes them itself with the standalone quantizer's arithmetic
 // (quantization.cpp:202-212: fmaxf absmax, absmax / 127 correctly rounded,
 // round half away from zero), so a decode matmul is a single launch.
-template <int kType, int kM, int kCols, int kUnroll, bool kFused, int kThreads>
+template <int kType, int kM, int kCols, int kUnroll, bool kFused, int kThreads, bool kX16>
 __global__ void __launch_bounds__(kThreads) gemv_kernel(const uint8_t* __restrict__ panel, int N, int Kp,
                                                             const float* __restrict__ col_scale,
                                                             const int8_t* __restrict__ q,
@@ -173,8 +174,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const uint8_t* __restric
             for (int w = 1; w < kThreads / 32; ++w) t = fmaxf(t, redm[w][m]);
             srow[m] = m < M ? zq_scale_from_absmax(t, 127.0f) : 0.0f;
         }
-        // codes into shared memory, 8 per step: k order for INT8 weights,
-        // split even/odd per group of 8 to pair with INT4 nibbles
+        // codes into shared memory in k order, 8 per step
         uint32_t* s4 = reinterpret_cast<uint32_t*>(sq);
         const int kgroups = Kp >> 3;
         for (int gi = threadIdx.x; gi < kM * kgroups; gi += kThreads) {
@@ -197,15 +197,8 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const uint8_t* __restric
             uint32_t c[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) c[j] = (uint32_t)(uint8_t)(int8_t)zq_quantize_value(v[j], sm, 127);
-            const uint32_t a = c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24);
-            const uint32_t b = c[4] | (c[5] << 8) | (c[6] << 16) | (c[7] << 24);
-            if (kType == kInt8) {
-                s4[2 * gi] = a;
-                s4[2 * gi + 1] = b;
-            } else {
-                s4[2 * gi] = __byte_perm(a, b, 0x6420);
-                s4[2 * gi + 1] = __byte_perm(a, b, 0x7531);
-            }
+            s4[2 * gi] = c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24);
+            s4[2 * gi + 1] = c[4] | (c[5] << 8) | (c[6] << 16) | (c[7] << 24);
         }
     } else {
     // Stage the activation codes (rows >= M are zero).
@@ -216,20 +209,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const uint8_t* __restric
         for (int i = threadIdx.x; i < kM * words; i += kThreads) {
             const int m = i / words;
             const int wi = i - m * words;
-            if (kType == kInt8) {
-                s4[i] = m < M ? q4[(size_t)m * words + wi] : 0u;
-            } else {
-                // two source words (8 codes) -> even/odd split
-                if ((wi & 1) == 0) {
-                    uint32_t a = 0, b = 0;
-                    if (m < M) {
-                        a = q4[(size_t)m * words + wi];
-                        b = q4[(size_t)m * words + wi + 1];
-                    }
-                    s4[i] = __byte_perm(a, b, 0x6420);
-                    s4[i + 1] = __byte_perm(a, b, 0x7531);
-                }
-            }
+            s4[i] = m < M ? q4[(size_t)m * words + wi] : 0u;
         }
     }
 #pragma unroll
@@ -238,19 +218,25 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const uint8_t* __restric
     __syncthreads();
 
     for (int g = warp_global; g < groups; g += warps_total)
-        gemv_group<kType, kM, kCols, kUnroll>(g, panel, N, Kp, col_bytes, chunks, sq, col_scale, srow, bias, y, M, lane);
+        gemv_group<kType, kM, kCols, kUnroll, kX16>(g, panel, N, Kp, col_bytes, chunks, sq, col_scale, srow, bias, y, M,
+                                                    lane);
 }
 
 // Four chunks per lane: with at most 64 resident warps per SM, eight per
 // lane (one round for a 4096-code column) measured slower (fewer warps).
 template <int kType, int kM, int kCols, int kUnroll = 4, bool kFused = false>
-cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl);
+
+// INT4 codes are unpacked as 16 x the code (three operations per eight
+// codes instead of nine) whenever the dot then fits in int32.
+template <int kType, int kM, int kCols, int kUnroll, bool kFused, bool kX16>
+cudaError_t launch_gemv_x(const GemvArgs& a, cudaStream_t stream, bool pdl) {
     // The fused variant runs 512-thread blocks, so each SM reads and
     // quantizes the activation rows half as often as with 256 (512 keeps the
     // register budget of the 256-thread variants: no spills, same occupancy).
     constexpr int kThreads = kFused ? 512 : kGemvThreads;
     const size_t smem = (size_t)kM * a.Kp;
-    auto kern = gemv_kernel<kType, kM, kCols, kUnroll, kFused, kThreads>;
+    auto kern = gemv_kernel<kType, kM, kCols, kUnroll, kFused, kThreads, kX16>;
     cudaError_t e = ensure_smem_attr(kern, smem);
     if (e != cudaSuccess) return e;
     const int sms = sm_count(a.reserved_sms);
@@ -294,6 +280,14 @@ cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kern, a.panel, a.N, a.Kp, a.col_scale, a.q, a.row_scale, a.bias, a.y,
                               a.M, a.x, a.K);
+}
+
+template <int kType, int kM, int kCols, int kUnroll, bool kFused>
+cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+    if constexpr (kType == kInt4) {
+        if (int4_x16_fits(a.Kp)) return launch_gemv_x<kType, kM, kCols, kUnroll, kFused, true>(a, stream, pdl);
+    }
+    return launch_gemv_x<kType, kM, kCols, kUnroll, kFused, false>(a, stream, pdl);
 }
 
 template <int kType>

@@ -26,9 +26,12 @@ struct zq_weight {
     std::mutex mu;
     CUtensorMap tmap_b[4];
     bool tmap_ready[4] = {false, false, false, false};
-    // INT4: tensor map over the packed panel for the decode kernel.
+    // INT4: tensor map over the packed panel for the decode kernel, and per
+    // GEMM tile shape (the GEMMs unpack in shared memory).
     CUtensorMap tmap_w4;
     bool tmap_w4_ready = false;
+    CUtensorMap tmap_p[4];
+    bool tmap_p_ready[4] = {false, false, false, false};
     // Options of this weight's matmuls (zq_weight_set_option).
     std::atomic<int> opt_decode{ZQ_DECODE_AUTO};
     std::atomic<int> opt_reserved_sms{0};

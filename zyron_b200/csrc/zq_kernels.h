@@ -82,6 +82,9 @@ struct GemmArgs {
     uint32_t* err;
     int group_m;  // tile-order group size in M-tiles (0 = all M-tiles)
     int reserved_sms = 0;  // SMs left out of the persistent grid
+    // INT4 weights: tmap_b covers the packed panel [N][Kp/2] (box 64 bytes x
+    // BN or 128 rows, unswizzled) and the kernel unpacks in shared memory.
+    bool w4 = false;
 };
 
 // `zero` (n_zero ints, may be NULL) is cleared by the same launch: the
@@ -95,7 +98,6 @@ cudaError_t launch_quantize_weights(const float* w, int K, int N, int Kp, int ty
                                     float* scales, uint8_t* panel, cudaStream_t stream);
 cudaError_t launch_dequantize(const uint8_t* panel, int type, int K, int N, int Kp, const float* scales,
                               float* out, cudaStream_t stream);
-cudaError_t launch_expand_int4(const uint8_t* panel4, int N, int Kp, int8_t* panel8, cudaStream_t stream);
 
 size_t gemv_smem_bytes(int M, int Kp);
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl);

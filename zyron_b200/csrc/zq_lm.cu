@@ -157,8 +157,8 @@ __global__ void embed_kernel(const uint8_t* __restrict__ panel, int type, int Kp
     if (type == kInt8) {
         code = (int8_t)panel[(size_t)j * Kp + tok];
     } else {
-        const uint8_t b = panel[(size_t)j * (Kp >> 1) + (tok >> 1)];
-        const int nib = (tok & 1) ? (b >> 4) : (b & 0x0F);
+        const uint8_t b = panel[(size_t)j * (Kp >> 1) + panel_int4_byte(tok)];
+        const int nib = (b >> panel_int4_shift(tok)) & 0x0F;
         code = nib < 8 ? nib : nib - 16;
     }
     float v = x86_mul((float)code, scales[j]);
@@ -170,8 +170,8 @@ __global__ void embed_kernel(const uint8_t* __restrict__ panel, int type, int Kp
 // The row prologue of every decode linear: xs[0, K) holds the activation row
 // (fp32, shared memory, [K, Kp) zero).  Optional RMSNorm / LayerNorm (norm
 // 284-319) in place, then the per-row activation quantizer
-// (quantization.cpp:202-212) into qs: INT8 codes in k order, or for INT4
-// weights split even/odd per group of 8 codes to match the nibble unpack.
+// (quantization.cpp:202-212) into qs, codes in k order (the INT4 panel
+// layout unpacks into k order too).
 // Returns the row scale.  Every thread of the block calls it.
 // ---------------------------------------------------------------------------
 // One-barrier block reductions for the row prologue: the r-th reduction of a
@@ -233,12 +233,7 @@ __device__ float quantize_row(float* xs, int8_t* qs, int K, int Kp, int type, in
     const float s = zq_scale_from_absmax(m, 127.0f);
     for (int i = threadIdx.x; i < Kp; i += kNT) {
         const int8_t code = i < K ? (int8_t)zq_quantize_value(xs[i], s, 127) : (int8_t)0;
-        if (type == kInt8) {
-            qs[i] = code;
-        } else {
-            const int g = i & ~7, r = i & 7;
-            qs[g + ((r & 1) ? 4 + (r >> 1) : (r >> 1))] = code;
-        }
+        qs[i] = code;
     }
     __syncthreads();
     return s;
@@ -787,12 +782,7 @@ __device__ float quantize_row_step(float* xs, int8_t* qs, int K, int Kp, int typ
     const float s = zq_scale_from_absmax(m, 127.0f);
     for (int i = tid; i < Kp; i += kStepThreads) {
         const int8_t code = i < K ? (int8_t)zq_quantize_value(xs[i], s, 127) : (int8_t)0;
-        if (type == kInt8) {
-            qs[i] = code;
-        } else {
-            const int g = i & ~7, r = i & 7;
-            qs[g + ((r & 1) ? 4 + (r >> 1) : (r >> 1))] = code;
-        }
+        qs[i] = code;
     }
     __syncthreads();
     return s;
@@ -1234,8 +1224,8 @@ __device__ __noinline__ bool linear_phase(const StepParams& p, const PhaseArgs& 
             if (kType == kInt8) {
                 code = (int8_t)p.emb_panel[(size_t)j * p.emb_Kp + tok];
             } else {
-                const uint8_t b = p.emb_panel[(size_t)j * (p.emb_Kp >> 1) + (tok >> 1)];
-                const int nib = (tok & 1) ? (b >> 4) : (b & 0x0F);
+                const uint8_t b = p.emb_panel[(size_t)j * (p.emb_Kp >> 1) + panel_int4_byte(tok)];
+                const int nib = (b >> panel_int4_shift(tok)) & 0x0F;
                 code = nib < 8 ? nib : nib - 16;
             }
             float v = x86_mul((float)code, p.emb_scales[j]);

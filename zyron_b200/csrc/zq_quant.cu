@@ -6,7 +6,10 @@
 // (src/quantization/quantization.cpp:52-67, 155).  On the device every column
 // starts on a 16-byte boundary and is zero-padded to Kp codes:
 //   INT8: codes[n * Kp + k]                       Kp = roundup(K, 16)
-//   INT4: byte[n * Kp/2 + k/2], low nibble = even k   Kp = roundup(K, 32)
+//   INT4: Kp/2 bytes per column, Kp = roundup(K, 32), codes in groups of
+//         eight: byte 4g + j holds code 8g + j (low nibble) and 8g + j + 4
+//         (high nibble), so a 32-bit word unpacks into codes in k order
+//         without byte shuffles (panel_int4_byte, panel_int4_shift)
 // Zero codes contribute nothing to an integer dot product, so padding never
 // changes a result; it gives every TMA tensor map 16-byte strides and every
 // GEMV lane aligned 128-bit loads.
@@ -166,9 +169,8 @@ cudaError_t launch_quantize_rows(const float* x, int M, int K, int Kp, int8_t* q
 }
 
 // ---------------------------------------------------------------------------
-// INT4 repack: reference nibble stream (column c at nibble c*K) -> panel
-// layout.  Needed only when K is odd (columns straddle bytes); even K is a
-// pitched copy.  One thread per output byte.
+// INT4 repack: reference nibble stream (column c at nibble c*K, low nibble =
+// even linear index) -> panel layout.  One thread per output byte.
 // ---------------------------------------------------------------------------
 __global__ void repack_int4_kernel(const uint8_t* __restrict__ src, int K, int N, int Kp,
                                    uint8_t* __restrict__ dst) {
@@ -181,7 +183,7 @@ __global__ void repack_int4_kernel(const uint8_t* __restrict__ src, int K, int N
         uint32_t out = 0;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            const int k = 2 * j + h;
+            const int k = ((j >> 2) << 3) + (j & 3) + 4 * h;  // panel byte j: codes k (low) and k + 4 (high)
             if (k < K) {
                 const size_t lin = c * (size_t)K + k;
                 const uint8_t b = src[lin >> 1];
@@ -202,8 +204,8 @@ cudaError_t launch_repack_int4(const uint8_t* src, int K, int N, int Kp, uint8_t
     return cudaGetLastError();
 }
 
-// Panel layout -> reference payload (for save / download).  INT4 only needs
-// a kernel when K is odd; one thread per output byte of the reference stream.
+// Panel layout -> reference payload (for save / download); one thread per
+// output byte of the reference stream.
 __global__ void unpack_panel_int4_kernel(const uint8_t* __restrict__ panel, int K, int N, int Kp,
                                          uint8_t* __restrict__ dst) {
     const size_t nibbles = (size_t)K * N;
@@ -218,8 +220,8 @@ __global__ void unpack_panel_int4_kernel(const uint8_t* __restrict__ panel, int 
             if (lin < nibbles) {
                 const size_t c = lin / K;
                 const int k = (int)(lin - c * K);
-                const uint8_t b = panel[c * bpc + (k >> 1)];
-                out |= (uint32_t)((k & 1) ? (b >> 4) : (b & 0x0Fu)) << (4 * h);
+                const uint8_t b = panel[c * bpc + panel_int4_byte(k)];
+                out |= (uint32_t)((b >> panel_int4_shift(k)) & 0x0Fu) << (4 * h);
             }
         }
         dst[i] = (uint8_t)out;
@@ -294,10 +296,15 @@ __global__ void __launch_bounds__(256) quantize_panel_kernel(const float* __rest
         const uint32_t c2 = (uint8_t)tile[c][4 * tx + 2], c3 = (uint8_t)tile[c][4 * tx + 3];
         if (kType == kInt8) {
             *reinterpret_cast<uint32_t*>(panel + (size_t)nn * Kp + k) = c0 | (c1 << 8) | (c2 << 16) | (c3 << 24);
-        } else {
-            // byte k/2 holds codes k (low nibble) and k+1 (high nibble)
-            const uint32_t b0 = (c0 & 0x0Fu) | ((c1 & 0x0Fu) << 4), b1 = (c2 & 0x0Fu) | ((c3 & 0x0Fu) << 4);
-            *reinterpret_cast<uint16_t*>(panel + (size_t)nn * (Kp >> 1) + (k >> 1)) = (uint16_t)(b0 | (b1 << 8));
+        } else if ((tx & 1) == 0) {
+            // codes k .. k+7 of the group: byte j holds codes k+j (low) and
+            // k+j+4 (high nibble)
+            const int8_t* t = &tile[c][4 * tx];
+            uint32_t word = 0;
+#pragma unroll
+            for (int b = 0; b < 4; ++b)
+                word |= ((uint32_t)((uint8_t)t[b] & 0x0Fu) | ((uint32_t)((uint8_t)t[b + 4] & 0x0Fu) << 4)) << (8 * b);
+            *reinterpret_cast<uint32_t*>(panel + (size_t)nn * (Kp >> 1) + (k >> 1)) = word;
         }
     }
 }
@@ -344,8 +351,9 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const uint8_t* __restri
                 a = (int8_t)(pair & 0xFF);
                 b = (int8_t)(pair >> 8);
             } else {
-                const uint8_t byte = panel[(size_t)nn * (Kp >> 1) + (k >> 1)];
-                const int lo = byte & 0x0F, hi = byte >> 4;
+                const uint8_t* col = panel + (size_t)nn * (Kp >> 1);
+                const int lo = (col[panel_int4_byte(k)] >> panel_int4_shift(k)) & 0x0F;
+                const int hi = (col[panel_int4_byte(k + 1)] >> panel_int4_shift(k + 1)) & 0x0F;
                 a = (int8_t)(lo < 8 ? lo : lo - 16);
                 b = (int8_t)(hi < 8 ? hi : hi - 16);
             }
@@ -371,35 +379,6 @@ cudaError_t launch_dequantize(const uint8_t* panel, int type, int K, int N, int 
         dequantize_kernel<kInt8><<<g, dim3(32, 8), 0, stream>>>(panel, K, N, Kp, scales, out);
     else
         dequantize_kernel<kInt4><<<g, dim3(32, 8), 0, stream>>>(panel, K, N, Kp, scales, out);
-    return cudaGetLastError();
-}
-
-}  // namespace zq
-
-namespace zq {
-
-// ---------------------------------------------------------------------------
-// INT4 panel -> INT8 panel with the same Kp (two codes per input byte), used
-// by the prefill GEMM for INT4 weights.  Each thread expands 16 packed bytes
-// into 32 codes with the shared nibble unpack.
-// ---------------------------------------------------------------------------
-__global__ void expand_int4_kernel(const uint4* __restrict__ src, size_t chunks, uint4* __restrict__ dst) {
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < chunks;
-         i += (size_t)gridDim.x * blockDim.x) {
-        uint4 a, b;
-        zq_expand_int4x32(src[i], a, b);
-        dst[2 * i] = a;
-        dst[2 * i + 1] = b;
-    }
-}
-
-cudaError_t launch_expand_int4(const uint8_t* panel4, int N, int Kp, int8_t* panel8, cudaStream_t stream) {
-    const size_t chunks = (size_t)N * (size_t)(Kp >> 1) / 16;
-    const int threads = 256;
-    const size_t want = (chunks + threads - 1) / threads;
-    const int blocks = (int)(want < 148 * 32 ? want : 148 * 32);
-    expand_int4_kernel<<<blocks > 0 ? blocks : 1, threads, 0, stream>>>(
-        reinterpret_cast<const uint4*>(panel4), chunks, reinterpret_cast<uint4*>(panel8));
     return cudaGetLastError();
 }
 

@@ -21,15 +21,15 @@
 // Work split (stream-K): the (column block, k-block) iterations are cut into
 // equal contiguous ranges, one per CTA and one CTA per SM, so every SM
 // streams the same number of weight bytes whatever N and K are.  A column
-// block whose k-range spans several CTAs is finished by the one that starts
-// its share last: each takes an arrival ticket when it starts its share; the
-// others write their int32 partial sums to the workspace and count them as
-// published; the last adds them (integer addition, exact in any order) and
-// applies the epilogue.  It waits only for CTAs that arrived before it, which
-// need nothing but their own MMAs to publish, so the wait always ends, and it
-// gathers their sums while its own MMAs are still running.  The counters are
-// zeroed by the kernel launched just before this one (the activation
-// quantizer, or a zeroing kernel).
+// block whose k-range spans several CTAs is finished by the one that
+// completes its share last: every sharer writes its int32 partial sums to
+// the workspace and then counts its share done; the CTA whose count
+// completes the block adds the others' sums to its own (integer addition,
+// exact in any order) and applies the epilogue.  No CTA ever waits for
+// another.  (Choosing the finisher by arrival instead left CTAs waiting up to
+// 10 us for a CTA that shares the block from the middle of its range.)  The
+// counters are zeroed by the kernel launched just before this one (the
+// activation quantizer, or a zeroing kernel).
 //
 // INT4 weights arrive as packed [128 columns][64 bytes] tiles; four unpack
 // warps sign-extend each into the 128-byte-swizzled int8 tile the MMA reads.
@@ -64,7 +64,7 @@ struct SkCfg<kInt8> {
 template <>
 struct SkCfg<kInt4> {
     static constexpr int kStages = 6;
-    static constexpr int kThreads = 320;
+    static constexpr int kThreads = 192 + 32 * kStages;  // one unpack warp per stage
     static constexpr int kWBytes = kSkBlockN * kSkKBlock / 2;  // packed, row-major [128][64]
     static constexpr int kXBytes = kSkRows * kSkKBlock;
     static constexpr int kConvBytes = kSkBlockN * kSkKBlock;  // unpacked int8, swizzled
@@ -114,7 +114,7 @@ __global__ void __launch_bounds__(SkCfg<kType>::kThreads, 1)
                   int N, int KB, long long T, const float* __restrict__ row_scale,
                   const float* __restrict__ col_scale, const float* __restrict__ bias, float* __restrict__ y,
                   int* __restrict__ counters, int* __restrict__ partials, uint32_t* __restrict__ err,
-                  int wait_extra, unsigned long long peer_limit_ns) {
+                  int wait_extra, unsigned long long peer_limit_ns, int x16) {
     using C = SkCfg<kType>;
     constexpr int S = C::kStages;
     constexpr uint32_t kTmemCols = 32;  // two 16-column accumulators
@@ -143,7 +143,7 @@ __global__ void __launch_bounds__(SkCfg<kType>::kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&conv_full[s], 4);
+            mbar_init(&conv_full[s], 1);  // the stage's unpack warp
             mbar_init(&empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -267,45 +267,6 @@ __global__ void __launch_bounds__(SkCfg<kType>::kThreads, 1)
             const long long bk0 = (long long)b * KB, bk1 = bk0 + KB;
             const bool whole = t == bk0 && it1 >= bk1;
             t = it1 < bk1 ? it1 : bk1;
-            // A block shared with other CTAs: take the arrival ticket now,
-            // before this CTA's share is computed.  The last to arrive
-            // finishes the block.  The others arrived first and need nothing
-            // but their own MMAs to publish their shares, so the finisher
-            // gathers them while its own MMAs still run, and after its last
-            // MMA only a TMEM load, an add and the stores remain.
-            int* arrived = counters + b * 8 + q;
-            int* published = arrived + 4;
-            bool finisher = false, ok = true;
-            uint32_t other[kSkRows];
-#pragma unroll
-            for (int m = 0; m < kSkRows; ++m) other[m] = 0u;
-            if (!whole) {
-                int ticket = 0;
-                if (lane == 0) ticket = atomicAdd(arrived, 1);
-                ticket = __shfl_sync(0xffffffffu, ticket, 0);
-                const int g0 = sk_owner(bk0, T, G), g1 = sk_owner(bk1 - 1, T, G);
-                finisher = ticket == g1 - g0;
-                if (finisher) {
-                    int fine = 1;
-                    if (lane == 0)
-                        fine = wait_count_bounded(published, g1 - g0 + wait_extra, err, kDevErrTimeoutPeer,
-                                                  peer_limit_ns)
-                                   ? 1
-                                   : 0;
-                    ok = __shfl_sync(0xffffffffu, fine, 0) != 0;
-                    if (ok) {
-                        (void)ld_acquire_gpu(published);  // orders this lane's loads after the publications
-                        for (int h = g0; h <= g1; ++h) {
-                            if (h == g) continue;
-                            const int hs = sk_start(h, T, G) / KB == b ? 0 : 1;
-                            const int* p = partials + (size_t)(h * 2 + hs) * M * kSkBlockN + col_local;
-#pragma unroll
-                            for (int m = 0; m < kSkRows; ++m)
-                                if (m < M) other[m] += (uint32_t)__ldcg(p + (size_t)m * kSkBlockN);
-                        }
-                    }
-                }
-            }
             if (!mbar_wait_bounded(&tfull[acc], acc_phase, err, kDevErrTimeoutEpilogue)) break;
             tmem_fence_after();
             uint32_t r[kSkRows];
@@ -316,21 +277,47 @@ __global__ void __launch_bounds__(SkCfg<kType>::kThreads, 1)
             if (++acc == 2) acc = 0, acc_phase ^= 1u;
 
             if (!whole) {
-                if (!finisher) {
-                    // publish this CTA's share of the block
-                    const int slot = b == first_b ? 0 : 1;
-                    int* mine = partials + (size_t)(g * 2 + slot) * M * kSkBlockN + col_local;
+                // A block shared with other CTAs: publish this CTA's exact
+                // int32 share, then count it; the CTA whose count completes
+                // the block adds the others' shares to its own and writes the
+                // output.  Nobody waits: the block is finished by whichever
+                // CTA finishes its share last.
+                const int slot = b == first_b ? 0 : 1;
+                int* mine = partials + (size_t)(g * 2 + slot) * M * kSkBlockN + col_local;
+#pragma unroll
+                for (int m = 0; m < kSkRows; ++m)
+                    if (m < M) mine[(size_t)m * kSkBlockN] = (int)r[m];
+                __threadfence();
+                __syncwarp();
+                int* done = counters + b * 8 + q;
+                const int g0 = sk_owner(bk0, T, G), g1 = sk_owner(bk1 - 1, T, G);
+                int prior = 0;
+                if (lane == 0) prior = atomicAdd(done, 1);
+                prior = __shfl_sync(0xffffffffu, prior, 0);
+                if (prior != g1 - g0) continue;  // another CTA's share is still running
+                if (wait_extra > 0) {
+                    // failure-path test only: wait for shares that do not exist
+                    int fine = 1;
+                    if (lane == 0)
+                        fine = wait_count_bounded(done, g1 - g0 + 1 + wait_extra, err, kDevErrTimeoutPeer,
+                                                  peer_limit_ns)
+                                   ? 1
+                                   : 0;
+                    if (__shfl_sync(0xffffffffu, fine, 0) == 0) continue;
+                }
+                __threadfence();  // the other shares were published before their counts
+                for (int h = g0; h <= g1; ++h) {
+                    if (h == g) continue;
+                    const int hs = sk_start(h, T, G) / KB == b ? 0 : 1;
+                    const int* p = partials + (size_t)(h * 2 + hs) * M * kSkBlockN + col_local;
 #pragma unroll
                     for (int m = 0; m < kSkRows; ++m)
-                        if (m < M) mine[(size_t)m * kSkBlockN] = (int)r[m];
-                    __threadfence();
-                    __syncwarp();
-                    if (lane == 0) atomicAdd(published, 1);
-                    continue;
+                        if (m < M) r[m] += (uint32_t)__ldcg(p + (size_t)m * kSkBlockN);
                 }
-                if (!ok) continue;
+            }
+            if (x16) {
 #pragma unroll
-                for (int m = 0; m < kSkRows; ++m) r[m] += other[m];
+                for (int m = 0; m < kSkRows; ++m) r[m] = (uint32_t)((int32_t)r[m] >> 4);  // 16 x the dot, exactly
             }
             const int n = b * kSkBlockN + col_local;
             if (n < N) {
@@ -348,25 +335,32 @@ __global__ void __launch_bounds__(SkCfg<kType>::kThreads, 1)
             }
         }
     } else if constexpr (kType == kInt4) {
-        // Unpack: 128 threads turn the packed [128][64 B] tile into the
-        // swizzled int8 [128][128 B] tile.  Thread i takes 16-byte chunks
-        // i, i+128, ...: row = chunk / 4, codes 32 * (chunk % 4) .. +31, which
-        // land in the row's logical 16-byte chunks 2c and 2c+1, stored at
-        // physical chunk (logical ^ row % 8) -- the 128-byte swizzle.
-        const int tid = threadIdx.x - 192;
-        int stage = 0;
+        // Unpack: warp 6 + s owns stage s and turns its packed [128][64 B]
+        // tile into the swizzled int8 [128][128 B] tile at every phase.  Lane
+        // i takes 16-byte chunks i, i + 32, ...: row = chunk / 4, codes
+        // 32 * (chunk % 4) .. +31 (in k order: the panel layout), which land in
+        // the row's logical 16-byte chunks 2c and 2c+1, stored at physical
+        // chunk (logical ^ row % 8) -- the 128-byte swizzle.  One warp per
+        // stage: the generic-to-async proxy fence before each release then
+        // overlaps across stages (four warps sharing every stage paid it
+        // stage after stage, slower than the weight stream).  With x16 the
+        // codes enter as 16 x the code and the epilogue shifts the sums back.
+        const int u = warp - 6;
         uint32_t phase = 0;
-        for (long long t = it0; t < it1; ++t) {
-            if (!mbar_wait_bounded(&full[stage], phase, err, kDevErrTimeoutMma)) break;
-            const uint8_t* raw = smem + stage * C::kStageBytes;
-            uint8_t* conv = smem + stage * C::kStageBytes + C::kWBytes + C::kXBytes;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int idx = tid + 128 * j;
+        for (long long t = it0 + u; t < it1; t += S) {
+            if (!mbar_wait_bounded(&full[u], phase, err, kDevErrTimeoutMma)) break;
+            const uint8_t* raw = smem + u * C::kStageBytes;
+            uint8_t* conv = smem + u * C::kStageBytes + C::kWBytes + C::kXBytes;
+#pragma unroll 4
+            for (int j = 0; j < 16; ++j) {
+                const int idx = lane + 32 * j;
                 const int row = idx >> 2, c = idx & 3;
                 const uint4 v = *reinterpret_cast<const uint4*>(raw + idx * 16);
                 uint4 lo, hi;
-                zq_expand_int4x32(v, lo, hi);
+                if (x16)
+                    zq_expand_int4x32_x16(v, lo, hi);
+                else
+                    zq_expand_int4x32(v, lo, hi);
                 uint8_t* rp = conv + row * 128;
                 const int sw = row & 7;
                 *reinterpret_cast<uint4*>(rp + (((2 * c) ^ sw) << 4)) = lo;
@@ -375,8 +369,8 @@ __global__ void __launch_bounds__(SkCfg<kType>::kThreads, 1)
             // generic-proxy writes become visible to the tensor core's reads
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
-            if (lane == 0) mbar_arrive(&conv_full[stage]);
-            if (++stage == S) stage = 0, phase ^= 1u;
+            if (lane == 0) mbar_arrive(&conv_full[u]);
+            phase ^= 1u;
         }
     }
 
@@ -418,7 +412,8 @@ cudaError_t launch_skinny_t(const SkinnyArgs& a, cudaStream_t stream, bool pdl) 
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kern, *a.tmap_w, *a.tmap_x, a.M, a.N, KB, T, a.row_scale, a.col_scale, a.bias,
                               a.y, a.counters, a.partials, a.err, a.wait_extra,
-                              (unsigned long long)(a.peer_limit_ns ? a.peer_limit_ns : 4000000000ull));
+                              (unsigned long long)(a.peer_limit_ns ? a.peer_limit_ns : 4000000000ull),
+                              (kType == kInt4 && int4_x16_fits(a.Kp)) ? 1 : 0);
 }
 
 }  // namespace

@@ -135,7 +135,7 @@ zq_status zq_quantize_rows(const float* x, size_t m, size_t k, int8_t* q, size_t
                            void* stream);
 
 /* Row length of the activation codes zq_matmul_codes expects for `w`
- * (rows rounded up to 16 codes for INT8, 32 for INT4). */
+ * (K rounded up to a multiple of 128 codes). */
 size_t zq_weight_padded_k(const zq_weight* w);
 
 /* quantization::matmul (quantization.cpp:177-238) followed, when bias is not

@@ -80,10 +80,10 @@ def test_python_mirror_errors(native_lib):
 
 
 def test_device_layout_constants():
-    # The panel layout pads K to 16 codes (INT8) / 32 codes (INT4); workspace
-    # sizes follow from it.  Restated here from csrc/zq_kernels.h.
+    # The panel layout pads K to whole 128-code k-blocks for both types;
+    # workspace sizes follow from it.  Restated here from csrc/zq_kernels.h.
     def padded(t, k):
-        return (k + 15) // 16 * 16 if t == 1 else (k + 31) // 32 * 32
+        return (k + 127) // 128 * 128
 
-    assert padded(1, 1) == 16 and padded(1, 16) == 16 and padded(1, 17) == 32
-    assert padded(2, 1) == 32 and padded(2, 33) == 64
+    assert padded(1, 1) == 128 and padded(1, 128) == 128 and padded(1, 129) == 256
+    assert padded(2, 1) == 128 and padded(2, 4096) == 4096 and padded(2, 11008) == 11008

@@ -3,9 +3,11 @@ oracle, through both decode kernels: the tcgen05 kernel (weights streamed by
 TMA, work split evenly over the SMs with exact int32 partial sums) and the
 dp4a warp-per-column GEMV (M <= 8).
 
-The shapes stress the split: N not a multiple of the 128-column block, K not
+The shapes stress the split: N not a multiple of the 64-column block, K not
 a multiple of the 128-code k-block, one column block shared by 64 CTAs,
-blocks of a single k-block, and more CTAs than column blocks.
+blocks of a single k-block, more CTAs than column blocks, and more column
+blocks than CTAs (shared pieces streamed first, whole blocks after, each
+shared block finished by its latest share).
 """
 import ctypes as C
 
@@ -21,7 +23,7 @@ TENSOR_CORE, CUDA_CORE = 1, 2
 DECODE_SHAPES = [
     (1, 1, 1), (1, 64, 7), (1, 4096, 1000), (2, 31, 33), (3, 129, 255), (4, 8192, 64), (5, 1000, 300),
     (7, 12288, 129), (8, 4096, 1100), (8, 33, 1), (9, 200, 130), (12, 3000, 777), (16, 4096, 2048),
-    (16, 100, 5000),
+    (16, 100, 5000), (8, 4096, 11008), (2, 384, 20000),
 ]
 
 
@@ -158,7 +160,7 @@ def test_bounded_wait_timeout_reports_and_recovers(zb, qt):
     from zyron_b200 import _lib
 
     L = zb._lib.lib()
-    M, K, N = 8, 4096, 11008  # 86 column blocks over the SMs: many are split
+    M, K, N = 8, 4096, 11008  # 172 column blocks over the SMs: many are split
     x, w, b = _case(M, K, N, qt)
     pay, sc = O.quantize_weights(w, qt)
     W = zb.QuantizedMatrix.from_parts(qt, K, N, sc, pay)

@@ -217,6 +217,34 @@ zq_status encode_packed_int4(CUtensorMap* map, const void* base, size_t cols, in
     return ZQ_OK;
 }
 
+// 3-D view of a K-major [rows][Kp] panel (Kp a multiple of 128 codes) for
+// the decode kernel: (bytes within a k-block row, rows, k-block), box
+// kblock_bytes x box_rows x zq::skinny_kgroup().  INT8 panels and activation
+// codes: 128 bytes per k-block row, 128-byte swizzle; packed INT4 panels: 64
+// bytes, unswizzled (the kernel unpacks them).
+zq_status encode_decode_view(CUtensorMap* map, const void* base, size_t rows, int Kp, int kblock_bytes,
+                             int box_rows) {
+    zq_status s = get_encoder();
+    if (s != ZQ_OK) return s;
+    if (Kp % 128 != 0) return fail(ZQ_ERR_RUNTIME, "zyron_b200: decode view needs whole 128-code k-blocks");
+    const int row_bytes = kblock_bytes == 128 ? Kp : Kp / 2;
+    cuuint64_t dims[3] = {(cuuint64_t)kblock_bytes, (cuuint64_t)rows, (cuuint64_t)(Kp / 128)};
+    cuuint64_t strides[2] = {(cuuint64_t)row_bytes, (cuuint64_t)kblock_bytes};
+    cuuint32_t box[3] = {(cuuint32_t)kblock_bytes, (cuuint32_t)box_rows, (cuuint32_t)zq::skinny_kgroup()};
+    cuuint32_t estr[3] = {1u, 1u, 1u};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          kblock_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        char buf[160];
+        std::snprintf(buf, sizeof buf, "zyron_b200: cuTensorMapEncodeTiled failed (%d) rows=%zu Kp=%d (decode view)",
+                      (int)r, rows, Kp);
+        return fail(ZQ_ERR_CUDA, buf);
+    }
+    return ZQ_OK;
+}
+
 int tile_index(int block_n) {
     return block_n == zq::kPairBlockN ? 3 : (block_n == 256 ? 2 : (block_n == 128 ? 1 : 0));
 }
@@ -571,28 +599,19 @@ zq_status run_codes_out(const zq_weight* w, const int8_t* codes, const float* rs
         int* partials = reinterpret_cast<int*>(scratch + align256((size_t)zq::skinny_counter_words(N) * sizeof(int)));
         if (!pdl) ZQ_CUDA(zq::launch_zero_words(counters, zq::skinny_counter_words(N), st));
         CUtensorMap tmap_x;
-        s = encode_kmajor(&tmap_x, codes, m, Kp, 16);
+        s = encode_decode_view(&tmap_x, codes, m, Kp, 128, 16);
         if (s != ZQ_OK) return s;
         const CUtensorMap* tmap_w = nullptr;
         {
             zq_weight* mw = const_cast<zq_weight*>(w);
             std::lock_guard<std::mutex> lk(mw->mu);
-            if (w->type == ZQ_TYPE_INT8) {
-                const int ti = tile_index(zq::kPairBlockN);  // 128 columns x 128 B, swizzled
-                if (!mw->tmap_ready[ti]) {
-                    s = encode_kmajor(&mw->tmap_b[ti], w->panel, w->N, Kp, box_rows_b(zq::kPairBlockN));
-                    if (s != ZQ_OK) return s;
-                    mw->tmap_ready[ti] = true;
-                }
-                tmap_w = &mw->tmap_b[ti];
-            } else {
-                if (!mw->tmap_w4_ready) {
-                    s = encode_packed_int4(&mw->tmap_w4, w->panel, w->N, Kp);
-                    if (s != ZQ_OK) return s;
-                    mw->tmap_w4_ready = true;
-                }
-                tmap_w = &mw->tmap_w4;
+            if (!mw->tmap_dec_ready) {
+                s = encode_decode_view(&mw->tmap_dec, w->panel, w->N, Kp, w->type == ZQ_TYPE_INT8 ? 128 : 64,
+                                       zq::skinny_block_n());
+                if (s != ZQ_OK) return s;
+                mw->tmap_dec_ready = true;
             }
+            tmap_w = &mw->tmap_dec;
         }
         zq::SkinnyArgs a{w->type, tmap_w, &tmap_x, M, N, Kp, rs, w->scales, bias, y, counters, partials, err};
         a.reserved_sms = reserved;

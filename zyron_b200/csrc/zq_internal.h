@@ -22,16 +22,19 @@ struct zq_weight {
     float* scales = nullptr;   // [N]
     size_t panel_bytes = 0;
     // Tensor maps over the INT8 panel, one per GEMM tile shape (64/128/256
-    // columns, and the 2-SM pair tile).
+    // columns, and the 2-SM pair tile); the decode kernel reads 64-column
+    // boxes.
     std::mutex mu;
     CUtensorMap tmap_b[4];
     bool tmap_ready[4] = {false, false, false, false};
-    // INT4: tensor map over the packed panel for the decode kernel, and per
-    // GEMM tile shape (the GEMMs unpack in shared memory).
-    CUtensorMap tmap_w4;
-    bool tmap_w4_ready = false;
+    // INT4: tensor maps over the packed panel per tile shape (the kernels
+    // unpack in shared memory).
     CUtensorMap tmap_p[4];
     bool tmap_p_ready[4] = {false, false, false, false};
+    // The decode kernel's 3-D view of the panel: boxes of several k-blocks
+    // of 64 columns.
+    CUtensorMap tmap_dec;
+    bool tmap_dec_ready = false;
     // Options of this weight's matmuls (zq_weight_set_option).
     std::atomic<int> opt_decode{ZQ_DECODE_AUTO};
     std::atomic<int> opt_reserved_sms{0};

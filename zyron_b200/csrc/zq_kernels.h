@@ -38,9 +38,14 @@ constexpr int kGemvMaxRows = 8;
 // GemmArgs::block_n value selecting the 2-SM (cluster pair) 256 x 256 tile kernel.
 constexpr int kPairBlockN = 512;
 
-// Codes per column on the device, rounded up so every column starts on a
-// 16-byte boundary (INT8: 16 codes, INT4: 32 codes).
-inline int padded_k(int type, int K) { return type == 1 ? (K + 15) / 16 * 16 : (K + 31) / 32 * 32; }
+// Codes per column on the device, rounded up to whole 128-code k-blocks (the
+// padding codes are zero): every column starts on a 16-byte boundary, and the
+// decode kernel's 3-D TMA boxes, several k-blocks deep, never cross from one
+// column into the next.
+inline int padded_k(int type, int K) {
+    (void)type;
+    return (K + 127) / 128 * 128;
+}
 
 struct GemvArgs {
     int type;
@@ -107,15 +112,15 @@ constexpr int kSkinnyMaxRows = 16;
 constexpr int kSkinnyMaxCtas = 256;
 struct SkinnyArgs {
     int type;
-    const CUtensorMap* tmap_w;  // INT8: [N][Kp] box 128 B x 128 rows, 128B swizzle; INT4: [N][Kp/2] box 64 B x 128 rows
-    const CUtensorMap* tmap_x;  // codes [M][Kp], box 128 B x 16 rows, 128B swizzle
+    const CUtensorMap* tmap_w;  // 3-D panel view (k-block row bytes, N, Kp/128), box x 64 columns x skinny_kgroup()
+    const CUtensorMap* tmap_x;  // 3-D view of the codes [M][Kp], box 128 B x 16 rows x skinny_kgroup(), swizzled
     int M, N, Kp;
     const float* row_scale;
     const float* col_scale;
     const float* bias;
     float* y;
     int* counters;  // skinny_counter_words(N), zero when the kernel starts
-    int* partials;  // kSkinnyMaxCtas * 2 * M * 128
+    int* partials;  // kSkinnyMaxCtas * 2 * M * skinny_block_n()
     uint32_t* err;
     // Failure-path testing only (0 otherwise): a split block's finisher waits
     // for wait_extra more partial sums than exist, giving up after
@@ -124,6 +129,10 @@ struct SkinnyArgs {
     uint64_t peer_limit_ns = 0;
     int reserved_sms = 0;  // SMs left out of the grid
 };
+// Weight columns per decode tile and the tiles of N columns.
+int skinny_block_n();
+// k-blocks per decode iteration (the depth of its 3-D TMA boxes).
+int skinny_kgroup();
 int skinny_blocks(int N);
 // Arrival and publication counters of the split blocks (8 per block).
 int skinny_counter_words(int N);

@@ -198,6 +198,27 @@ __device__ __forceinline__ float row_max(float v, float* red, int r) {
     return t;
 }
 
+// Copies the activation row x[0, K) into xs (zero up to Kp) with every
+// thread's loads issued before its first store: a row of a few thousand
+// floats then costs one L2 round trip instead of one per strided element.
+template <int kNT>
+__device__ __forceinline__ void load_row(const float* __restrict__ x, int K, int Kp, float* xs) {
+    constexpr int kBatch = 8;
+    for (int i0 = 0; i0 < Kp; i0 += kBatch * kNT) {
+        float v[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int i = i0 + threadIdx.x + u * kNT;
+            v[u] = i < K ? __ldcg(x + i) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int i = i0 + threadIdx.x + u * kNT;
+            if (i < Kp) xs[i] = v[u];
+        }
+    }
+}
+
 // `red` holds 96 floats.
 template <int kNT>
 __device__ float quantize_row(float* xs, int8_t* qs, int K, int Kp, int type, int pro, const float* __restrict__ nw,
@@ -329,7 +350,7 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const float* __restric
     __shared__ float red[96];
     __shared__ unsigned long long blk_key;
     __shared__ int blk_nan;
-    constexpr int kPre = 4;  // 16-byte weight chunks per lane fetched before the dependency wait
+    constexpr int kPre = 8;  // 16-byte weight chunks per lane fetched before the dependency wait (K <= 4096 INT8)
     const int lane = threadIdx.x & 31;
     const int warps_total = gridDim.x * (kThreads / 32);
     const size_t cb = kType == kInt8 ? (size_t)Kp : (size_t)(Kp >> 1);
@@ -363,7 +384,7 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const float* __restric
         merge_rows<kThreads>(merge, nchunk, xs, mls, mls + 2 * merge.heads * merge.n_chunks_max);
         for (int i = K + threadIdx.x; i < Kp; i += kThreads) xs[i] = 0.0f;
     } else {
-        for (int i = threadIdx.x; i < Kp; i += kThreads) xs[i] = i < K ? __ldcg(x + i) : 0.0f;
+        load_row<kThreads>(x, K, Kp, xs);
     }
     __syncthreads();
     if (kEpi == kEpiLogits && threadIdx.x == 0) blk_key = 0ull, blk_nan = 0;
@@ -1234,7 +1255,7 @@ __device__ __noinline__ bool linear_phase(const StepParams& p, const PhaseArgs& 
             if (blockIdx.x == 0) p.h[j] = v;  // residual stream, read after the next barriers
         }
     } else if (a.row_src == kRowGlobal) {
-        for (int j = tid; j < a.K; j += kStepThreads) xs[j] = __ldcg(a.row + j);
+        load_row<kStepThreads>(a.row, a.K, a.K, xs);
     } else {
         merge_context(p, nchunk, xs, m.mls, m.invl);
     }

@@ -205,7 +205,8 @@ def run_ours(args, rank, world, local_rank):
     x = torch.randn((M, K), generator=g, device=dev, dtype=torch.float32)
     g.manual_seed(1000 + rank)
     w_f32 = torch.randn((K, n_loc), generator=g, device=dev, dtype=torch.float32).mul_(0.02)
-    W = zb.quantize(w_f32, zb.Type.Int8)
+    int4 = args.weight_type == "int4"
+    W = zb.quantize(w_f32, zb.Type.Int4 if int4 else zb.Type.Int8)
     del w_f32
     torch.cuda.empty_cache()
     y = torch.empty((M, n_loc), dtype=torch.float32, device=dev)
@@ -354,11 +355,13 @@ def run_ours(args, rank, world, local_rank):
             cpu = {"value": None, "unit": UNIT, "cores": None, "kind": None, "sample": f"failed: {exc}"}
 
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "metric": METRIC.replace("int8", "int4").replace("INT8", "INT4") if int4 else METRIC, "value": value,
+        "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": WORKLOAD if (M, K, N) == (M_ROWS, K_DIM, N_COLS) else f"prefill_int8_gemm_M{M}_K{K}_N{N}",
-                   "M": M, "K": K, "N": N, "weight": "int8 per-column (device quantize)",
+        "config": {"workload": WORKLOAD if (M, K, N) == (M_ROWS, K_DIM, N_COLS) and not int4
+                   else f"prefill_{args.weight_type}_gemm_M{M}_K{K}_N{N}",
+                   "M": M, "K": K, "N": N, "weight": f"{args.weight_type} per-column (device quantize)",
                    "x": "N(0,1) fp32", "w": "N(0,0.02) fp32 before quantization",
                    "parallelism": f"column-sharded x{world}" + (
                        " + all-gather of outputs fused into the matmul epilogue (NVLink peer stores)"
@@ -366,7 +369,9 @@ def run_ours(args, rank, world, local_rank):
                    "l2": "inputs larger than L2 (x 256 MiB, W 512 MiB, y 2 GiB); no flush"},
         "gpu_launches": (2 * args.steps),
         "clocks": sampler.summary(),
-        "roofline": {"bound": "tensor", "kernel": "gemm_i8_pair_kernel (tcgen05.mma.cta_group::2.kind::i8, 2-SM 256x256 tiles)",
+        "roofline": {"bound": "tensor",
+                     "kernel": "gemm_i8_pair_kernel (tcgen05.mma.cta_group::2.kind::i8, 2-SM 256x256 tiles"
+                               + (", packed INT4 tiles unpacked in shared memory)" if int4 else ")"),
                      "achieved": gemm_tops, "peak": int8_peak, "unit": UNIT, "frac": gemm_tops / int8_peak,
                      "peak_source": peak_src, "traffic": traffic,
                      "ms_per_launch": gemm_ms, "ops_per_launch": ops(M, n_loc, K)},
@@ -886,6 +891,8 @@ def main():
                     help="skip the decode GEMV and LM decode figures after the headline (profiling runs)")
     ap.add_argument("--once", action="store_true",
                     help="gemv / small / qlm workloads: a few untimed calls of the kernels (for ncu captures)")
+    ap.add_argument("--weight-type", choices=["int8", "int4"], default="int8",
+                    help="prefill workload: weight type (the headline configuration is INT8)")
     ap.add_argument("--shape", type=lambda v: tuple(int(t) for t in v.split(",")),
                     default=(M_ROWS, K_DIM, N_COLS), help="M,K,N override for small profiling cases")
     args = ap.parse_args()

@@ -818,6 +818,23 @@ zq_status zq_matmul_multi(const zq_weight* w, const float* x, size_t m, const fl
     }
     zq_status s = validate_matmul(w, m, x, out.base[0], workspace, workspace_bytes);
     if (s != ZQ_OK) return s;
+    if (out.vec && n_dst > 1) {
+        // every destination 16-byte aligned at the column offset, pitch a
+        // multiple of 16 bytes: the epilogue can store with TMA
+        s = get_encoder();
+        if (s != ZQ_OK) return s;
+        for (int i = 0; i < n_dst; ++i) {
+            cuuint64_t dims[2] = {(cuuint64_t)w->N, (cuuint64_t)m};
+            cuuint64_t strides[1] = {(cuuint64_t)(ldy * sizeof(float))};
+            cuuint32_t box[2] = {32u, 32u};
+            cuuint32_t estr[2] = {1u, 1u};
+            CUresult r = g_encode(&out.map[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dsts[i] + col_offset, dims, strides,
+                                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (r != CUDA_SUCCESS) return fail(ZQ_ERR_CUDA, "zyron_b200: cuTensorMapEncodeTiled failed (output view)");
+        }
+        out.tma = 1;
+    }
     return matmul_in_workspace_out(w, x, m, bias, out, static_cast<uint8_t*>(workspace), as_stream(stream));
 }
 

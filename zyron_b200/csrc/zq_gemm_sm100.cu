@@ -76,7 +76,21 @@ __device__ __forceinline__ int32_t acc_of(uint32_t r, int shift) { return (int32
 // accumulators around in shared memory so that global stores are 128-byte
 // row segments (coalesced in HBM, large packets over NVLink).
 constexpr int kEpiPitch = 32;  // floats per staged row; float4 slots XOR-swizzled by row
-constexpr int kEpiBytes = 4 * 32 * kEpiPitch * 4;
+constexpr int kEpiBlockFloats = 32 * kEpiPitch;      // one staged 32 x 32 block (4 KiB)
+constexpr int kEpiBytes = 4 * 2 * kEpiBlockFloats * 4;  // two blocks per epilogue warp
+
+// TMA store of one staged 32 x 32 fp32 block (128-byte swizzle, the staging
+// layout) through an output view, in a bulk group of this thread.
+__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+                 "r"(smem_u32(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// At most one bulk group of this thread still reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+// Every bulk group of this thread complete (its global writes performed).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // Ring stage: [A 128x128 | B BNx128 int8, swizzled] (INT8) or [A] (INT4);
 // INT4 adds kSlots slots of [unpacked B BNx128, swizzled | packed B BNx64].
@@ -89,9 +103,11 @@ struct Smem {
     static constexpr int kSlotOffset = STAGES * kStageBytes;
     static constexpr int kSlotBytes = kBBytes + kPBytes;
     static constexpr int kSlotsBytes = kW4 ? kSlots * kSlotBytes : 0;
-    static constexpr int kBarrierBytes = (8 * (2 * STAGES + 4 * kSlots + 6) + 16 + 127) / 128 * 128;  // keeps the staging area aligned
+    // rounded to 1 KiB: the staging area after it takes 128-byte-swizzled TMA stores
+    static constexpr int kBarrierBytes = (8 * (2 * STAGES + 4 * kSlots + 6) + 16 + 1023) / 1024 * 1024;
     // staging area last: it is only allocated when the output has peers
     static constexpr int kTotal = 1024 /*alignment slack*/ + kSlotOffset + kSlotsBytes + kBarrierBytes;
+    static_assert(kTotal + kEpiBytes <= 227 * 1024, "shared memory of the gathering kernel");
 };
 
 // Unpack of one stage's packed INT4 tile (rows x 64 bytes of the panel
@@ -141,11 +157,20 @@ __device__ __forceinline__ void unpack_stage(const uint8_t* __restrict__ packed,
 // 16-byte writes and reads) and stored so that each store instruction writes
 // four rows x 128 contiguous bytes to every destination -- large NVLink
 // packets instead of 16-byte ones.  Ragged blocks store element by element.
-__device__ __forceinline__ void store_block(const uint32_t (&r)[32], float* __restrict__ stage, int row0, int lane,
+//
+// With output views (out.tma) a full block leaves by TMA instead: lane 0
+// stores the staged block through every destination's view and commits one
+// bulk group (returns true); the caller alternates between two staging
+// blocks, and the wait before staging keeps at most one group reading.
+__device__ __forceinline__ bool store_block(const uint32_t (&r)[32], float* __restrict__ stage, int row0, int lane,
                                             int M, int n0, int N, float sr, const float* __restrict__ col_scale,
                                             const float* __restrict__ bias, const OutDesc& out, int shift) {
     const int row = row0 + lane;
     if (out.vec && n0 + 32 <= N) {
+        if (out.tma) {
+            if (lane == 0) bulk_wait_read_1();  // this staging block's previous group has been read
+            __syncwarp();
+        }
         const float4* cs4 = reinterpret_cast<const float4*>(col_scale + n0);
         const float4* b4 = bias ? reinterpret_cast<const float4*>(bias + n0) : nullptr;
         float4 o[8];
@@ -168,6 +193,16 @@ __device__ __forceinline__ void store_block(const uint32_t (&r)[32], float* __re
         float4* st4 = reinterpret_cast<float4*>(stage);
 #pragma unroll
         for (int j = 0; j < 8; ++j) st4[lane * 8 + (j ^ (lane & 7))] = o[j];
+        if (out.tma) {
+            // generic-proxy writes become visible to the TMA unit's reads
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+                for (int d = 0; d < out.count; ++d) tma_store_2d(&out.map[d], stage, n0, row0);
+                bulk_commit();
+            }
+            return true;
+        }
         __syncwarp();
         const int sub = lane >> 3;  // row within a group of four
         const int q = lane & 7;     // column quad
@@ -182,9 +217,9 @@ __device__ __forceinline__ void store_block(const uint32_t (&r)[32], float* __re
             }
         }
         __syncwarp();  // the staging area is reused by the next block
-        return;
+        return false;
     }
-    if (row >= M) return;
+    if (row >= M) return false;
     const size_t base_off = (size_t)row * (size_t)out.ldy + (size_t)out.col_offset;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
@@ -196,6 +231,7 @@ __device__ __forceinline__ void store_block(const uint32_t (&r)[32], float* __re
             for (int d = 0; d < out.count; ++d) out.base[d][base_off + n] = val;
         }
     }
+    return false;
 }
 
 // One destination (the plain matmul): each thread rescales its row of the
@@ -456,6 +492,7 @@ __global__ void __launch_bounds__(threads_for<kW4>(), 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         const bool vec1 = out.vec != 0;
+        int nb = 0;  // bulk groups this warp committed (gathering epilogue, output views)
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
             int mt, nt;
             tile_coords(t, m_tiles, n_tiles, group_m, mt, nt);
@@ -468,14 +505,17 @@ __global__ void __launch_bounds__(threads_for<kW4>(), 1)
             if constexpr (!kGather) {
                 store_tile_rows<BN>(taddr, row, row < M, nt * BN, N, sr, col_scale, bias, out.base[0], vec1, shift);
             } else {
-                float* stage = epi_stage + quarter * 32 * kEpiPitch;
+                float* stage = epi_stage + quarter * 2 * kEpiBlockFloats;  // this warp's two staging blocks
 #pragma unroll 1
                 for (int c = 0; c < BN / 32; ++c) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(taddr + c * 32, r);
                     tmem_ld_wait();
                     const int n0 = nt * BN + c * 32;
-                    if (row0 < M && n0 < N) store_block(r, stage, row0, lane, M, n0, N, sr, col_scale, bias, out, shift);
+                    if (row0 < M && n0 < N &&
+                        store_block(r, stage + (nb & 1) * kEpiBlockFloats, row0, lane, M, n0, N, sr, col_scale, bias,
+                                    out, shift))
+                        ++nb;
                 }
             }
             tmem_fence_before();
@@ -484,6 +524,7 @@ __global__ void __launch_bounds__(threads_for<kW4>(), 1)
         }
     }
 
+    if (kGather && warp >= 2 && lane == 0) bulk_wait_all();  // this thread's TMA stores complete
     if (kGather && warp >= 2) __threadfence_system();  // peer stores performed before the grid ends
     tmem_fence_before();
     __syncthreads();
@@ -561,8 +602,9 @@ struct Smem2 {
     static constexpr int kSlotOffset = kStages * kStageBytes;
     static constexpr int kSlotBytes = kBBytes + kPBytes;
     static constexpr int kSlotsBytes = kW4 ? kSlots * kSlotBytes : 0;
-    static constexpr int kBarrierBytes = (8 * (2 * kStages + 4 * kSlots + 6) + 16 + 127) / 128 * 128;
+    static constexpr int kBarrierBytes = (8 * (2 * kStages + 4 * kSlots + 6) + 16 + 1023) / 1024 * 1024;
     static constexpr int kTotal = 1024 + kSlotOffset + kSlotsBytes + kBarrierBytes;
+    static_assert(kTotal + kEpiBytes <= 227 * 1024, "shared memory of the gathering kernel");
 };
 
 
@@ -820,6 +862,7 @@ __global__ void __launch_bounds__(threads_for<kW4>(), 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         const bool vec1 = out.vec != 0;
+        int nb = 0;  // bulk groups this warp committed (gathering epilogue, output views)
         for (int t = cluster; t < num_tiles; t += clusters) {
             int mt, nt;
             tile_coords(t, m_tiles, n_tiles, group_m, mt, nt);
@@ -832,14 +875,17 @@ __global__ void __launch_bounds__(threads_for<kW4>(), 1)
             if constexpr (!kGather) {
                 store_tile_rows<256>(taddr, row, row < M, nt * 256, N, sr, col_scale, bias, out.base[0], vec1, shift);
             } else {
-                float* stage = epi_stage + quarter * 32 * kEpiPitch;
+                float* stage = epi_stage + quarter * 2 * kEpiBlockFloats;  // this warp's two staging blocks
 #pragma unroll 1
                 for (int c = 0; c < 256 / 32; ++c) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(taddr + c * 32, r);
                     tmem_ld_wait();
                     const int n0 = nt * 256 + c * 32;
-                    if (row0 < M && n0 < N) store_block(r, stage, row0, lane, M, n0, N, sr, col_scale, bias, out, shift);
+                    if (row0 < M && n0 < N &&
+                        store_block(r, stage + (nb & 1) * kEpiBlockFloats, row0, lane, M, n0, N, sr, col_scale, bias,
+                                    out, shift))
+                        ++nb;
                 }
             }
             tmem_fence_before();
@@ -848,6 +894,7 @@ __global__ void __launch_bounds__(threads_for<kW4>(), 1)
         }
     }
 
+    if (kGather && warp >= 2 && lane == 0) bulk_wait_all();  // this thread's TMA stores complete
     if (kGather && warp >= 2) __threadfence_system();  // peer stores performed before the grid ends
     tmem_fence_before();
     cluster_sync_all();  // no CTA leaves while its peer may still signal its barriers

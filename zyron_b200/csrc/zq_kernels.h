@@ -73,6 +73,12 @@ struct OutDesc {
     int vec;  // ldy, col_offset and every base allow 16-byte stores
     long long ldy;
     long long col_offset;
+    // Several destinations with vec: 2-D fp32 views [M][N] of each
+    // destination from its column offset (row pitch ldy), 32 x 32 boxes with
+    // the 128-byte swizzle; the gathering epilogue stores whole 32 x 32
+    // blocks with TMA through them.
+    int tma;
+    CUtensorMap map[kMaxOutputs];
 };
 
 struct GemmArgs {

@@ -92,6 +92,57 @@ def test_quantize_rows_bit_exact(zb, M, K):
     assert_bits_equal(s.cpu().numpy(), so, "row scales")
 
 
+def _near_tie_rows(rng, M, K):
+    """Rows whose quotients x / s sit within a few ulps of half-integers, where
+    the kernels' multiply-by-reciprocal fast path must hand over to the exact
+    division: each row's absmax fixes s = absmax / 127 (not a power of two),
+    and the other values are (k + 1/2) * s, k in [-127, 126), moved by -3..3
+    ulps; +-absmax give quotients at the clamp."""
+    x = np.empty((M, K), dtype=np.float32)
+    for r in range(M):
+        amax = np.float32(rng.uniform(0.5, 300.0))
+        s = np.float32(amax / np.float32(127.0))
+        k = rng.integers(-127, 126, K).astype(np.float32) + np.float32(0.5)
+        v = (k * s).astype(np.float32)
+        nudge = rng.integers(-3, 4, K)
+        toward = np.where(nudge > 0, np.float32(np.inf), np.float32(-np.inf)).astype(np.float32)
+        for step in range(3):
+            v = np.where(np.abs(nudge) > step, np.nextafter(v, toward), v).astype(np.float32)
+        v[0] = amax
+        if K > 1:
+            v[1] = -amax
+        x[r] = v
+    return x
+
+
+@pytest.mark.parametrize("M,K", [(1, 4096), (4, 1000), (64, 3072)])
+def test_quantize_near_ties_bit_exact(zb, M, K):
+    """Near-tie quotients through the standalone quantizer, the 1-4-row GEMV
+    that quantizes its rows itself, the GEMM path and the device weight
+    quantizer, against the oracle."""
+    import torch
+
+    rng = np.random.default_rng(9000 + M + K)
+    x = _near_tie_rows(rng, M, K)
+    q, s = zb.quantize_rows(torch.from_numpy(x).cuda())
+    qo, so = O.quantize_rows(x)
+    assert np.array_equal(q.cpu().numpy(), qo), f"{(q.cpu().numpy() != qo).sum()} codes differ"
+    assert_bits_equal(s.cpu().numpy(), so, "row scales")
+    w = (rng.standard_normal((K, 96)) * 0.02).astype(np.float32)
+    for qt in (1, 2):
+        pay, sc = O.quantize_weights(w, qt)
+        W = zb.QuantizedMatrix.from_parts(qt, K, 96, sc, pay)
+        y = zb.matmul(torch.from_numpy(x).cuda(), W).cpu().numpy()
+        assert_bits_equal(y, O.matmul(x, qt, pay, sc, 96)[3], f"matmul t{qt}")
+        # the same values as weights: columns of x.T, device quantize()
+        wt = np.ascontiguousarray(x.T)
+        Wq = zb.quantize(torch.from_numpy(wt).cuda(), zb.Type(qt))
+        pay_o, sc_o = O.quantize_weights(wt, qt)
+        assert np.array_equal(Wq.payload(), pay_o), f"device quantize payload t{qt}"
+        assert_bits_equal(Wq.scales(), sc_o, f"device quantize scales t{qt}")
+    assert zb.device_error() == 0
+
+
 SHAPES = [
     # decode GEMV sizes (M <= 8)
     (1, 64, 7), (1, 4096, 1000), (2, 31, 33), (3, 129, 255), (5, 1000, 300), (8, 4096, 1100), (8, 33, 1),

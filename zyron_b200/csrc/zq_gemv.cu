@@ -195,8 +195,9 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const uint8_t* __restric
                 for (int j = 0; j < 8; ++j) v[j] = (m < M && k0 + j < K) ? __ldg(xk + j) : 0.0f;
             }
             uint32_t c[8];
+            const float rcp = zq_quant_rcp(sm);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) c[j] = (uint32_t)(uint8_t)(int8_t)zq_quantize_value(v[j], sm, 127);
+            for (int j = 0; j < 8; ++j) c[j] = (uint32_t)(uint8_t)(int8_t)zq_quantize_value_rcp(v[j], sm, rcp, 127);
             s4[2 * gi] = c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24);
             s4[2 * gi + 1] = c[4] | (c[5] << 8) | (c[6] << 16) | (c[7] << 24);
         }

@@ -219,17 +219,28 @@ __device__ __forceinline__ void load_row(const float* __restrict__ x, int K, int
     }
 }
 
-// `red` holds 96 floats.
+// Norm weights held in registers: element tid + kNT k for k < kNormRegs
+// (the rest of a longer row is read from global memory).
+constexpr int kNormRegs = 4;
+
+// `red` holds 96 floats; nwr / nbr hold this thread's norm weights and
+// LayerNorm biases (loaded before the kernel's dependency wait).
 template <int kNT>
 __device__ float quantize_row(float* xs, int8_t* qs, int K, int Kp, int type, int pro, const float* __restrict__ nw,
-                              const float* __restrict__ nb, float eps, float* red) {
+                              const float* __restrict__ nb, const float (&nwr)[kNormRegs],
+                              const float (&nbr)[kNormRegs], float eps, float* red) {
     if (pro == kProRms) {
         float ss = 0.0f;
         for (int i = threadIdx.x; i < K; i += kNT) ss = __fadd_rn(ss, __fmul_rn(xs[i], xs[i]));
         ss = row_sum<kNT>(ss, red, 0);
         const float var = __fdiv_rn(ss, (float)K);
         const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-        for (int i = threadIdx.x; i < K; i += kNT) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), nw[i]);
+#pragma unroll
+        for (int k = 0; k < kNormRegs; ++k) {
+            const int i = threadIdx.x + kNT * k;
+            if (i < K) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), nwr[k]);
+        }
+        for (int i = threadIdx.x + kNT * kNormRegs; i < K; i += kNT) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), nw[i]);
         __syncthreads();
     } else if (pro == kProLayer) {
         float sm = 0.0f;
@@ -244,7 +255,12 @@ __device__ float quantize_row(float* xs, int8_t* qs, int K, int Kp, int type, in
         ss = row_sum<kNT>(ss, red, 1);
         const float var = __fdiv_rn(ss, (float)K);
         const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-        for (int i = threadIdx.x; i < K; i += kNT)
+#pragma unroll
+        for (int k = 0; k < kNormRegs; ++k) {
+            const int i = threadIdx.x + kNT * k;
+            if (i < K) xs[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xs[i], mean), inv), nwr[k]), nbr[k]);
+        }
+        for (int i = threadIdx.x + kNT * kNormRegs; i < K; i += kNT)
             xs[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xs[i], mean), inv), nw[i]), nb[i]);
         __syncthreads();
     }
@@ -252,8 +268,9 @@ __device__ float quantize_row(float* xs, int8_t* qs, int K, int Kp, int type, in
     for (int i = threadIdx.x; i < K; i += kNT) m = fmaxf(m, fabsf(xs[i]));
     m = row_max<kNT>(m, red, 2);
     const float s = zq_scale_from_absmax(m, 127.0f);
+    const float rcp = zq_quant_rcp(s);
     for (int i = threadIdx.x; i < Kp; i += kNT) {
-        const int8_t code = i < K ? (int8_t)zq_quantize_value(xs[i], s, 127) : (int8_t)0;
+        const int8_t code = i < K ? (int8_t)zq_quantize_value_rcp(xs[i], s, rcp, 127) : (int8_t)0;
         qs[i] = code;
     }
     __syncthreads();
@@ -284,6 +301,23 @@ template <int kNT>
 __device__ void merge_rows(const MergeArgs& a, int nchunk, float* xs, float* mls, float* invl) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const size_t stride = kMaxHeadDim + 2;
+    const int H = a.heads * a.hd;
+    // Contexts of up to 768 positions, rows of up to 3 kNT: this thread's
+    // chunk contexts are loaded with the (m, l) pairs, one round trip.
+    constexpr int kRegChunks = 12, kRegRows = 3;
+    const bool fast = nchunk <= kRegChunks && H <= kRegRows * kNT;
+    float cv[kRegRows][kRegChunks];
+    if (fast) {
+#pragma unroll
+        for (int k = 0; k < kRegRows; ++k) {
+            const int o = tid + kNT * k;
+            const int hq = o < H ? o / a.hd : 0, d = o < H ? o - hq * a.hd : 0;
+            const float* ph = a.part + (size_t)hq * a.n_chunks_max * stride + 2 + d;
+#pragma unroll
+            for (int c = 0; c < kRegChunks; ++c)
+                cv[k][c] = (o < H && c < nchunk) ? __ldcg(ph + (size_t)c * stride) : 0.0f;
+        }
+    }
     for (int e = tid; e < a.heads * nchunk; e += kNT) {
         const int hq = e / nchunk, c = e - hq * nchunk;
         const float* pc = a.part + ((size_t)hq * a.n_chunks_max + c) * stride;
@@ -306,7 +340,22 @@ __device__ void merge_rows(const MergeArgs& a, int nchunk, float* xs, float* mls
         if (lane == 0) invl[hq] = L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f;
     }
     __syncthreads();
-    const int H = a.heads * a.hd;
+    if (fast) {
+#pragma unroll
+        for (int k = 0; k < kRegRows; ++k) {
+            const int o = tid + kNT * k;
+            if (o < H) {
+                const int hq = o / a.hd;
+                float acc = 0.0f;
+#pragma unroll
+                for (int c = 0; c < kRegChunks; ++c)
+                    if (c < nchunk) acc = __fadd_rn(acc, __fmul_rn(cv[k][c], mls[2 * (hq * nchunk + c)]));
+                xs[o] = __fmul_rn(acc, invl[hq]);
+            }
+        }
+        __syncthreads();
+        return;
+    }
     for (int o = tid; o < H; o += kNT) {
         const int hq = o / a.hd, d = o - hq * a.hd;
         const float* ph = a.part + (size_t)hq * a.n_chunks_max * stride + 2 + d;
@@ -370,6 +419,15 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const float* __restric
     const bool lead = lane == 0 && first_col < N;  // lane 0 finishes the warp's columns
     const float pre_scale = lead ? scales[first_col] : 0.0f;
     const float pre_bias = (lead && bias) ? bias[first_col] : 0.0f;
+    // this thread's norm weights (and LayerNorm biases), also independent of
+    // earlier kernels
+    float nwr[kNormRegs], nbr[kNormRegs];
+#pragma unroll
+    for (int k = 0; k < kNormRegs; ++k) {
+        const int i = threadIdx.x + kThreads * k;
+        nwr[k] = ((kPro == kProRms || kPro == kProLayer) && i < K) ? nw[i] : 0.0f;
+        nbr[k] = (kPro == kProLayer && i < K) ? nb[i] : 0.0f;
+    }
     pdl_launch_dependents();
     pdl_wait_primary();
     if (skip_prefill && __ldcg(&st->pos) + 1 < __ldcg(&st->prompt_len)) return;
@@ -388,7 +446,7 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(const float* __restric
     }
     __syncthreads();
     if (kEpi == kEpiLogits && threadIdx.x == 0) blk_key = 0ull, blk_nan = 0;
-    const float s = quantize_row<kThreads>(xs, qs, K, Kp, kType, kPro, nw, nb, eps, red);
+    const float s = quantize_row<kThreads>(xs, qs, K, Kp, kType, kPro, nw, nb, nwr, nbr, eps, red);
     unsigned long long best = 0ull;
     int nan = 0;
 
@@ -801,8 +859,9 @@ __device__ float quantize_row_step(float* xs, int8_t* qs, int K, int Kp, int typ
     for (int i = tid; i < K; i += kStepThreads) m = fmaxf(m, fabsf(xs[i]));
     m = block_max1(m, red, rsel);
     const float s = zq_scale_from_absmax(m, 127.0f);
+    const float rcp = zq_quant_rcp(s);
     for (int i = tid; i < Kp; i += kStepThreads) {
-        const int8_t code = i < K ? (int8_t)zq_quantize_value(xs[i], s, 127) : (int8_t)0;
+        const int8_t code = i < K ? (int8_t)zq_quantize_value_rcp(xs[i], s, rcp, 127) : (int8_t)0;
         qs[i] = code;
     }
     __syncthreads();

@@ -58,21 +58,22 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restr
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     const float s = zq_scale_from_absmax(m, 127.0f);
     if (lane == 0) row_scale[warp] = s;
+    const float rcp = zq_quant_rcp(s);
 
     if (kVec) {
         const float4* x4 = reinterpret_cast<const float4*>(xr);
         uint32_t* q4 = reinterpret_cast<uint32_t*>(qr);
         for (int i = lane; i < (K >> 2); i += 32) {
             const float4 v = __ldg(x4 + i);
-            const uint32_t b0 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value(v.x, s, 127);
-            const uint32_t b1 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value(v.y, s, 127);
-            const uint32_t b2 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value(v.z, s, 127);
-            const uint32_t b3 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value(v.w, s, 127);
+            const uint32_t b0 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value_rcp(v.x, s, rcp, 127);
+            const uint32_t b1 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value_rcp(v.y, s, rcp, 127);
+            const uint32_t b2 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value_rcp(v.z, s, rcp, 127);
+            const uint32_t b3 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value_rcp(v.w, s, rcp, 127);
             q4[i] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
         }
         for (int i = (K >> 2) + lane; i < (Kp >> 2); i += 32) q4[i] = 0u;
     } else {
-        for (int i = lane; i < K; i += 32) qr[i] = (int8_t)zq_quantize_value(__ldg(xr + i), s, 127);
+        for (int i = lane; i < K; i += 32) qr[i] = (int8_t)zq_quantize_value_rcp(__ldg(xr + i), s, rcp, 127);
         for (int i = K + lane; i < Kp; i += 32) qr[i] = 0;
     }
 }
@@ -120,15 +121,16 @@ __global__ void __launch_bounds__(256) quantize_rows_reg_kernel(const float* __r
     if (row >= M) return;
     const float s = zq_scale_from_absmax(m, 127.0f);
     if (t == 0) row_scale[row] = s;
+    const float rcp = zq_quant_rcp(s);
     uint32_t* q4 = reinterpret_cast<uint32_t*>(q + (size_t)row * Kp);
 #pragma unroll
     for (int i = 0; i < kVec; ++i) {
         const int idx = t + i * kT;
         if (idx < k4) {
-            const uint32_t b0 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value(v[i].x, s, 127);
-            const uint32_t b1 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value(v[i].y, s, 127);
-            const uint32_t b2 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value(v[i].z, s, 127);
-            const uint32_t b3 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value(v[i].w, s, 127);
+            const uint32_t b0 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value_rcp(v[i].x, s, rcp, 127);
+            const uint32_t b1 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value_rcp(v[i].y, s, rcp, 127);
+            const uint32_t b2 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value_rcp(v[i].z, s, rcp, 127);
+            const uint32_t b3 = (uint32_t)(uint8_t)(int8_t)zq_quantize_value_rcp(v[i].w, s, rcp, 127);
             q4[idx] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
         }
     }
@@ -278,11 +280,12 @@ __global__ void __launch_bounds__(256) quantize_panel_kernel(const float* __rest
     const int limit = kType == kInt8 ? 127 : 7;
     const int n = n0 + tx;
     const float s = n < N ? scales[n] : 1.0f;
+    const float rcp = zq_quant_rcp(s);
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
         const int k = k0 + ty + 8 * j;
         int8_t v = 0;
-        if (n < N && k < K) v = (int8_t)zq_quantize_value(__ldg(w + (size_t)k * N + n), s, limit);
+        if (n < N && k < K) v = (int8_t)zq_quantize_value_rcp(__ldg(w + (size_t)k * N + n), s, rcp, limit);
         tile[tx][ty + 8 * j] = v;
     }
     __syncthreads();

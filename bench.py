@@ -760,17 +760,20 @@ QLM_WORKLOAD = "qlm_decode_d768_L12_H12_KV4_F3072_V16384_prompt64_new512"
 def qlm_measure(args, cpu_baseline=True):
     """QuantizedLanguageModel decode: d_model 768, 12 layers, 12 heads, 4 KV
     heads, GELU FFN 3072, tied vocab 16384, INT8, batch 1, 64-token uniform
-    prompt, 512 greedy tokens.  Per-token time = (generate(512) -
-    generate(1)) / 511, best of 3, with the SM clocks sampled meanwhile."""
+    prompt, 512 greedy tokens.  The model is LanguageModel(config, 0)
+    quantized to INT8, initialised by the library with the reference's
+    generator and seeds (the image equals the reference's byte for byte).
+    Per-token time = (generate(512) - generate(1)) / 511, best of 3, with the
+    SM clocks sampled meanwhile."""
     import tempfile
 
     import torch
 
-    from zyron_b200.qlm import Config, GenerationConfig, QuantizedLanguageModel, random_zyqmodel
+    from zyron_b200.qlm import Config, GenerationConfig, QuantizedLanguageModel, init_zyqmodel
 
     cfg = Config(vocab_size=16384, hidden_size=768, num_layers=12, num_heads=12, num_kv_heads=4,
                  intermediate_size=3072, max_sequence_length=576)
-    img = random_zyqmodel(cfg, seed=0)
+    img = init_zyqmodel(cfg, seed=0)
     lm = QuantizedLanguageModel.load_bytes(img)
     prompt = np.random.default_rng(0).integers(0, 16384, 64).tolist()
     lm.generate(prompt, GenerationConfig(max_new_tokens=512, top_k=1))  # builds the graphs
@@ -830,13 +833,13 @@ def qlm_measure(args, cpu_baseline=True):
 
 def run_qlm_workload(args):
     """The LM decode workload on its own line (see qlm_measure)."""
-    from zyron_b200.qlm import Config, GenerationConfig, QuantizedLanguageModel, random_zyqmodel
+    from zyron_b200.qlm import Config, GenerationConfig, QuantizedLanguageModel, init_zyqmodel
 
     if args.once:
         # profiling aid: one 4-token generation after the 64-token prompt
         cfg = Config(vocab_size=16384, hidden_size=768, num_layers=12, num_heads=12, num_kv_heads=4,
                      intermediate_size=3072, max_sequence_length=576)
-        lm = QuantizedLanguageModel.load_bytes(random_zyqmodel(cfg, seed=0))
+        lm = QuantizedLanguageModel.load_bytes(init_zyqmodel(cfg, seed=0))
         prompt = np.random.default_rng(0).integers(0, 16384, 64).tolist()
         toks = lm.generate(prompt, GenerationConfig(max_new_tokens=4, top_k=1))
         print(json.dumps({"workload": "qlm_decode_d768_L12", "once": True, "tokens": list(map(int, toks))}))
@@ -845,7 +848,8 @@ def run_qlm_workload(args):
     line = {"metric": "quantized-LM decode tok/s (QuantizedLanguageModel::generate, greedy)", "value": r["tok_s"],
             "unit": "tok/s", "n_gpus": 1, "steps": 512, "warmup": args.warmup, "ms_per_step": r["ms_per_token"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": QLM_WORKLOAD, "weights": "random init of the architecture, INT8"},
+            "config": {"workload": QLM_WORKLOAD,
+                       "weights": "LanguageModel(config, 0) quantized to INT8 (the reference's init)"},
             "clocks": r["clocks"], "roofline": r["roofline"],
             "e2e": {"value": r["generate_512_tok_s"], "unit": "tok/s",
                     "note": "whole generate call incl. 64-token prefill", "h2d_bytes_per_step": 0,

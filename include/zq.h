@@ -383,6 +383,28 @@ zq_status zq_lm_destroy(zq_lm* lm);
  * Synchronous. */
 zq_status zq_quantize_checkpoint(const void* checkpoint, size_t len, int type, void* stream, void** out,
                                  size_t* out_len, double* compression_ratio);
+
+/* transformer::Config (include/zyron/transformer/config.hpp:10-26). */
+typedef struct zq_lm_config {
+    size_t vocab_size, hidden_size, num_layers, num_heads, num_kv_heads, intermediate_size, max_sequence_length;
+    float norm_eps;
+    int use_rms_norm, causal, use_rope, tie_word_embeddings;
+    float rope_theta, dropout;
+    int use_qat;
+    size_t qat_bits;
+} zq_lm_config;
+
+/* QuantizedLanguageModel(LanguageModel(config, seed), type).save(): the
+ * .zyqmodel image of a freshly initialised model (language_model.cpp:52-75;
+ * quantized_language_model.cpp:178-269, 615-625).  The parameters are drawn
+ * as the reference's constructors draw them -- std::mt19937 and
+ * std::uniform_real_distribution<float> per tensor, with the same seeds,
+ * ranges and order -- so on the same standard library the image is
+ * byte-identical to the reference's.  The config is validated as
+ * Config::validate does; weights are quantized on the current device.
+ * Output as for zq_quantize_checkpoint.  Synchronous. */
+zq_status zq_lm_init_image(const zq_lm_config* config, uint32_t seed, int type, void* stream, void** out,
+                           size_t* out_len, double* compression_ratio);
 void zq_free_buffer(void* p);
 
 /* ---- token sampling (host) --------------------------------------------- */

@@ -73,6 +73,22 @@ def test_cli_arguments_and_errors_match_reference(native_lib, cgold, tmp_path):
     assert not out.exists()
 
 
+def test_init_image_rejects_bad_config(native_lib):
+    """zq_lm_init_image validates the config as Config::validate does
+    (config.hpp:32-66), with its messages, before any device work."""
+    from zyron_b200 import _lib
+    from zyron_b200.qlm import Config, init_zyqmodel
+
+    with pytest.raises(_lib.ZQInvalidArgument, match="num_kv_heads must divide num_heads"):
+        init_zyqmodel(Config(num_heads=4, num_kv_heads=3))
+    with pytest.raises(_lib.ZQInvalidArgument, match="dimensions must be > 0"):
+        init_zyqmodel(Config(num_layers=0))
+    with pytest.raises(_lib.ZQInvalidArgument, match="RoPE requires an even attention head dimension"):
+        init_zyqmodel(Config(hidden_size=12, num_heads=4))
+    with pytest.raises(_lib.ZQInvalidArgument, match="type must be INT8 or INT4"):
+        init_zyqmodel(Config(), qtype=3)
+
+
 @pytest.mark.gpu
 def test_quantized_model_bytes_match_reference_tool(cuda, cgold, tmp_path):
     from zyron_b200.zyron_quantize import quantize_checkpoint_bytes

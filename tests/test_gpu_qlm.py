@@ -240,3 +240,39 @@ def test_baseline_width_two_layers_logits_to_the_ulp(cuda, tmp_path):
         span = float(r.max() - r.min())
         err = float(np.abs(logits[g] - r).max())
         assert err <= ULP_RTOL * span, f"step {g}: max logit error {err:.3g} (range {span:.3g})"
+
+
+# LanguageModel(config, seed) initialised by the library itself
+# (zq_lm_init_image) against the reference's constructors: the same generator,
+# seeds, ranges and parameter order give the same floats, and the device
+# quantizer the same codes, so the .zyqmodel images are byte-identical.
+INIT_CASES = [
+    # vocab, hidden, layers, heads, kv, ffn, max_seq, rope, rms, tie, seed, type
+    (40, 32, 3, 4, 2, 64, 24, True, True, True, 0, 1),
+    (40, 32, 2, 4, 4, 48, 24, False, False, False, 7, 1),
+    (48, 64, 2, 4, 1, 96, 16, True, False, True, 123, 2),
+    (16384, 768, 2, 12, 4, 3072, 576, True, True, True, 0, 1),
+]
+
+
+@pytest.mark.parametrize("case", INIT_CASES, ids=lambda c: "x".join(map(str, c[:7])) + f"_t{c[11]}")
+def test_init_image_equals_reference(cuda, tmp_path, case):
+    from oracle import oracle as O
+    from zyron_b200.qlm import Config, init_zyqmodel
+
+    if not O.ref_available():
+        pytest.skip("compiled reference not present")
+    V, H, L, nh, kv, F, S, rope, rms, tie, seed, qtype = case
+    ref = O.RefQlm.create(V, H, L, nh, kv, F, S, use_rope=rope, use_rms_norm=rms, tie=tie, seed=seed, qtype=qtype)
+    p = tmp_path / "ref.zyqmodel"
+    ref.save(p)
+    cfg = Config(vocab_size=V, hidden_size=H, num_layers=L, num_heads=nh, num_kv_heads=kv, intermediate_size=F,
+                 max_sequence_length=S, use_rope=rope, use_rms_norm=rms, tie_word_embeddings=tie)
+    mine = init_zyqmodel(cfg, seed=seed, qtype=qtype)
+    want = p.read_bytes()
+    assert len(mine) == len(want)
+    if mine != want:
+        a, b = np.frombuffer(mine, np.uint8), np.frombuffer(want, np.uint8)
+        first = int(np.flatnonzero(a != b)[0])
+        raise AssertionError(f"images differ from byte {first} of {len(want)}")
+

@@ -120,6 +120,7 @@ SIGNATURES = {
     "zq_lm_generate": (st, [vp, vp, sz, vp, vp, sz, C.POINTER(sz), vp, vp]),
     "zq_lm_destroy": (st, [vp]),
     "zq_quantize_checkpoint": (st, [vp, sz, C.c_int, vp, C.POINTER(vp), C.POINTER(sz), C.POINTER(C.c_double)]),
+    "zq_lm_init_image": (st, [vp, C.c_uint32, C.c_int, vp, C.POINTER(vp), C.POINTER(sz), C.POINTER(C.c_double)]),
     "zq_free_buffer": (None, [vp]),
     "zq_sampler_create": (st, [C.c_uint32, C.POINTER(vp)]),
     "zq_sampler_destroy": (st, [vp]),
@@ -133,6 +134,16 @@ class GenerationConfigC(C.Structure):
     _fields_ = [("max_new_tokens", C.c_size_t), ("temperature", C.c_float), ("top_k", C.c_size_t),
                 ("top_p", C.c_float), ("repetition_penalty", C.c_float), ("no_repeat_ngram_size", C.c_size_t),
                 ("seed", C.c_uint32)]
+
+
+class LmConfigC(C.Structure):
+    """zq_lm_config (include/zq.h)."""
+
+    _fields_ = [("vocab_size", C.c_size_t), ("hidden_size", C.c_size_t), ("num_layers", C.c_size_t),
+                ("num_heads", C.c_size_t), ("num_kv_heads", C.c_size_t), ("intermediate_size", C.c_size_t),
+                ("max_sequence_length", C.c_size_t), ("norm_eps", C.c_float), ("use_rms_norm", C.c_int),
+                ("causal", C.c_int), ("use_rope", C.c_int), ("tie_word_embeddings", C.c_int),
+                ("rope_theta", C.c_float), ("dropout", C.c_float), ("use_qat", C.c_int), ("qat_bits", C.c_size_t)]
 
 
 class IpcHandle(C.Structure):

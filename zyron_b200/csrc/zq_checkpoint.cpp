@@ -21,6 +21,7 @@
 #include <cstring>
 #include <limits>
 #include <new>
+#include <random>
 #include <string>
 #include <vector>
 
@@ -315,6 +316,8 @@ struct Result {
     uint64_t quantized_bytes = 0, float_bytes = 0;
 };
 
+Result build_image(const Config& c, const std::vector<Tensor>& params, int type, void* stream);
+
 Result convert(const uint8_t* data, size_t len, int type, void* stream) {
     Reader r{data, len};
     // Checkpoint::load (145-179)
@@ -351,8 +354,13 @@ Result convert(const uint8_t* data, size_t len, int type, void* stream) {
             fail(ZQ_ERR_INVALID_ARGUMENT, "ZYRON AdamW: checkpoint moment shape mismatch");
     if (tok_size == 0) fail(ZQ_ERR_RUNTIME, "ZYRON checkpoint: tokenizer data missing");
     check_tokenizer(tok, (size_t)tok_size);
+    return build_image(c, params, type, stream);
+}
 
-    // QuantizedLanguageModel(model, type) and save (178-269, 615-625)
+// QuantizedLanguageModel(model, type) and save (quantized_language_model.cpp:
+// 178-269, 615-625) of a model whose parameters, in parameters() order and
+// with the shapes of parameter_shapes(c), are `params`.
+Result build_image(const Config& c, const std::vector<Tensor>& params, int type, void* stream) {
     const uint64_t H = c.hidden, V = c.vocab, F = c.ffn, kvd = c.kvh() * (c.hidden / c.heads);
     Result res;
     Writer w;
@@ -456,6 +464,61 @@ Result convert(const uint8_t* data, size_t len, int type, void* stream) {
     return res;
 }
 
+// The parameters of LanguageModel(config, seed) (language_model.cpp:52-75),
+// in parameters() order.  Every random tensor is Tensor::random(shape, -lim,
+// lim, s) (src/core/tensor.cpp:165-172): a fresh std::mt19937(s) and one
+// std::uniform_real_distribution<float>(-lim, lim) draw per element in
+// row-major order, so the values equal the reference's bit for bit on the
+// same standard library.  The seeds follow the constructors: the embedding
+// (range 0.02, embedding.hpp:17) takes seed + 1; the transformer seed + 100,
+// its block l that + 100 l (transformer.cpp:44-47); a block's attention + 10
+// and its feed-forward + 20 (transformer_block.cpp:13-14); q, k, v and out
+// projections + 1..4 (attention.cpp:102-105); up and down + 1, + 2
+// (feed_forward.cpp:8-9); an untied lm_head seed + 200.  Linear weights use
+// the Xavier limit sqrt(6 / (in + out)) in float (linear.cpp:13-26); norm
+// weights are ones, norm and linear biases zeros.
+std::vector<std::vector<float>> init_parameters(const Config& c, uint32_t seed) {
+    const auto shapes = parameter_shapes(c);
+    std::vector<std::vector<float>> out;
+    out.reserve(shapes.size());
+    auto random = [&](uint64_t rows, uint64_t cols, float lim, uint32_t s) {
+        std::vector<float> v((size_t)(rows * cols));
+        std::mt19937 rng(s);
+        std::uniform_real_distribution<float> dist(-lim, lim);
+        for (float& x : v) x = dist(rng);
+        out.push_back(std::move(v));
+    };
+    auto fill = [&](uint64_t n, float value) { out.push_back(std::vector<float>((size_t)n, value)); };
+    auto linear = [&](uint64_t in, uint64_t o, uint32_t s) {
+        random(in, o, std::sqrt(6.0f / static_cast<float>(in + o)), s);
+        fill(o, 0.0f);
+    };
+    const uint64_t H = c.hidden, V = c.vocab, F = c.ffn, kvd = c.kvh() * (c.hidden / c.heads);
+    random(V, H, 0.02f, seed + 1u);
+    const uint32_t transformer_seed = seed + 100u;
+    for (uint64_t l = 0; l < c.layers; ++l) {
+        const uint32_t block = transformer_seed + static_cast<uint32_t>(l * 100);
+        const uint32_t attn = block + 10u, ffn = block + 20u;
+        fill(H, 1.0f);
+        if (!c.rms) fill(H, 0.0f);
+        linear(H, H, attn + 1u);
+        linear(H, kvd, attn + 2u);
+        linear(H, kvd, attn + 3u);
+        linear(H, H, attn + 4u);
+        fill(H, 1.0f);
+        if (!c.rms) fill(H, 0.0f);
+        linear(H, F, ffn + 1u);
+        linear(F, H, ffn + 2u);
+    }
+    fill(H, 1.0f);
+    if (!c.tie) random(H, V, std::sqrt(6.0f / static_cast<float>(H + V)), seed + 200u);
+    fill(V, 0.0f);
+    if (out.size() != shapes.size()) fail(ZQ_ERR_RUNTIME, "zyron_b200: parameter list mismatch");
+    for (size_t i = 0; i < out.size(); ++i)
+        if (out[i].size() != shape_size(shapes[i])) fail(ZQ_ERR_RUNTIME, "zyron_b200: parameter size mismatch");
+    return out;
+}
+
 }  // namespace
 
 extern "C" {
@@ -469,6 +532,56 @@ zq_status zq_quantize_checkpoint(const void* checkpoint, size_t len, int type, v
         return zq::set_error(ZQ_ERR_INVALID_ARGUMENT, "--bits must be 4 or 8");
     try {
         Result r = convert(static_cast<const uint8_t*>(checkpoint), checkpoint ? len : 0, type, stream);
+        void* buf = std::malloc(r.bytes.size());
+        if (!buf) return zq::set_error(ZQ_ERR_RUNTIME, "zyron_b200: out of host memory");
+        std::memcpy(buf, r.bytes.data(), r.bytes.size());
+        *out = buf;
+        *out_len = r.bytes.size();
+        if (compression_ratio)
+            *compression_ratio = r.quantized_bytes == 0 ? 0.0 : (double)r.float_bytes / (double)r.quantized_bytes;
+        return ZQ_OK;
+    } catch (const Fail& f) {
+        return zq::set_error(f.status, f.msg.c_str());
+    } catch (const std::bad_alloc&) {
+        return zq::set_error(ZQ_ERR_RUNTIME, "zyron_b200: out of host memory");
+    }
+}
+
+zq_status zq_lm_init_image(const zq_lm_config* config, uint32_t seed, int type, void* stream, void** out,
+                           size_t* out_len, double* compression_ratio) {
+    if (!out || !out_len || !config) return zq::set_error(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: null argument");
+    *out = nullptr;
+    *out_len = 0;
+    if (type != ZQ_TYPE_INT8 && type != ZQ_TYPE_INT4)
+        return zq::set_error(ZQ_ERR_INVALID_ARGUMENT, "zyron_b200: type must be INT8 or INT4");
+    try {
+        Config c;
+        c.vocab = config->vocab_size;
+        c.hidden = config->hidden_size;
+        c.layers = config->num_layers;
+        c.heads = config->num_heads;
+        c.kv_heads = config->num_kv_heads;
+        c.ffn = config->intermediate_size;
+        c.max_seq = config->max_sequence_length;
+        c.eps = config->norm_eps;
+        c.rms = config->use_rms_norm != 0;
+        c.causal = config->causal != 0;
+        c.rope = config->use_rope != 0;
+        c.tie = config->tie_word_embeddings != 0;
+        c.theta = config->rope_theta;
+        c.dropout = config->dropout;
+        c.qat = config->use_qat != 0;
+        c.qat_bits = config->qat_bits;
+        validate(c);
+        const std::vector<std::vector<float>> store = init_parameters(c, seed);
+        const auto shapes = parameter_shapes(c);
+        std::vector<Tensor> params(store.size());
+        for (size_t i = 0; i < store.size(); ++i) {
+            params[i].dims = shapes[i];
+            params[i].data = store[i].data();
+            params[i].count = store[i].size();
+        }
+        Result r = build_image(c, params, type, stream);
         void* buf = std::malloc(r.bytes.size());
         if (!buf) return zq::set_error(ZQ_ERR_RUNTIME, "zyron_b200: out of host memory");
         std::memcpy(buf, r.bytes.data(), r.bytes.size());

@@ -6,13 +6,14 @@ format (src/model/quantized_language_model.cpp:615-642) and keeps weights,
 KV cache and activations on the GPU; ``generate(ids, config)`` is the
 reference's generate (496-547) for every GenerationConfig.
 
-``random_zyqmodel`` builds a ``.zyqmodel`` image of a randomly initialised
-model of a given architecture.  Weight shapes and init follow the reference's
-``LanguageModel(config, seed)``: Xavier-uniform linears with bias 0
-(src/nn/linear.cpp:13-44), U(-0.02, 0.02) embedding, unit norm weights, and
-an lm_head tied to the transposed embedding (src/model/language_model.cpp:
-54-76).  The random values come from numpy, not from the reference's
-generator.
+``init_zyqmodel(config, seed)`` builds the ``.zyqmodel`` image of the
+reference's ``LanguageModel(config, seed)`` quantized with
+``QuantizedLanguageModel(model, type)``: the parameters are drawn with the
+reference's generator, seeds and order (src/model/language_model.cpp:52-75),
+so the image equals the reference's byte for byte.  ``random_zyqmodel``
+builds one of the same shapes and init ranges -- Xavier-uniform linears with
+bias 0 (src/nn/linear.cpp:13-44), U(-0.02, 0.02) embedding, unit norm
+weights, an lm_head tied to the transposed embedding -- from numpy draws.
 """
 from __future__ import annotations
 
@@ -213,6 +214,27 @@ def _config(c: Config):
             _u64(c.num_kv_heads) + _u64(c.intermediate_size) + _u64(c.max_sequence_length) + _f32(c.norm_eps) +
             _u32(c.use_rms_norm) + _u32(c.causal) + _u32(c.use_rope) + _u32(c.tie_word_embeddings) +
             _f32(c.rope_theta) + _f32(c.dropout) + _u32(c.use_qat) + _u64(c.qat_bits))
+
+
+def init_zyqmodel(config: Config, seed: int = 42, qtype: Type = Type.Int8, stream=None) -> bytes:
+    """QuantizedLanguageModel(LanguageModel(config, seed), qtype).save() as
+    bytes: the parameters drawn as the reference's constructors draw them
+    (language_model.cpp:52-75, tensor.cpp:165-172), weights quantized on the
+    GPU (quantized_language_model.cpp:178-269).  See ``zq_lm_init_image``."""
+    c = config
+    cfg = _lib.LmConfigC(c.vocab_size, c.hidden_size, c.num_layers, c.num_heads, c.num_kv_heads,
+                         c.intermediate_size, c.max_sequence_length, c.norm_eps, int(c.use_rms_norm), int(c.causal),
+                         int(c.use_rope), int(c.tie_word_embeddings), c.rope_theta, c.dropout, int(c.use_qat),
+                         c.qat_bits)
+    L = lib()
+    out = C.c_void_p()
+    n = C.c_size_t()
+    st = None if stream is None else C.c_void_p(stream.cuda_stream)
+    check(L.zq_lm_init_image(C.byref(cfg), int(seed) & 0xFFFFFFFF, int(qtype), st, C.byref(out), C.byref(n), None))
+    try:
+        return C.string_at(out, n.value)
+    finally:
+        L.zq_free_buffer(out)
 
 
 def random_zyqmodel(config: Config, seed: int = 0, qtype: Type = Type.Int8) -> bytes:

@@ -1,7 +1,8 @@
 """Column-sharded matmul with the all-gather fused into the epilogue, on 2
-GPUs (one process per GPU, NCCL for the IPC-handle exchange and the
-completion barrier).  Skipped when fewer than two GPUs are visible.  Each rank
-checks its full gathered output against the oracle, bit for bit."""
+GPUs and on every visible GPU (one process per GPU, NCCL for the IPC-handle
+exchange and the completion barrier).  Skipped when too few GPUs are
+visible.  Each rank checks its full gathered output against the oracle, bit
+for bit."""
 import os
 import socket
 
@@ -59,25 +60,41 @@ def _rank(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_gathered_matmul_two_gpus():
-    import torch
+def _run_gathered(world):
     import torch.multiprocessing as mp
 
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(180)
         assert p.exitcode == 0
-    res = sorted(q.get(timeout=10) for _ in range(2))
-    assert res == [(0, True, 0), (1, True, 0)]
+    res = sorted(q.get(timeout=10) for _ in range(world))
+    assert res == [(r, True, 0) for r in range(world)]
+
+
+def test_gathered_matmul_two_gpus():
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    _run_gathered(2)
+
+
+def test_gathered_matmul_all_gpus():
+    """Every visible GPU (up to eight) as one rank: each rank's epilogue
+    stores its columns into every peer's output."""
+    import torch
+
+    world = min(torch.cuda.device_count(), 8)
+    if world < 3:
+        pytest.skip("needs more than two GPUs")
+    _run_gathered(world)
 
 
 def _nccl_rank(rank, world, port, q):

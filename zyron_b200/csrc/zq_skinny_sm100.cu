@@ -18,12 +18,13 @@
 // 32-lane quarter, 16 TMEM columns = activation rows).
 //
 // One iteration is four k-blocks of one column block: a single 3-D TMA box
-// of [4 k-blocks][64 columns][128 B] (32 KiB of INT8 weights).  TMA streaming
-// measured flat at about 4.4 TB/s for 16-64 KiB per copy instruction on a
-// 45 MB panel, whether the box is one k-block of 128 columns, four k-blocks
-// of 64 or a contiguous bulk copy, and much slower at 8 KiB (2.4 TB/s for
-// one k-block of 64 columns): the cost is per copy instruction, not the
-// 128-byte row pieces of the box.  MMAs that accumulate
+// of [4 k-blocks][64 columns][128 B] (32 KiB of INT8 weights).  Streaming a
+// 45 MB panel in back-to-back launches measured flat at about 4.4 TB/s for
+// 16-64 KiB per copy instruction, whether the box is one k-block of 128
+// columns, four k-blocks of 64 or a contiguous bulk copy, the same as plain
+// 16-byte loads with no ring; 8 KiB copies were much slower (2.4 TB/s for
+// one k-block of 64 columns), so small copies cost per instruction, not per
+// 128-byte row piece of the box.  MMAs that accumulate
 // into one TMEM accumulator run one after another (about 130 ns each for
 // M=64 N=16 K=32), which would make a single chain slower than the weight
 // stream; so the four K=32 slices of each k-block go to four accumulators

@@ -264,6 +264,27 @@ def test_pair_tile_gemm_bit_exact(zb, qt, M, K, N):
     assert zb.device_error() == 0
 
 
+@pytest.mark.parametrize("M,K,N", [(1024, 8192, 9472), (1000, 4000, 9500)])
+def test_int4_pair_gemm_equals_int8_on_same_codes(zb, M, K, N):
+    """Long-K INT4 GEMMs on the 2-SM tile.  INT4 weights must give exactly the
+    INT8 result for the same codes and scales (the integer dot and the
+    epilogue are the same), so the INT8 kernel -- bit-exact against the
+    oracle above -- checks the INT4 unpack at sizes where the CPU oracle
+    would take minutes.  The second shape is ragged in M, K and N."""
+    import torch
+
+    rng = np.random.default_rng(M + K)
+    x, w = make(rng, M, K, N)
+    pay4, sc = O.quantize_weights(w, 2)
+    codes = O.unpack_codes(2, pay4, K, N)
+    W4 = zb.QuantizedMatrix.from_parts(2, K, N, sc, pay4)
+    W8 = zb.QuantizedMatrix.from_parts(1, K, N, sc, codes.view(np.uint8).ravel())
+    xd = torch.from_numpy(x).cuda()
+    assert_bits_equal(zb.matmul(xd, W4).cpu().numpy(), zb.matmul(xd, W8).cpu().numpy(),
+                      f"int4 vs int8 pair gemm {M}x{K}x{N}")
+    assert zb.device_error() == 0
+
+
 def test_host_entry_point_chunked(zb):
     """Host calls with > 64 MiB of input run in pipelined row chunks; the
     result must equal the device-pointer path bit for bit (ragged last

@@ -27,8 +27,8 @@
 // INT4 weights (kW4) stay packed in HBM and in the TMA copy.  The A boxes
 // keep their own ring, as deep as the INT8 kernel's; k-block i's packed
 // BNx64-byte B box goes to slot i % 4, which also holds its unpacked
-// 128-byte-swizzled BNx128-byte int8 tile.  Eight more warps (6..13) own the
-// slots, two per slot: they unpack slot u's box for k-blocks u, u + 4, ...,
+// 128-byte-swizzled BNx128-byte int8 tile.  Sixteen more warps (6..21) own
+// the slots, four per slot: they unpack slot u's box for k-blocks u, u + 4, ...,
 // release the packed box to the producer and the tile to the MMA, which
 // reads it with the stage's A box and frees it with a second commit.  Every
 // release of a tile needs a generic-to-async proxy fence; with slots owned
@@ -61,7 +61,7 @@ constexpr int kBK = 128;  // bytes == int8 codes per k-block (one 128 B swizzle 
 constexpr int kUmmaK = 32;
 constexpr int kThreads = 192;
 constexpr int kEpilogueThreads = 128;
-constexpr int kUnpackThreads = 256;  // warps 6..13 of an INT4-weight kernel
+constexpr int kUnpackThreads = 512;  // warps 6..21 of an INT4-weight kernel (two per slot: 0.95x)
 constexpr int kUnpackWarps = kUnpackThreads / 32;
 constexpr int kSlots = 4;              // packed + unpacked B tiles of an INT4-weight kernel
 constexpr int kSlotWarps = kUnpackWarps / kSlots;  // unpack warps per slot
@@ -467,7 +467,7 @@ __global__ void __launch_bounds__(threads_for<kW4>(), 1)
             mbar_drain_bounded(mma_done, 0, err, kDevErrTimeoutDrain);
         }
     } else if (kW4 && warp >= 6) {
-        // Unpack warps 6 + 2u and 7 + 2u own slot u: k-blocks u, u + 4, ...
+        // Unpack warps 6 + 4u .. 9 + 4u own slot u: k-blocks u, u + 4, ...
         const int u = (warp - 6) / kSlotWarps;  // the slot's warps are consecutive: different sub-partitions
         const int tid = ((warp - 6) % kSlotWarps) * 32 + lane;  // within the slot's warps
         uint8_t* conv = slot_base + u * S::kSlotBytes;
@@ -836,7 +836,7 @@ __global__ void __launch_bounds__(threads_for<kW4>(), 1)
             mbar_drain_bounded(mma_done, 0, err, kDevErrTimeoutDrain);
         }
     } else if (kW4 && warp >= 6) {
-        // Unpack warps 6 + 2u and 7 + 2u (both CTAs) own slot u: this CTA's
+        // Unpack warps 6 + 4u .. 9 + 4u (both CTAs) own slot u: this CTA's
         // tiles of k-blocks u, u + 4, ..., announced on the leader's barrier.
         const int u = (warp - 6) / kSlotWarps;  // the slot's warps are consecutive: different sub-partitions
         const int tid = ((warp - 6) % kSlotWarps) * 32 + lane;  // within the slot's warps

@@ -330,9 +330,11 @@ def run_ours(args, rank, world, local_rank):
         int8_peak = 2.0 * 1590.0
         peak_src = "fallback: 2 x 1590 TFLOP/s bf16 (earlier pool measurement)"
     gemm_tops = ops(M, n_loc, K) / (gemm_ms * 1e-3) / 1e12
+    # the committed DRAM figure is for the 1-GPU INT8 headline workload only
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "gemm_traffic.json")
-    if os.path.exists(tpath):
+    headline = (M, K, n_loc) == (M_ROWS, K_DIM, N_COLS) and args.weight_type == "int8"
+    if headline and os.path.exists(tpath):
         with open(tpath) as f:
             traffic = json.load(f).get("dram_bytes_per_launch_full_workload")
 

@@ -164,6 +164,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// The first 1024-byte-aligned byte (in the shared window) of a dynamic
+// shared-memory array.  Pure arithmetic on the array pointer: an integer round
+// trip would hide its address space from the compiler and turn every access
+// through the result into a generic load or store.
+__device__ __forceinline__ uint8_t* smem_align1024(uint8_t* raw) {
+    return raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u);
+}
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -312,7 +312,7 @@ __global__ void __launch_bounds__(threads_for<kW4>(), 1)
     using S = Smem<BN, STAGES, kW4>;
     constexpr uint32_t kTmemCols = 2 * BN;  // power of two >= 32 for BN in {64,128,256}
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = smem_align1024(smem_raw);
     uint8_t* stage_base = smem;
     uint8_t* slot_base = smem + S::kSlotOffset;  // INT4: [unpacked | packed] B tiles
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kSlotOffset + S::kSlotsBytes);
@@ -668,7 +668,7 @@ __global__ void __launch_bounds__(threads_for<kW4>(), 1)
     constexpr int kStages2 = S::kStages;
     constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = smem_align1024(smem_raw);
     uint8_t* stage_base = smem;
     uint8_t* slot_base = smem + S::kSlotOffset;  // INT4: [unpacked | packed] B tiles
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kSlotOffset + S::kSlotsBytes);

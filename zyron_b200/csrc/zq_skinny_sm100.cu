@@ -254,7 +254,7 @@ __global__ void __launch_bounds__(SkCfg<kType>::kThreads, 1)
     constexpr int S = C::kStages;
     constexpr uint32_t kTmemCols = 2 * kSkChains * kSkRows;  // two buffers of four 16-column accumulators
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = smem_align1024(smem_raw);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes);
     uint64_t* full = bars;           // TMA -> MMA (INT8) or -> unpack (INT4)
     uint64_t* conv_full = bars + S;  // unpack -> MMA (INT4)

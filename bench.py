@@ -22,6 +22,7 @@ from __future__ import annotations
 
 import argparse
 import ctypes as C
+import hashlib
 import json
 import os
 import statistics
@@ -106,15 +107,37 @@ class ClockSampler:
 # --------------------------------------------------------------------------
 # reference CPU timing (oracle/_ref or the oracle port) -- checker side only
 # --------------------------------------------------------------------------
-def synthetic_zyq_bytes(K, N, seed):
-    """A .zyq record with random INT8 codes / scales of the workload's shape.
-    The reference matmul's cost does not depend on the values."""
-    from oracle import oracle as O
+# Inputs shared by both arms: numpy PCG64 streams that either arm can
+# regenerate on the host.  x is one stream (any prefix of rows is the same);
+# W is stored transposed per 256-column block, block b drawn from
+# PCG64(seed).jumped(b), so a rank generates only its own column shard.
+X_SEED, W_SEED, W_BLOCK = 0, 1, 256
+OUTPUT_CHECK_ROWS = 16
+INPUTS_NOTE = ("x: numpy PCG64(0) standard normal fp32 [M, K]; W: N(0, 0.02) fp32, 256-column blocks of W^T from "
+               "PCG64(1).jumped(block); the same values in both arms")
 
-    rng = np.random.default_rng(seed)
-    payload = rng.integers(-127, 128, size=K * N, dtype=np.int8).view(np.uint8)
-    scales = (np.abs(rng.standard_normal(N)) * 0.02 * 4.0 / 127.0 + 1e-6).astype(np.float32)
-    return O.zyq_bytes(1, K, N, scales, payload)
+
+def synthetic_x(M, K):
+    """x ~ N(0, 1), fp32 [M, K]."""
+    return np.random.Generator(np.random.PCG64(X_SEED)).standard_normal((M, K), dtype=np.float32)
+
+
+def synthetic_wT(K, N, c0, n):
+    """Columns c0 .. c0+n of W ~ N(0, 0.02) as W^T, fp32 [n, K]."""
+    out = np.empty((n, K), dtype=np.float32)
+    for b in range(c0 // W_BLOCK, (c0 + n + W_BLOCK - 1) // W_BLOCK):
+        blk = np.random.Generator(np.random.PCG64(W_SEED).jumped(b)).standard_normal((W_BLOCK, K),
+                                                                                   dtype=np.float32)
+        lo, hi = max(c0, b * W_BLOCK), min(c0 + n, (b + 1) * W_BLOCK)
+        out[lo - c0:hi - c0] = blk[lo - b * W_BLOCK:hi - b * W_BLOCK]
+    out *= np.float32(0.02)
+    return out
+
+
+def output_digest(y_rows):
+    """sha256 of the first output rows' fp32 bytes: both arms print it for the
+    same inputs, and bit-exact results give the same digest."""
+    return hashlib.sha256(np.ascontiguousarray(y_rows, dtype=np.float32).tobytes()).hexdigest()
 
 
 def reference_cpu_timer(zyq: bytes, x_rows: np.ndarray):
@@ -150,18 +173,31 @@ def run_reference_arm(args, rank, world):
     if rank != 0:
         return
     K, N = K_DIM, N_COLS
-    zyq = synthetic_zyq_bytes(K, N, seed=1)
-    x = np.random.default_rng(0).standard_normal((64, K)).astype(np.float32)
     from oracle import oracle as O
 
+    # the inputs of our arm: the same x rows and W (quantized by the reference)
+    x = synthetic_x(max(64, OUTPUT_CHECK_ROWS), K)
+    w = np.ascontiguousarray(synthetic_wT(K, N, 0, N).T)
+    if O.ref_available():
+        zyq = O.RefMatrix.quantize(w, O.INT8).save_bytes()
+    else:
+        pay, sc = O.quantize_weights(w, O.INT8)
+        zyq = O.zyq_bytes(1, K, N, sc, pay)
+    del w
     threads = O.ref_set_threads(os.cpu_count() or 1) if O.ref_available() else 1
     rows = max(1, min(64, threads))
-    call, threads, kind, _keep = reference_cpu_timer(zyq, x[:rows])
+    call, threads, kind, keep = reference_cpu_timer(zyq, x[:rows])
     for _ in range(args.warmup):
         call()
     times = [call() for _ in range(args.steps)]
     t = sum(times) / len(times)
     value = ops(rows, N, K) / t / 1e12
+    # untimed: the first output rows, for the digest our arm prints too
+    if keep is not None:
+        y_chk = keep.matmul(x[:OUTPUT_CHECK_ROWS])
+    else:
+        pay, sc = np.frombuffer(zyq[36 + 4 * N + 8:], dtype=np.uint8), np.frombuffer(zyq[36:36 + 4 * N], np.float32)
+        y_chk = O.matmul(x[:OUTPUT_CHECK_ROWS], 1, pay, sc, N)[3]
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
@@ -173,6 +209,8 @@ def run_reference_arm(args, rank, world):
                                    f"ZYRON quantization::matmul on {threads} host threads "
                                    f"(os.cpu_count()={os.cpu_count()})"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "inputs": INPUTS_NOTE,
+        "output_check": {"rows": OUTPUT_CHECK_ROWS, "sha256": output_digest(y_chk)},
     }
     print(json.dumps(line), flush=True)
 
@@ -198,13 +236,11 @@ def run_ours(args, rank, world, local_rank):
     n_loc = N // world
     c0 = rank * n_loc
 
-    # Inputs, generated on the device (seeded): x is the same on every rank,
-    # each rank quantizes its own column shard of W on the device.
-    g = torch.Generator(device=dev)
-    g.manual_seed(0)
-    x = torch.randn((M, K), generator=g, device=dev, dtype=torch.float32)
-    g.manual_seed(1000 + rank)
-    w_f32 = torch.randn((K, n_loc), generator=g, device=dev, dtype=torch.float32).mul_(0.02)
+    # Inputs generated on the host from the streams the reference arm uses
+    # too: x is the same on every rank, each rank quantizes its own column
+    # shard of W on the device.
+    x = torch.from_numpy(synthetic_x(M, K)).to(dev)
+    w_f32 = torch.from_numpy(synthetic_wT(K, N, c0, n_loc)).to(dev).t().contiguous()
     int4 = args.weight_type == "int4"
     W = zb.quantize(w_f32, zb.Type.Int4 if int4 else zb.Type.Int8)
     del w_f32
@@ -223,12 +259,14 @@ def run_ours(args, rank, world, local_rank):
 
         peer_out = PeerOutputs(M, N, dev)
 
+    result = [y]
+
     def step():
         if world == 1:
             _lib.check(L.zq_matmul(W.handle, C.c_void_p(x.data_ptr()), M, None, C.c_void_p(y.data_ptr()),
                                    C.c_void_p(ws_ptr), ws_bytes, sp))
             return
-        sharded_matmul_gathered(x, W, peer_out, workspace=(ws_ptr, ws_bytes), stream=stream)
+        result[0] = sharded_matmul_gathered(x, W, peer_out, workspace=(ws_ptr, ws_bytes), stream=stream)
 
     def barrier():
         if world > 1:
@@ -249,6 +287,8 @@ def run_ours(args, rank, world, local_rank):
         e1.record(stream)
         barrier()
     ms = e0.elapsed_time(e1) / args.steps
+    # the first output rows of the last step (the full gathered rows at N > 1)
+    digest = output_digest(result[0][:OUTPUT_CHECK_ROWS].cpu().numpy())
 
     # GEMM kernel alone (activation codes precomputed), same stream: the
     # dominant kernel's average launch duration for the roofline.
@@ -383,6 +423,10 @@ def run_ours(args, rank, world, local_rank):
                 "api": "zq_matmul_host (pinned host x -> host y), per rank on its column shard"},
         "cpu_baseline": cpu,
         "device_error": code,
+        "inputs": INPUTS_NOTE,
+        "output_check": {"rows": OUTPUT_CHECK_ROWS, "sha256": digest,
+                         "note": "sha256 of the first output rows; the reference arm prints the digest of its "
+                                 "own result for the same inputs (INT8 weights)"},
     }
     if world > 1:
         line["e2e"]["value"] = ops(M, N, K) / (e2e_ms * 1e-3) / 1e12

@@ -303,35 +303,38 @@ __device__ void merge_rows(const MergeArgs& a, int nchunk, float* xs, float* mls
     const size_t stride = kMaxHeadDim + 2;
     const int H = a.heads * a.hd;
     // Contexts of up to 768 positions, rows of up to 3 kNT: this thread's
-    // chunk contexts are loaded with the (m, l) pairs, one round trip.
+    // chunk contexts are loaded with the (m, l) pairs, one round trip.  The
+    // loads cover every chunk slot, used or not, so they need not wait for
+    // the position (nchunk); stale slots are never read back.
     constexpr int kRegChunks = 12, kRegRows = 3;
-    const bool fast = nchunk <= kRegChunks && H <= kRegRows * kNT;
+    const int nmax = a.n_chunks_max;
+    const bool rows_fit = H <= kRegRows * kNT;
+    const bool fast = nchunk <= kRegChunks && rows_fit;
     float cv[kRegRows][kRegChunks];
-    if (fast) {
+    if (rows_fit) {
 #pragma unroll
         for (int k = 0; k < kRegRows; ++k) {
             const int o = tid + kNT * k;
             const int hq = o < H ? o / a.hd : 0, d = o < H ? o - hq * a.hd : 0;
-            const float* ph = a.part + (size_t)hq * a.n_chunks_max * stride + 2 + d;
+            const float* ph = a.part + (size_t)hq * nmax * stride + 2 + d;
 #pragma unroll
             for (int c = 0; c < kRegChunks; ++c)
-                cv[k][c] = (o < H && c < nchunk) ? __ldcg(ph + (size_t)c * stride) : 0.0f;
+                cv[k][c] = (o < H && c < nmax) ? __ldcg(ph + (size_t)c * stride) : 0.0f;
         }
     }
-    for (int e = tid; e < a.heads * nchunk; e += kNT) {
-        const int hq = e / nchunk, c = e - hq * nchunk;
-        const float* pc = a.part + ((size_t)hq * a.n_chunks_max + c) * stride;
+    for (int e = tid; e < a.heads * nmax; e += kNT) {
+        const float* pc = a.part + (size_t)e * stride;
         mls[2 * e] = __ldcg(pc);
         mls[2 * e + 1] = __ldcg(pc + 1);
     }
     __syncthreads();
     for (int hq = warp; hq < a.heads; hq += kNT / 32) {
         float M = -INFINITY;
-        for (int c = lane; c < nchunk; c += 32) M = fmaxf(M, mls[2 * (hq * nchunk + c)]);
+        for (int c = lane; c < nchunk; c += 32) M = fmaxf(M, mls[2 * (hq * nmax + c)]);
         M = warp_max(M);
         float L = 0.0f;
         for (int c = lane; c < nchunk; c += 32) {
-            const int e = hq * nchunk + c;
+            const int e = hq * nmax + c;
             const float f = expf(__fsub_rn(mls[2 * e], M));
             L = __fadd_rn(L, __fmul_rn(mls[2 * e + 1], f));
             mls[2 * e] = f;
@@ -349,7 +352,7 @@ __device__ void merge_rows(const MergeArgs& a, int nchunk, float* xs, float* mls
                 float acc = 0.0f;
 #pragma unroll
                 for (int c = 0; c < kRegChunks; ++c)
-                    if (c < nchunk) acc = __fadd_rn(acc, __fmul_rn(cv[k][c], mls[2 * (hq * nchunk + c)]));
+                    if (c < nchunk) acc = __fadd_rn(acc, __fmul_rn(cv[k][c], mls[2 * (hq * nmax + c)]));
                 xs[o] = __fmul_rn(acc, invl[hq]);
             }
         }
@@ -366,7 +369,7 @@ __device__ void merge_rows(const MergeArgs& a, int nchunk, float* xs, float* mls
             for (int u = 0; u < 8; ++u) cv[u] = c0 + u < nchunk ? __ldcg(ph + (size_t)(c0 + u) * stride) : 0.0f;
 #pragma unroll
             for (int u = 0; u < 8; ++u)
-                if (c0 + u < nchunk) acc = __fadd_rn(acc, __fmul_rn(cv[u], mls[2 * (hq * nchunk + c0 + u)]));
+                if (c0 + u < nchunk) acc = __fadd_rn(acc, __fmul_rn(cv[u], mls[2 * (hq * nmax + c0 + u)]));
         }
         xs[o] = __fmul_rn(acc, invl[hq]);
     }
@@ -1037,6 +1040,9 @@ __device__ __noinline__ void attention_item(const StepParams& p, int grp, int ch
     const float* vsrc = p.qkv + (size_t)(p.heads + p.kvh) * hd + (size_t)grp * hd;
     // Every load is issued before the first wait: the cached keys and values
     // of this warp's positions, the new key and value, the first queries.
+    // The cache rows are loaded whatever the position (every row below
+    // max_seq exists), so these loads need not wait for `pos`; rows past it
+    // are zeroed once it is known.
     float kr[kAttnPosPerWarp][kPerLane], vr[kAttnPosPerWarp][kPerLane];
 #pragma unroll
     for (int i = 0; i < kAttnPosPerWarp; ++i) {
@@ -1046,11 +1052,12 @@ __device__ __noinline__ void attention_item(const StepParams& p, int grp, int ch
 #pragma unroll
         for (int r = 0; r < kPerLane; ++r) {
             const int d = lane + 32 * r;
-            const bool cached = d < hd && j < pos;
-            kr[i][r] = cached ? __ldcg(kj + d) : 0.0f;
-            vr[i][r] = cached ? __ldcg(vj + d) : 0.0f;
+            const bool row = d < hd && j < p.max_seq;
+            kr[i][r] = row ? __ldcg(kj + d) : 0.0f;
+            vr[i][r] = row ? __ldcg(vj + d) : 0.0f;
         }
     }
+    if (chunk * kAttnChunk > pos) return;  // a chunk past the position (the whole block leaves)
     if (p.rcos) {
         if (tid < half) {
             const float c = p.rcos[(size_t)pos * half + tid], sn = p.rsin[(size_t)pos * half + tid];
@@ -1070,12 +1077,16 @@ __device__ __noinline__ void attention_item(const StepParams& p, int grp, int ch
     }
 #pragma unroll
     for (int i = 0; i < kAttnPosPerWarp; ++i) {
-        if (chunk * kAttnChunk + warp * kAttnPosPerWarp + i == pos) {
+        const int j = chunk * kAttnChunk + warp * kAttnPosPerWarp + i;
+        if (j == pos) {
 #pragma unroll
             for (int r = 0; r < kPerLane; ++r) {
                 const int d = lane + 32 * r;
                 if (d < hd) kr[i][r] = kn[d], vr[i][r] = vn[d];
             }
+        } else if (j > pos) {
+#pragma unroll
+            for (int r = 0; r < kPerLane; ++r) kr[i][r] = vr[i][r] = 0.0f;
         }
     }
     for (int hb = 0; hb < rep; hb += kHeadBatch) {
@@ -1157,8 +1168,7 @@ __global__ void __launch_bounds__(kStepThreads) attn_chunk_kernel(const __grid_c
     pdl_wait_primary();
     const int pos = __ldcg(&p.state->pos);
     const int grp = blockIdx.x / p.n_chunks_max, chunk = blockIdx.x - grp * p.n_chunks_max;
-    if (chunk * kAttnChunk > pos) return;
-    attention_item(p, grp, chunk, pos, li, q_s, kn, vn, sc, mh, wpart);
+    attention_item(p, grp, chunk, pos, li, q_s, kn, vn, sc, mh, wpart);  // returns at once past pos
 }
 
 // Context row of the attention: merges the chunks' (m, l, c) partials into

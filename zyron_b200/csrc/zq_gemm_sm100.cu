@@ -26,9 +26,10 @@
 //
 // INT4 weights (kW4) stay packed in HBM and in the TMA copy.  The A boxes
 // keep their own ring, as deep as the INT8 kernel's; k-block i's packed
-// BNx64-byte B box goes to slot i % 4, which also holds its unpacked
-// 128-byte-swizzled BNx128-byte int8 tile.  Sixteen more warps (6..21) own
-// the slots, four per slot: they unpack slot u's box for k-blocks u, u + 4, ...,
+// BNx64-byte B box goes to slot i % S (S = 4, or 5 in the 2-SM kernel without
+// output staging), which also holds its unpacked 128-byte-swizzled
+// BNx128-byte int8 tile.  Four more warps per slot (warps 6, 7, ...) own the
+// slots: they unpack slot u's box for k-blocks u, u + S, ...,
 // release the packed box to the producer and the tile to the MMA, which
 // reads it with the stage's A box and frees it with a second commit.  Every
 // release of a tile needs a generic-to-async proxy fence; with slots owned
@@ -67,6 +68,14 @@ constexpr int kSlots = 4;              // packed + unpacked B tiles of an INT4-w
 constexpr int kSlotWarps = kUnpackWarps / kSlots;  // unpack warps per slot
 template <bool kW4>
 constexpr int threads_for() { return kW4 ? kThreads + kUnpackThreads : kThreads; }
+// The 2-SM kernel's INT4 slots: four unpack warps each; the gathering kernel
+// keeps four slots beside its epilogue staging, the plain one takes one more
+// (8192 x 8192 x 16384: 2273 TOPS against 2057 with four).
+constexpr int kPairSlotsGather = 4, kPairSlotsPlain = 5;
+template <bool kW4, bool kGather>
+constexpr int pair_slots() { return kW4 ? (kGather ? kPairSlotsGather : kPairSlotsPlain) : kSlots; }
+template <bool kW4, bool kGather>
+constexpr int pair_threads() { return kW4 ? kThreads + 32 * kSlotWarps * pair_slots<kW4, kGather>() : kThreads; }
 
 // An accumulator word: the int32 dot, or (INT4 weights unpacked as 16 x the
 // code, see unpack_stage) 16 x the dot, shifted back exactly.
@@ -592,8 +601,9 @@ cudaError_t launch_gemm_t(const GemmArgs& a, cudaStream_t stream, bool pdl) {
 // leader's MMA issuer waits there for both CTAs' tiles, and its commits free
 // the tile (`conv_empty`) in both CTAs.
 // ===========================================================================
-template <bool kW4>
+template <bool kW4, bool kGather>
 struct Smem2 {
+    static constexpr int kSlotsN = pair_slots<kW4, kGather>();
     static constexpr int kStages = 6;
     static constexpr int kABytes = 128 * kBK;  // this CTA's 128 rows of A
     static constexpr int kBBytes = 128 * kBK;  // this CTA's 128 rows (columns of W) of B, int8 swizzled
@@ -601,10 +611,10 @@ struct Smem2 {
     static constexpr int kStageBytes = kABytes + (kW4 ? 0 : kBBytes);  // = TMA bytes per stage and CTA
     static constexpr int kSlotOffset = kStages * kStageBytes;
     static constexpr int kSlotBytes = kBBytes + kPBytes;
-    static constexpr int kSlotsBytes = kW4 ? kSlots * kSlotBytes : 0;
-    static constexpr int kBarrierBytes = (8 * (2 * kStages + 4 * kSlots + 6) + 16 + 1023) / 1024 * 1024;
+    static constexpr int kSlotsBytes = kW4 ? kSlotsN * kSlotBytes : 0;
+    static constexpr int kBarrierBytes = (8 * (2 * kStages + 4 * kSlotsN + 6) + 16 + 1023) / 1024 * 1024;
     static constexpr int kTotal = 1024 + kSlotOffset + kSlotsBytes + kBarrierBytes;
-    static_assert(kTotal + kEpiBytes <= 227 * 1024, "shared memory of the gathering kernel");
+    static_assert(kTotal + (kGather ? kEpiBytes : 0) <= 227 * 1024, "shared memory of the 2-SM kernel");
 };
 
 
@@ -659,12 +669,13 @@ __device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
 }
 
 template <bool kGather, bool kW4>
-__global__ void __launch_bounds__(threads_for<kW4>(), 1)
+__global__ void __launch_bounds__((pair_threads<kW4, kGather>()), 1)
     gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                         int M, int N, int Kp, const float* __restrict__ row_scale,
                         const float* __restrict__ col_scale, const float* __restrict__ bias,
                         const __grid_constant__ OutDesc out, uint32_t* __restrict__ err, int group_m, int shift) {
-    using S = Smem2<kW4>;
+    using S = Smem2<kW4, kGather>;
+    constexpr int kPS = S::kSlotsN;
     constexpr int kStages2 = S::kStages;
     constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -683,9 +694,9 @@ __global__ void __launch_bounds__(threads_for<kW4>(), 1)
     // unpacked tiles ready (leader's copy, both CTAs' unpack warps) / read
     // (MMA commit, both copies)
     uint64_t* full_p = bars + 2 * kStages2 + 6;
-    uint64_t* p_empty = full_p + kSlots;
-    uint64_t* conv_full = full_p + 2 * kSlots;
-    uint64_t* conv_empty = full_p + 3 * kSlots;
+    uint64_t* p_empty = full_p + kPS;
+    uint64_t* conv_full = full_p + 2 * kPS;
+    uint64_t* conv_empty = full_p + 3 * kPS;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -704,7 +715,7 @@ __global__ void __launch_bounds__(threads_for<kW4>(), 1)
             mbar_init(&empty[s], 1);
         }
         if (kW4)
-            for (int c = 0; c < kSlots; ++c) {
+            for (int c = 0; c < kPS; ++c) {
                 mbar_init(&full_p[c], 1);
                 mbar_init(&p_empty[c], kSlotWarps);
                 mbar_init(&conv_full[c], 2 * kSlotWarps);  // both CTAs' slot warps
@@ -739,12 +750,12 @@ __global__ void __launch_bounds__(threads_for<kW4>(), 1)
             uint32_t pphase = 0;
             int issued[kStages2];
             uint32_t last_phase[kStages2];
-            int p_issued[kSlots];
-            uint32_t p_last[kSlots];
+            int p_issued[kPS];
+            uint32_t p_last[kPS];
 #pragma unroll
             for (int s = 0; s < kStages2; ++s) issued[s] = 0, last_phase[s] = 0;
 #pragma unroll
-            for (int s = 0; s < kSlots; ++s) p_issued[s] = 0, p_last[s] = 0;
+            for (int s = 0; s < kPS; ++s) p_issued[s] = 0, p_last[s] = 0;
             bool ok = true;
             for (int t = cluster; t < num_tiles && ok; t += clusters) {
                 int mt, nt;
@@ -766,7 +777,7 @@ __global__ void __launch_bounds__(threads_for<kW4>(), 1)
                                     kb * (kBK / 2), nt * 256 + (int)rank * 128);
                         p_issued[slot] = 1;
                         p_last[slot] = pphase;
-                        if (++slot == kSlots) slot = 0, pphase ^= 1u;
+                        if (++slot == kPS) slot = 0, pphase ^= 1u;
                     } else {
                         tma_load_2d_pair(sa + S::kABytes, &tmap_b, &full[stage], kb * kBK,
                                          nt * 256 + (int)rank * 128);
@@ -787,7 +798,7 @@ __global__ void __launch_bounds__(threads_for<kW4>(), 1)
                 else
                     mbar_drain_bounded(&empty[s], last_phase[s], err, kDevErrTimeoutDrain);
             }
-            for (int s = 0; s < kSlots; ++s)
+            for (int s = 0; s < kPS; ++s)
                 if (p_issued[s]) mbar_drain_bounded(&full_p[s], p_last[s], err, kDevErrTimeoutDrain);
         }
     } else if (warp == 1) {
@@ -820,7 +831,7 @@ __global__ void __launch_bounds__(threads_for<kW4>(), 1)
                     umma_commit_pair(&empty[stage]);
                     if (kW4) {
                         umma_commit_pair(&conv_empty[slot]);
-                        if (++slot == kSlots) slot = 0, cphase ^= 1u;
+                        if (++slot == kPS) slot = 0, cphase ^= 1u;
                     }
                     if (++stage == kStages2) stage = 0, phase ^= 1u;
                 }
@@ -844,7 +855,7 @@ __global__ void __launch_bounds__(threads_for<kW4>(), 1)
         const uint32_t conv_leader = map_to_rank(&conv_full[u], 0);
         uint32_t ph = 0;
         const long long total = (long long)((num_tiles - cluster + clusters - 1) / clusters) * k_blocks;
-        for (long long it = u; it < total; it += kSlots) {
+        for (long long it = u; it < total; it += kPS) {
             if (!mbar_wait_bounded(&full_p[u], ph, err, kDevErrTimeoutMma) ||
                 !mbar_wait_bounded(&conv_empty[u], ph ^ 1u, err, kDevErrTimeoutMma))
                 break;
@@ -907,10 +918,9 @@ __global__ void __launch_bounds__(threads_for<kW4>(), 1)
 
 template <bool kW4>
 cudaError_t launch_gemm_pair(const GemmArgs& a, cudaStream_t stream, bool pdl) {
-    using S = Smem2<kW4>;
     const bool gather = general_output(a);
     auto kern = gather ? gemm_i8_pair_kernel<true, kW4> : gemm_i8_pair_kernel<false, kW4>;
-    const int smem = S::kTotal + (gather ? kEpiBytes : 0);
+    const int smem = gather ? Smem2<kW4, true>::kTotal + kEpiBytes : Smem2<kW4, false>::kTotal;
     cudaError_t e = ensure_smem_attr(kern, smem);
     if (e != cudaSuccess) return e;
     const int sms = sm_count(a.reserved_sms);
@@ -920,7 +930,7 @@ cudaError_t launch_gemm_pair(const GemmArgs& a, cudaStream_t stream, bool pdl) {
     if (clusters > tiles) clusters = tiles;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters);
-    cfg.blockDim = dim3(threads_for<kW4>());
+    cfg.blockDim = dim3(gather ? pair_threads<kW4, true>() : pair_threads<kW4, false>());
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
